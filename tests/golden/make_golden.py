@@ -1,0 +1,195 @@
+"""Generate the golden vectors that pin the oracle, by running the reference itself (CPU) on seeded inputs.
+
+Run from the repository root, in a container where the reference checkout is available:
+
+    python tests/golden/make_golden.py --reference <path to the lookatmyquant checkout>
+
+The reference reads a model config at import (opgraph/model.py:37-47) and writes fitted trellis tables next to its
+sources (opgraph/codes.py:42); both are redirected to a temporary directory, the reference's files are only read. The
+outputs are small `.npz` fixtures in this directory, plus the reference's four fitted L=12 trellis tables
+(cache/codes/trellis_L12_k{1,2,3,4}_T256_s0_ema.pt, fp64 data) re-encoded as raw little-endian fp64 under
+lookatmyquant_b200/tables/, where the package and the tests read them on machines without the reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import shutil
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+TABLES = REPO / "lookatmyquant_b200" / "tables"
+
+SMOLLM2 = {"hidden_size": 960, "num_attention_heads": 15, "num_key_value_heads": 5, "intermediate_size": 2560,
+           "num_hidden_layers": 32, "rms_norm_eps": 1e-5, "rope_theta": 100000.0, "vocab_size": 49152,
+           "tie_word_embeddings": True, "model_type": "llama"}
+
+
+def setup_reference(ref: Path):
+    home = Path(tempfile.mkdtemp(prefix="lamq_ref_home_"))
+    snap = home / ".cache/huggingface/hub/models--HuggingFaceTB--SmolLM2-360M/snapshots/x"
+    snap.mkdir(parents=True)
+    (snap / "config.json").write_text(json.dumps(SMOLLM2))
+    os.environ["HOME"] = str(home)
+    os.environ["OPGRAPH_DEVICE"] = "cpu"
+    os.environ["PYTHONDONTWRITEBYTECODE"] = "1"
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, str(ref))
+    import opgraph.codes as C
+    cache = home / "codes"
+    shutil.copytree(ref / "cache" / "codes", cache)
+    C.CACHE = cache
+    return C
+
+
+def calib_H(n, tokens, seed, dead=()):
+    """Config-1-style statistics: Gaussian tokens, per-channel std lognormal(0, 1), 4 outlier channels ×20;
+    H = XᵀX / tokens, rounded to fp32 values so the fixture stores it exactly."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    std = torch.exp(torch.randn(n, generator=g, dtype=torch.float64))
+    out = torch.randperm(n, generator=g)[:4]
+    std[out] *= 20
+    X = torch.randn(tokens, n, generator=g, dtype=torch.float64) * std
+    for d in dead:
+        X[:, d] = 0
+    H = (X.T @ X / tokens).float().double()
+    return H
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    args = ap.parse_args()
+    C = setup_reference(args.reference.resolve())
+    import torch
+    import quantize as Q
+    import compiler_artifact as CA
+    from opgraph.frame import Environment
+
+    # the reference's fitted L=12 tables, as raw fp64
+    TABLES.mkdir(parents=True, exist_ok=True)
+    digests = {}
+    for k in (1, 2, 3, 4):
+        v = C.trellis_values(12, k, 256).double().numpy()
+        path = TABLES / f"trellis_L12_k{k}_T256_s0_ema.f64"
+        path.write_bytes(v.astype("<f8").tobytes())
+        digests[path.name] = hashlib.sha256(path.read_bytes()).hexdigest()
+    (TABLES / "SHA256SUMS").write_text("".join(f"{h}  {n}\n" for n, h in sorted(digests.items())))
+
+    # 1. Viterbi (codes.py:151-181): windows with a start state, free-start runs, small tables
+    vit = {}
+    g = torch.Generator().manual_seed(11)
+    for k in (1, 2, 3, 4):
+        v = C.trellis_values(12, k, 256)
+        X = torch.randn(48, 24, generator=g, dtype=torch.float64).float().double()
+        start = torch.randint(0, 4096, (48,), generator=g)
+        vit[f"k{k}_X"] = X.numpy()
+        vit[f"k{k}_start"] = start.numpy()
+        vit[f"k{k}_states_start"] = C.viterbi(X, v, 12, k, start=start).numpy()
+        X2 = torch.randn(8, 256, generator=g, dtype=torch.float64).float().double()
+        vit[f"k{k}_Xfree"] = X2.numpy()
+        vit[f"k{k}_states_free"] = C.viterbi(X2, v, 12, k).numpy()
+        X3 = torch.randn(16, 7, generator=g, dtype=torch.float64).float().double()  # short windows (T < 8)
+        vit[f"k{k}_Xshort"] = X3.numpy()
+        vit[f"k{k}_states_short"] = C.viterbi(X3, v, 12, k, start=torch.zeros(16, dtype=torch.long)).numpy()
+    v8 = torch.randn(256, generator=g, dtype=torch.float64).float().double()
+    X8 = torch.randn(32, 40, generator=g, dtype=torch.float64).float().double()
+    vit["L8_values"], vit["L8_X"], vit["L8_states"] = v8.numpy(), X8.numpy(), C.viterbi(X8, v8, 8, 2).numpy()
+    v4 = torch.randn(16, generator=g, dtype=torch.float64).float().double()
+    X4 = torch.randn(5, 7, generator=g, dtype=torch.float64).float().double()
+    vit["L4_values"], vit["L4_X"], vit["L4_states"] = v4.numpy(), X4.numpy(), C.viterbi(X4, v4, 4, 1).numpy()
+    np.savez_compressed(HERE / "viterbi.npz", **vit)
+
+    # 2. Hadamard rotations (codes.py:97-132)
+    rot = {}
+    for n, seed in ((64, 5), (200, 7), (256, 301), (320, 9), (960, 301), (2560, 1301), (4096, 2201), (9728, 3301)):
+        A, B = C.hadamard_factors(n)
+        R = C.rht(n, seed)
+        rot[f"n{n}_seed"] = np.array(seed)
+        rot[f"n{n}_shapes"] = np.array([A.shape[0], B.shape[0]])
+        rot[f"n{n}_rows"] = R[:2].numpy()
+        vec = torch.randn(n, generator=torch.Generator().manual_seed(n), dtype=torch.float64)
+        rot[f"n{n}_Rv"] = (R @ vec).numpy()
+        del R
+    np.savez_compressed(HERE / "rotation.npz", **rot)
+
+    # 3. Environment (frame.py:515-522), with a dead input
+    H = calib_H(128, 1024, 3, dead=(5,))
+    env = Environment(H)
+    np.savez_compressed(HERE / "environment.npz", H=H.float().numpy(), U=env.U.numpy(), dead=env.dead.numpy())
+
+    # 4. Row-trellis LDLQ words (codes.py:413-462 with RowTrellisCode, the lm2 path), pack_trellis
+    ldlq = {}
+    cases = [("a", 64, 256, 2, 300, 301), ("b", 48, 320, 3, 1200, 1201), ("c", 32, 200, 1, 7, 8), ("d", 32, 256, 4, 5, 6)]
+    for name, m, n, k, seed, in_seed in cases:
+        gW = torch.Generator().manual_seed(1000 + m + n + k)
+        W = (0.02 * torch.randn(m, n, generator=gW, dtype=torch.float64)).float().double()
+        H = calib_H(n, 2048, 17 + k)
+        code = C.RowTrellisCode(12, k, T=256, width=16, look=8)
+        net = C.ldlq_words([W], H, code, [seed], in_seed=in_seed, out_rot=False)[0]
+        Wq = net.matrix(dtype=torch.float64)
+        E = Wq - W
+        states = Q.trellis_states(net.cores["W"].data, code.values)
+        ldlq[f"{name}_W"] = W.float().numpy()
+        ldlq[f"{name}_H"] = H.float().numpy()
+        ldlq[f"{name}_meta"] = np.array([m, n, k, seed, in_seed])
+        ldlq[f"{name}_states"] = states.numpy()
+        ldlq[f"{name}_S"] = net.cores["W.S"].data.numpy()
+        ldlq[f"{name}_Wq"] = Wq.float().numpy()
+        ldlq[f"{name}_proxy"] = np.array(float((E @ H * E).sum()))
+        ldlq[f"{name}_packed"] = CA.pack_trellis(states.numpy().astype(np.int64), k)
+    # no rotation, with a dead input (syntax.py:100-101)
+    m, n, k = 32, 128, 2
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(77), dtype=torch.float64)).float().double()
+    H = calib_H(n, 1024, 23, dead=(3, 40))
+    code = C.RowTrellisCode(12, k, T=256, width=16, look=8)
+    net = C.ldlq_words([W], H, code, [0], incoherent=False)[0]
+    ldlq["e_W"], ldlq["e_H"], ldlq["e_meta"] = W.float().numpy(), H.float().numpy(), np.array([m, n, k, 0, -1])
+    ldlq["e_states"] = Q.trellis_states(net.cores["W"].data, code.values).numpy()
+    ldlq["e_S"] = net.cores["W.S"].data.numpy()
+    ldlq["e_Wq"] = net.matrix(dtype=torch.float64).float().numpy()
+    np.savez_compressed(HERE / "ldlq_row.npz", **ldlq)
+
+    # 5. Row groups (quantize.py:530-565) through the reference's own `word` (quantize.py:332-347)
+    m, n = 256, 256
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(5), dtype=torch.float64)).float().double()
+    H = calib_H(n, 2048, 31)
+    perm = torch.randperm(m, generator=torch.Generator().manual_seed(6))
+    groups = [{"rows": perm[:64], "bits": 2}, {"rows": perm[64:128], "bits": 1}, {"rows": perm[128:192], "bits": 3},
+              {"rows": perm[192:], "bits": 2}]
+    trellis = {b: C.RowTrellisCode(12, b, T=256, width=16, look=8) for b in (1, 2, 3, 4)}
+    in_seed = 3301
+
+    def round_group(rows, bits):
+        return Q.word(f"tr{bits}x", W[rows], H, 3300, trellis, in_seed, False)
+
+    Wq, rate, entry = Q.quantize_row_groups(W, groups, round_group, in_seed, True)
+    grp = {"W": W.float().numpy(), "H": H.float().numpy(), "perm": perm.numpy(), "bits": np.array([2, 1, 3, 2]),
+           "in_seed": np.array(in_seed), "Wq": Wq.float().numpy(), "states": entry["states"].numpy(),
+           "scales": entry["scales"].numpy(), "rate": np.array(rate)}
+    np.savez_compressed(HERE / "row_groups.npz", **grp)
+
+    # 6. Column trellis (TrellisCode, codes.py:363-383; the `measure` path, two-sided rotation)
+    m, n, k = 256, 64, 2
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(9), dtype=torch.float64)).float().double()
+    H = calib_H(n, 1024, 41)
+    code = C.TrellisCode(12, k, T=256)
+    net = C.ldlq_words([W], H, code, [40])[0]
+    col = {"W": W.float().numpy(), "H": H.float().numpy(), "meta": np.array([m, n, k, 40, 256]),
+           "Wq": net.matrix(dtype=torch.float64).float().numpy(), "settled": net.cores["W"].data.numpy().reshape(m, n),
+           "S": net.cores["W.S"].data.numpy()}
+    np.savez_compressed(HERE / "column_trellis.npz", **col)
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
