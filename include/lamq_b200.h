@@ -1,0 +1,80 @@
+/*
+ * lamq_b200 — C ABI of the B200 (sm_100a) kernels for LookAtMyQuant's quantization-build hot path.
+ *
+ * Every entry point takes plain device pointers and sizes, runs asynchronously on the given CUDA stream and returns an
+ * int status (LAMQ_OK = 0). The caller owns every buffer; entry points that need scratch take a caller-provided
+ * workspace whose size a *_workspace_size() query returns, and allocate nothing themselves. Row-major layouts
+ * throughout; `ld*` arguments are leading dimensions in elements.
+ *
+ * Reference interfaces replaced (ShinMegamiBoson/lookatmyquant, file:line):
+ *   lamq_viterbi           opgraph/codes.py:151-181   viterbi(X, values, L, k, chunk=None, start=None)
+ *   lamq_ldlq_rowtrellis   opgraph/syntax.py:86-124   sweep(W, env, project, width=16, lazy=128) with the project of
+ *                          opgraph/codes.py:442-450 and RowTrellisCode.step (codes.py:397-404)
+ */
+#ifndef LAMQ_B200_H
+#define LAMQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *lamq_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+enum {
+    LAMQ_OK = 0,
+    LAMQ_ERR_INVALID = 1,   /* bad shape, width, pointer or workspace size */
+    LAMQ_ERR_CUDA = 2,      /* a CUDA launch or runtime error (lamq_last_error() has the text) */
+    LAMQ_ERR_NOT_PD = 3,    /* a matrix was not positive definite even with the reference's extra damping */
+    LAMQ_ERR_TIMEOUT = 4,   /* a bounded device-side wait gave up */
+    LAMQ_ERR_NOT_PATH = 5   /* states are not a path through the trellis */
+};
+
+/* Version of this ABI (incremented on any signature change). */
+int lamq_abi_version(void);
+
+/* Text of the last error raised on the calling host thread ("" if none). */
+const char *lamq_last_error(void);
+
+/*
+ * Viterbi over a bitshift trellis (opgraph/codes.py:151-181).
+ * X: rows x T fp32 (ldX = T); values: 2^L fp32 table; start: rows int64 states or NULL (free start);
+ * states: rows x T int64 out. Supported: L = 12, k in 1..4, T >= 1.
+ * Each row's costs are fp32 and rounded exactly as the reference's tensor ops; ties go to the smallest predecessor and
+ * the smallest final state, so the states are identical to the reference's.
+ * workspace: lamq_viterbi_workspace_size(rows, T, L, k) bytes of device memory (the back-pointers).
+ */
+size_t lamq_viterbi_workspace_size(int64_t rows, int T, int L, int k);
+int lamq_viterbi(const float *X, int64_t rows, int T, const float *values, int L, int k, const int64_t *start,
+                 int64_t *states, void *workspace, size_t workspace_bytes, lamq_stream_t stream);
+
+/*
+ * The block-LDLQ sweep with a row trellis as its projection (opgraph/syntax.py:86-124 with codes.py:397-404,442-450):
+ * the lm2 build's per-matrix hot loop, fused into one kernel in which each row is settled by its own warp.
+ *
+ * T:        rows x n fp64 (ldT), in/out. On entry the targets in the rotated basis (X = W·R_inᵀ); columns flagged in
+ *           `dead` are zeroed first (syntax.py:100-101). On exit each column as it stood just before it was settled —
+ *           what `sweep` returns.
+ * U:        n x n fp64 (ldU), the upper Cholesky factor of H⁻¹ (frame.py:522).
+ * dead:     n bytes (nonzero = dead input) or NULL.
+ * S:        rows fp64, each row's RMS scale (codes.py:436).
+ * tables:   4 x 2^L fp64: the trellis values for k = 1, 2, 3, 4 (row of k at (k-1)·2^L).
+ * row_bits: rows bytes, each row's k in 1..4 (the row plan's widths); NULL means every row uses `k_all`.
+ * width, look, lazy: RowTrellisCode's width and look-ahead and sweep's lazy run (16, 8, 128 in the reference);
+ *           width + look <= 32, lazy a multiple of width.
+ * states:   rows x n int16 out (ldStates = n): the trellis states.
+ * settled:  rows x n fp64 out or NULL: the settled table values, in units of the row scale.
+ * Supported: L = 12.
+ */
+int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,
+                         const uint8_t *dead, const double *S, const double *tables, const uint8_t *row_bits, int k_all,
+                         int L, int width, int look, int lazy, int16_t *states, double *settled,
+                         lamq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAMQ_B200_H */

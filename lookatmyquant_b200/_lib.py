@@ -1,0 +1,79 @@
+"""ctypes bindings to liblamq_b200.so (the C ABI declared in include/lamq_b200.h).
+
+The library is the product's only compute path: if it is missing or cannot load, every entry point raises — there is
+no CPU or PyTorch fallback. `torch` tensors are passed as raw device pointers on the current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "liblamq_b200.so"
+_lib = None
+_lock = threading.Lock()
+
+LAMQ_OK, LAMQ_ERR_INVALID, LAMQ_ERR_CUDA, LAMQ_ERR_NOT_PD, LAMQ_ERR_TIMEOUT, LAMQ_ERR_NOT_PATH = range(6)
+
+_c = ctypes
+_P, _I64, _I32, _SZ, _D = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_size_t, _c.c_double
+
+# name -> (restype, argtypes): every symbol include/lamq_b200.h declares
+SIGNATURES = {
+    "lamq_abi_version": (_I32, []),
+    "lamq_last_error": (_c.c_char_p, []),
+    "lamq_viterbi_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
+    "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
+    "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
+                                    _P, _P, _P]),
+}
+
+
+class LamqError(RuntimeError):
+    pass
+
+
+def load():
+    """Loads liblamq_b200.so (raising if it was not built) and declares every exported signature."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise LamqError(f"{LIB_PATH} is missing: build it with `python -m lookatmyquant_b200.build` "
+                                "(the CUDA kernels are the only implementation; there is no fallback)")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                f = getattr(lib, name)
+                f.restype, f.argtypes = res, args
+            _lib = lib
+    return _lib
+
+
+LAUNCHES = {"count": 0}  # kernels launched through this module (the benchmark's gpu_launches)
+
+
+def check(status: int, what: str, kernels: int = 1):
+    """Raises on a non-zero status; on success counts the entry point's kernel launches."""
+    if status == LAMQ_OK:
+        LAUNCHES["count"] += kernels
+    if status != LAMQ_OK:
+        msg = load().lamq_last_error().decode(errors="replace")
+        if status == LAMQ_ERR_INVALID:
+            raise ValueError(f"{what}: {msg}")
+        if status == LAMQ_ERR_NOT_PD:
+            raise AssertionError("H is not positive definite even with damping")
+        if status == LAMQ_ERR_NOT_PATH:
+            raise ValueError("the given projection is not a path through this trellis")
+        raise LamqError(f"{what} failed (status {status}): {msg}")
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device=None) -> int:
+    import torch
+    return torch.cuda.current_stream(device).cuda_stream

@@ -1,0 +1,277 @@
+"""Trellis codes and block-LDLQ words on B200: the host side of `opgraph.codes` (ShinMegamiBoson/lookatmyquant).
+
+Same names, argument meaning and errors as the reference module, so the reference's callers can bind to it:
+
+    viterbi(X, values, L, k, chunk=None, start=None)            opgraph/codes.py:151-181
+    trellis_values(L, k, T=320, seed=0, refine=None, fit=None)  opgraph/codes.py:187-220 (the shipped fitted tables)
+    hadamard_factors(n), hadamard(n), rht(n, seed)             opgraph/codes.py:97-132
+    is_trellis_path(states, L, k)                               opgraph/codes.py:246-248
+    RowTrellisCode(L, k, T=256, width=16, look=8, seed=0)       opgraph/codes.py:386-410
+    TrellisCode(L, k, T=320, width=16, seed=0)                  opgraph/codes.py:363-383
+    ldlq_words(Ws, H, code, seeds, incoherent=True, in_seed=None, out_rot=True)   opgraph/codes.py:413-462
+
+The compute runs in liblamq_b200.so (sm_100a): the Viterbi decode and the fused row-trellis sweep are hand-written
+kernels. The words come back as `TrellisWord`s exposing what the reference's callers read from a Net (`matrix()`,
+`rate_bits()`, the states and the row scales).
+"""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+from .frame import Environment
+
+TABLES = Path(__file__).resolve().parent / "tables"
+DEVICE = "cuda"
+WIDTH, LOOK, LAZY = 16, 8, 128  # RowTrellisCode's block and look-ahead, sweep's lazy run (codes.py:391, syntax.py:88)
+
+
+def _dev(device=None) -> torch.device:
+    d = torch.device(device or DEVICE)
+    if d.type != "cuda":
+        raise RuntimeError("lookatmyquant_b200 runs on CUDA devices only (no CPU fallback)")
+    return d
+
+
+# ----------------------------------------------------------------------------- tables
+
+
+def trellis_values(L: int, k: int, T: int = 320, seed: int = 0, refine: int | None = None, fit: str | None = None
+                   ) -> torch.Tensor:
+    """The 2^L trellis values for (L, k, T, seed, fit), fp64 on the CPU (codes.py:187-220). The reference's fitted e-means
+    tables ship with this package; a table that was never fitted raises instead of being fitted here."""
+    fit = fit or "ema"
+    name = f"trellis_L{L}_k{k}_T{T}_s{seed}{'' if fit == 'lloyd' else '_' + fit}.f64"
+    path = TABLES / name
+    if not path.exists():
+        raise FileNotFoundError(f"no fitted trellis table {name} in {TABLES}")
+    return torch.from_numpy(np.fromfile(path, dtype="<f8").copy())
+
+
+def stacked_tables(L: int = 12, T: int = 256, device=None) -> torch.Tensor:
+    """The four tables k = 1..4 as one (4, 2^L) fp64 device tensor, the layout lamq_ldlq_rowtrellis reads."""
+    return torch.stack([trellis_values(L, k, T) for k in (1, 2, 3, 4)]).to(_dev(device))
+
+
+# ----------------------------------------------------------------------------- the trellis
+
+
+def viterbi(X: torch.Tensor, values: torch.Tensor, L: int, k: int, chunk: int | None = None,
+            start: torch.Tensor | None = None) -> torch.Tensor:
+    """The path through a bitshift trellis nearest each row of X in squared error (codes.py:151-181): states
+    s_t = (s_{t-1}·2^k + b_t) mod 2^L emitting values[s_t]; with `start`, the state before the first entry is given.
+    Costs are fp32 as in the reference, and the states are identical to its. Returns int64 states (rows, T) on X's
+    device. `chunk` is accepted for signature compatibility (the kernel needs no row chunking)."""
+    dev = _dev(X.device if X.is_cuda else None)
+    x = X.to(dev, torch.float32).contiguous()
+    if x.dim() != 2:
+        raise ValueError("viterbi expects a (rows, T) matrix")
+    rows, T = x.shape
+    C = values.to(dev, torch.float32).contiguous()
+    if C.numel() != 1 << L:
+        raise ValueError(f"values must have 2^L = {1 << L} entries")
+    st = None if start is None else start.to(dev, torch.int64).contiguous()
+    out = torch.empty(rows, T, dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    ws_bytes = lib.lamq_viterbi_workspace_size(rows, T, L, k)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        check(lib.lamq_viterbi(ptr(x), rows, T, ptr(C), L, k, ptr(st), ptr(out), ptr(ws), ws_bytes,
+                               stream_ptr(dev)), "lamq_viterbi")
+    return out.to(X.device)
+
+
+def is_trellis_path(states: torch.Tensor, L: int, k: int) -> bool:
+    """codes.py:246-248: every step keeps the previous state's low L − k bits as its high bits."""
+    return bool(torch.all((states[..., 1:] >> k) == (states[..., :-1] & ((1 << (L - k)) - 1))))
+
+
+# ----------------------------------------------------------------------------- Hadamard rotations
+
+
+def _is_prime(q: int) -> bool:
+    return q > 1 and all(q % d for d in range(2, math.isqrt(q) + 1))
+
+
+def _paley(q: int) -> torch.Tensor:
+    """Paley's first construction of order q + 1 for a prime q ≡ 3 (mod 4) (codes.py:87-94)."""
+    sq = {(x * x) % q for x in range(1, q)}
+    chi = torch.tensor([0.0] + [1.0 if a in sq else -1.0 for a in range(1, q)], dtype=torch.float64)
+    Q = chi[(torch.arange(q)[None, :] - torch.arange(q)[:, None]) % q]
+    S = torch.zeros(q + 1, q + 1, dtype=torch.float64)
+    S[0, 1:], S[1:, 0], S[1:, 1:] = 1, -1, Q
+    return S + torch.eye(q + 1, dtype=torch.float64)
+
+
+def _sylvester(a: int) -> torch.Tensor:
+    H = torch.ones(1, 1, dtype=torch.float64)
+    while H.shape[0] < 2 ** a:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
+    return H
+
+
+def hadamard_factors(n: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """A and B with hadamard(n) = (A ⊗ B)/√n (codes.py:104-119)."""
+    for a in range(int(math.log2(n)), -1, -1):
+        if n % 2 ** a:
+            continue
+        p = n // 2 ** a
+        if p in (1, 2) or (_is_prime(p - 1) and (p - 1) % 4 == 3):
+            if p == 1 and a > 1:
+                return _sylvester(a // 2), _sylvester(a - a // 2)
+            P = (torch.tensor([[1.0, 1.0], [1.0, -1.0]], dtype=torch.float64) if p == 2
+                 else torch.ones(1, 1, dtype=torch.float64) if p == 1 else _paley(p - 1))
+            return _sylvester(a), P
+    raise ValueError(f"no Hadamard construction here for order {n}")
+
+
+def hadamard(n: int) -> torch.Tensor:
+    A, B = hadamard_factors(n)
+    return torch.kron(A, B) / math.sqrt(n)
+
+
+def rht_signs(n: int, seed: int) -> torch.Tensor:
+    """The random signs of rht(n, seed) (codes.py:131), from torch's CPU generator as the reference draws them."""
+    u = torch.rand(n, generator=torch.Generator().manual_seed(int(seed)), dtype=torch.float64)
+    return torch.where(u < 0.5, -1.0, 1.0).to(torch.float64)
+
+
+def rht(n: int, seed: int) -> torch.Tensor:
+    """A randomized Hadamard transform hadamard(n)·diag(s) (codes.py:129-132), fp64 on the CPU."""
+    return hadamard(n) * rht_signs(n, seed)[None, :]
+
+
+# ----------------------------------------------------------------------------- codes
+
+
+class RowTrellisCode:
+    """Each row as one trellis path along its columns, from state 0 (codes.py:386-410). Block LDLQ settles `width`
+    columns at a time; each block's Viterbi also looks `look` columns ahead."""
+
+    def __init__(self, L: int, k: int, T: int = 256, width: int = 16, look: int = 8, seed: int = 0):
+        self.L, self.k, self.T, self.width, self.look, self.seed = L, k, T, width, look, seed
+        self.values = trellis_values(L, k, T, seed)
+        self.state = None
+
+    def step(self, j, X, ahead):
+        """Column j onward, `width` columns: the block's settled values, continuing each row's path (codes.py:397-404)."""
+        if j == 0:
+            self.state = torch.zeros(len(X), dtype=torch.long, device=X.device)
+        w = X.shape[1]
+        path = viterbi(torch.cat([X, ahead], 1), self.values, self.L, self.k, start=self.state)[:, :w]
+        self.state = path[:, -1]
+        return self.values.to(X.device, X.dtype)[path]
+
+
+class TrellisCode:
+    """Sequences of T consecutive outputs (one column) onto trellis paths (codes.py:363-383)."""
+
+    def __init__(self, L: int, k: int, T: int = 320, width: int = 16, seed: int = 0):
+        self.L, self.k, self.T, self.width, self.seed = L, k, T, width, seed
+        self.values = trellis_values(L, k, T, seed)
+
+    def _seqs(self, X):
+        o, w = X.shape
+        return X.reshape(o // self.T, self.T, w).permute(0, 2, 1).reshape(-1, self.T)
+
+    def project(self, X):
+        o, w = X.shape
+        Q = self.values.to(X.device, X.dtype)[viterbi(self._seqs(X), self.values, self.L, self.k)]
+        return Q.reshape(o // self.T, w, self.T).permute(0, 2, 1).reshape(o, w)
+
+
+class TrellisWord:
+    """One matrix's trellis word: W ≈ R_outᵀ·diag(S)·V[states]·R_in. The fields are device tensors:
+    `states` (rows × n int16), `scales` S (rows fp64), `settled` V[states] (fp64, units of S)."""
+
+    def __init__(self, states, scales, settled, values, L, k, in_seed, R_in, R_out=None, fixed_start=True, T=None):
+        self.states, self.scales, self.settled, self.values = states, scales, settled, values
+        self.L, self.k, self.in_seed, self.R_in, self.R_out = L, k, in_seed, R_in, R_out
+        self.fixed_start, self.T = fixed_start, T
+
+    def matrix(self, device=None, dtype=torch.float64) -> torch.Tensor:
+        """The dequantized matrix (reference Net.matrix, frame.py:112-134)."""
+        W = (self.settled * self.scales[:, None]) @ self.R_in
+        if self.R_out is not None:
+            W = self.R_out.T @ W
+        return W.to(device=device or W.device, dtype=dtype)
+
+    def rate_bits(self) -> float:
+        """Stored bits (frame.py:137-147): k per entry, plus L − k per sequence without a fixed start, 16 per row
+        scale, one sign per input (and per output with an output rotation)."""
+        m, n = self.states.shape
+        bits = float(m * n * self.k) + 16.0 * m + n + (m if self.R_out is not None else 0)
+        if not self.fixed_start:
+            bits += (m * n / self.T) * (self.L - self.k)
+        return bits
+
+
+# ----------------------------------------------------------------------------- words
+
+
+def _row_trellis_sweep(X, S, env, code, row_bits=None, settled_out=True):
+    """The fused sweep kernel: X (rows × n fp64, device) is settled in place; returns (before, states, settled)."""
+    dev = X.device
+    rows, n = X.shape
+    T = X.contiguous().clone()
+    states = torch.empty(rows, n, dtype=torch.int16, device=dev)
+    settled = torch.empty(rows, n, dtype=torch.float64, device=dev) if settled_out else None
+    tables = stacked_tables(code.L, code.T, dev) if code.L == 12 else None
+    if tables is None:
+        raise ValueError("the fused sweep supports L = 12")
+    if row_bits is None:
+        tables[code.k - 1] = code.values.to(dev)
+    dead = env.dead.to(dev, torch.uint8) if bool(env.dead.any()) else None
+    with torch.cuda.device(dev):
+        check(_lib.load().lamq_ldlq_rowtrellis(
+            ptr(T), n, rows, n, ptr(env.U), env.U.stride(0), ptr(dead), ptr(S.contiguous()), ptr(tables),
+            ptr(row_bits), code.k, code.L, code.width, code.look, LAZY, ptr(states), ptr(settled),
+            stream_ptr(dev)), "lamq_ldlq_rowtrellis")
+    return T, states, settled
+
+
+def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list[int], incoherent: bool = True,
+               in_seed: int | None = None, out_rot: bool = True, device=None) -> list[TrellisWord]:
+    """(Gauge: incoherence →) Split(scale, per row, by RMS) → (block LDLQ sweep →) the trellis code, for matrices that
+    read the same input (codes.py:413-462), on the GPU in fp64. Matrices are swept together (rows do not interact
+    under Refit). Returns one TrellisWord per matrix."""
+    dev = _dev(device)
+    Ws = [W.to(dev, torch.float64) for W in Ws]
+    n = Ws[0].shape[1]
+    R_in = rht(n, seeds[0] + 1 if in_seed is None else in_seed).to(dev) if incoherent else None
+    Xs, R_outs = [], []
+    for W, s in zip(Ws, seeds):
+        if incoherent and out_rot:
+            R_out = rht(W.shape[0], s).to(dev)
+            Xs.append(R_out @ W @ R_in.T)
+            R_outs.append(R_out)
+        else:
+            Xs.append(W @ R_in.T if incoherent else W)
+            R_outs.append(None)
+    X = torch.cat(Xs)
+    S = X.pow(2).mean(1).sqrt().clamp(min=1e-12)
+    if isinstance(code, RowTrellisCode):
+        if H is None:
+            raise NotImplementedError("row-trellis words without H (plain Viterbi per row) are not wired yet")
+        Hr = (R_in @ H.to(dev, torch.float64) @ R_in.T) if incoherent else H.to(dev, torch.float64)
+        env = Environment(Hr)
+        _, states, settled = _row_trellis_sweep(X, S, env, code)
+        fixed, T = True, None
+    elif isinstance(code, TrellisCode):
+        raise NotImplementedError("the column-trellis sweep is not wired yet")
+    else:
+        raise TypeError(f"unsupported code {type(code).__name__}")
+    eye = torch.eye(n, dtype=torch.float64, device=dev)
+    out, r0 = [], 0
+    for W, R_out in zip(Ws, R_outs):
+        r1 = r0 + W.shape[0]
+        out.append(TrellisWord(states[r0:r1], S[r0:r1], settled[r0:r1], code.values, code.L, code.k,
+                               in_seed, R_in if R_in is not None else eye, R_out, fixed, T))
+        r0 = r1
+    return out

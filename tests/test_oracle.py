@@ -1,0 +1,131 @@
+"""The oracle against the reference's own outputs (golden vectors made by tests/golden/make_golden.py)."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import table
+from oracle import core as O
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4])
+def test_viterbi_matches_reference(golden, k):
+    g = golden("viterbi")
+    v = table(k)
+    assert np.array_equal(O.viterbi(g[f"k{k}_X"], v, 12, k, start=g[f"k{k}_start"]), g[f"k{k}_states_start"])
+    assert np.array_equal(O.viterbi(g[f"k{k}_Xfree"], v, 12, k), g[f"k{k}_states_free"])
+    zero = np.zeros(len(g[f"k{k}_Xshort"]), dtype=np.int64)
+    assert np.array_equal(O.viterbi(g[f"k{k}_Xshort"], v, 12, k, start=zero), g[f"k{k}_states_short"])
+
+
+def test_viterbi_small_tables(golden):
+    g = golden("viterbi")
+    assert np.array_equal(O.viterbi(g["L8_X"], g["L8_values"], 8, 2), g["L8_states"])
+    assert np.array_equal(O.viterbi(g["L4_X"], g["L4_values"], 4, 1), g["L4_states"])
+
+
+def test_viterbi_is_optimal():
+    """As tests/test_codes.py:101-117 of the reference: the decoded path is the brute-force minimum (L=4, k=1, T=7)."""
+    rng = np.random.default_rng(0)
+    v = rng.standard_normal(16).astype(np.float32).astype(np.float64)
+    X = rng.standard_normal((5, 7)).astype(np.float32).astype(np.float64)
+    st = O.viterbi(X, v, 4, 1)
+    assert O.is_trellis_path(st, 4, 1)
+    got = ((X - v[st]) ** 2).sum(1)
+    for r in range(len(X)):
+        assert abs(got[r] - O.viterbi_bruteforce(X[r], v, 4, 1)) < 1e-4
+
+
+def test_empty_and_single_column():
+    v = table(2)
+    assert O.viterbi(np.zeros((0, 5)), v, 12, 2).shape == (0, 5)
+    x = np.array([[0.3], [-1.2]])
+    st = O.viterbi(x, v, 12, 2)
+    assert np.array_equal(st[:, 0], np.argmin((x.astype(np.float32) - v.astype(np.float32)) ** 2, axis=1))
+
+
+@pytest.mark.parametrize("n", [64, 200, 256, 320, 960, 2560, 4096, 9728])
+def test_rotations_match_reference(golden, n):
+    g = golden("rotation")
+    A, B = O.hadamard_factors(n)
+    assert (A.shape[0], B.shape[0]) == tuple(g[f"n{n}_shapes"])
+    R = O.rht(n, int(g[f"n{n}_seed"]))
+    assert np.array_equal(R[:2], g[f"n{n}_rows"])
+    vec = torch.randn(n, generator=torch.Generator().manual_seed(n), dtype=torch.float64).numpy()
+    assert np.abs(R @ vec - g[f"n{n}_Rv"]).max() < 1e-12
+    if n <= 2560:
+        assert np.abs(R @ R.T - np.eye(n)).max() < 1e-10
+
+
+def test_environment_matches_reference(golden):
+    g = golden("environment")
+    U, dead, _ = O.environment(g["H"].astype(np.float64))
+    assert np.array_equal(dead, g["dead"])
+    assert np.abs(U - g["U"]).max() <= 1e-12 * np.abs(g["U"]).max()
+
+
+@pytest.mark.parametrize("case", ["a", "b", "c", "d"])
+def test_ldlq_row_words_match_reference(golden, case):
+    g = golden("ldlq_row")
+    m, n, k, seed, in_seed = (int(x) for x in g[f"{case}_meta"])
+    out = O.ldlq_row_words(g[f"{case}_W"].astype(np.float64), g[f"{case}_H"].astype(np.float64), table(k), 12, k,
+                           in_seed)
+    assert np.array_equal(out["states"], g[f"{case}_states"])
+    assert np.abs(out["S"] - g[f"{case}_S"]).max() < 1e-15
+    assert np.abs(out["Wq"] - g[f"{case}_Wq"]).max() < 1e-7  # the fixture is stored in fp32
+    assert abs(out["proxy"] - float(g[f"{case}_proxy"])) <= 1e-12 * abs(float(g[f"{case}_proxy"]))
+    assert np.array_equal(O.pack_trellis(out["states"], k), g[f"{case}_packed"])
+    assert np.array_equal(O.unpack_trellis(g[f"{case}_packed"], k, n), out["states"])
+
+
+def test_ldlq_without_rotation_dead_inputs(golden):
+    g = golden("ldlq_row")
+    m, n, k = (int(x) for x in g["e_meta"][:3])
+    W, H = g["e_W"].astype(np.float64), g["e_H"].astype(np.float64)
+    S = O.row_scale(W)
+    U, dead, _ = O.environment(H)
+    assert dead.sum() == 2
+    _, settled, states = O.row_trellis_sweep(W, S, U, dead, table(k), 12, k)
+    assert np.array_equal(states, g["e_states"])
+    assert np.abs(settled * S[:, None] - g["e_Wq"]).max() < 1e-7
+
+
+def test_row_groups_match_reference(golden):
+    """quantize.quantize_row_groups (quantize.py:530-565): groups swept separately, states offset by 4096 per table."""
+    g = golden("row_groups")
+    W, H, perm = g["W"].astype(np.float64), g["H"].astype(np.float64), g["perm"]
+    groups = [(perm[i * 64:(i + 1) * 64], int(b)) for i, b in enumerate(g["bits"])]
+    in_seed = int(g["in_seed"])
+    states = np.empty(W.shape, dtype=np.int64)
+    for ti, (rows, bits) in enumerate(groups):
+        out = O.ldlq_row_words(W[rows], H, table(bits), 12, bits, in_seed)
+        states[rows] = out["states"] + 4096 * ti
+    assert np.array_equal(states, g["states"])
+
+
+def test_column_trellis_matches_reference(golden):
+    """TrellisCode (codes.py:363-383), the `measure` path with a two-sided rotation."""
+    g = golden("column_trellis")
+    m, n, k, seed, Tm = (int(x) for x in g["meta"])
+    W, H = g["W"].astype(np.float64), g["H"].astype(np.float64)
+    Ri, Ro = O.rht(n, seed + 1), O.rht(m, seed)
+    X = Ro @ W @ Ri.T
+    S = O.row_scale(X)
+    U, dead, _ = O.environment(Ri @ H @ Ri.T)
+    _, settled, states = O.column_trellis_sweep(X, S, U, dead, table(k), 12, k, Tm)
+    assert np.array_equal(settled, g["settled"])
+    Wq = Ro.T @ (settled * S[:, None]) @ Ri
+    assert np.abs(Wq - g["Wq"]).max() < 1e-7
+
+
+def test_pack_symbols_round_trip():
+    rng = np.random.default_rng(1)
+    for bits in (1, 2, 3, 4, 5, 8):
+        q = rng.integers(0, 1 << bits, size=(7, 45))
+        assert np.array_equal(O.unpack_symbols(O.pack_symbols(q, bits), bits, 45), q)
+
+
+def test_trellis_states_inverts_table():
+    v = table(3)
+    st = np.random.default_rng(2).integers(0, 4096, size=(4, 9))
+    assert np.array_equal(O.trellis_states(v[st], v), st.astype(np.int16))
