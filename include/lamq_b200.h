@@ -51,6 +51,21 @@ int lamq_viterbi(const float *X, int64_t rows, int T, const float *values, int L
                  int64_t *states, void *workspace, size_t workspace_bytes, lamq_stream_t stream);
 
 /*
+ * lamq_viterbi without a workspace: no counterpart in the reference (its Viterbi is a PyTorch loop). For callers that
+ * cannot allocate device memory — a host application whose own pool owns the whole device and forbids library
+ * allocations, or an FFI binding (cgo, JNI, N-API) with no device allocator to take a workspace from. Same inputs,
+ * outputs and states as lamq_viterbi; it calls no cudaMalloc, cudaFree or allocating library routine. Sequences
+ * longer than 32 entries keep their back-pointers in a LAMQ_VITERBI_NOALLOC_SCRATCH_BYTES (32 MiB) array built into
+ * the library's device image, so rows x T may be at most 131072 when T > 32 (larger inputs are rejected with
+ * LAMQ_ERR_INVALID); sequences of at most 32 entries need no scratch and have no limit. The call runs on the current
+ * device; its first call on each device looks up the array's device address, so make that first call before any
+ * stream capture. All calls on a device share the array: calls whose kernels overlap on the GPU race on it.
+ */
+#define LAMQ_VITERBI_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *values, int L, int k,
+                         const int64_t *start, int64_t *states, lamq_stream_t stream);
+
+/*
  * The block-LDLQ sweep with a row trellis as its projection (opgraph/syntax.py:86-124 with codes.py:397-404,442-450):
  * the lm2 build's per-matrix hot loop, fused into one kernel in which each row is settled by its own warp.
  *

@@ -26,6 +26,7 @@ SIGNATURES = {
     "lamq_last_error": (_c.c_char_p, []),
     "lamq_viterbi_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
+    "lamq_viterbi_noalloc": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P]),
 }

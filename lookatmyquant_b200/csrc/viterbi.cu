@@ -3,6 +3,8 @@
 // Used for whole-row decodes (RowTrellisCode.apply without a sweep, codes.py:406-410), the column runs of
 // TrellisCode.project (codes.py:375-378) and the kernel-level parity tests. Sequences of up to 32 entries keep their
 // back-pointers in shared memory; longer ones keep them in the caller's workspace (256 bytes per entry per row).
+#include <mutex>
+
 #include "lamq_common.cuh"
 #include "trellis_warp.cuh"
 
@@ -112,5 +114,89 @@ extern "C" int lamq_viterbi(const float *X, int64_t rows, int T, const float *va
     const int64_t grid = (rows + kVitWarps - 1) / kVitWarps;
     viterbi_kernel<<<(unsigned)grid, kVitWarps * 32, smem, (cudaStream_t)stream>>>(p, k);
     LAMQ_CHECK_LAUNCH("lamq_viterbi");
+    return LAMQ_OK;
+}
+
+// ----------------------------------------------------------------------------- allocation-free variant
+//
+// Some callers cannot allocate device memory at all: a host application that hands every byte of the device to its
+// own memory pool and forbids libraries from calling cudaMalloc, or a foreign-language binding (cgo, JNI, N-API)
+// that has no device allocator of its own to carve a workspace from. lamq_viterbi_noalloc serves them: it decodes
+// exactly as lamq_viterbi does, but keeps the back-pointers of long sequences in the array below, which is part of
+// the library's device image (every GPU that loads the library holds these 32 MiB until the process exits).
+//
+// The array's name in host code is only a host-side stand-in for the symbol, never a device address, so the host
+// looks the real address up with cudaGetSymbolAddress once per device (with that device current) and passes it to
+// the kernel. Every call on a device shares the one array and it keeps whatever the last call left in it; nothing in
+// it needs to start at zero, because each back-pointer word the traceback reads was written earlier in the same call.
+// Two calls whose kernels overlap on the GPU (on different streams, say) would race on the array.
+
+namespace lamq {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = LAMQ_VITERBI_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned long long g_noalloc_backptr[kNoAllocScratchBytes / sizeof(unsigned long long)];
+
+constexpr int kMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static unsigned long long *g_noalloc_addr[kMaxDevices] = {};
+
+// The device address of g_noalloc_backptr on the current device, looked up on the first call per device.
+int noalloc_scratch(unsigned long long **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error("lamq_viterbi_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("lamq_viterbi_noalloc: device %d beyond the %d this library tracks", dev, kMaxDevices);
+        return LAMQ_ERR_INVALID;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_backptr);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("lamq_viterbi_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = reinterpret_cast<unsigned long long *>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return LAMQ_OK;
+}
+
+}  // namespace
+}  // namespace lamq
+
+extern "C" int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *values, int L, int k,
+                                    const int64_t *start, int64_t *states, lamq_stream_t stream) {
+    LAMQ_REQUIRE(L == kL, "lamq_viterbi_noalloc: only L = 12 is supported (got %d)", L);
+    LAMQ_REQUIRE(k >= 1 && k <= 4, "lamq_viterbi_noalloc: k must be 1..4 (got %d)", k);
+    LAMQ_REQUIRE(rows >= 0 && T >= 0, "lamq_viterbi_noalloc: negative shape");
+    if (rows == 0 || T == 0) return LAMQ_OK;
+    const size_t need = lamq_viterbi_workspace_size(rows, T, L, k);
+    LAMQ_REQUIRE(need <= kNoAllocScratchBytes,
+                 "lamq_viterbi_noalloc: %lld sequences of %d entries need %zu bytes of back-pointers, more than the "
+                 "built-in %zu (rows x T at most %zu for T > 32); use lamq_viterbi with a workspace",
+                 (long long)rows, T, need, kNoAllocScratchBytes, kNoAllocScratchBytes / (32 * 8));
+    LAMQ_REQUIRE(X && values && states, "lamq_viterbi_noalloc: null pointer");
+    unsigned long long *scratch = nullptr;
+    if (need != 0) {
+        const int st = noalloc_scratch(&scratch);
+        if (st != LAMQ_OK) return st;
+    }
+    VitParams p{X, rows, T, values, start, states, need ? scratch : nullptr};
+    const size_t per_warp = 2 * 2048 * sizeof(float) + (need ? 0 : (size_t)kShortT * 32 * 8);
+    const size_t smem = kVitWarps * per_warp;
+    cudaError_t e = cudaFuncSetAttribute(viterbi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+        set_error("lamq_viterbi_noalloc: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    const int64_t grid = (rows + kVitWarps - 1) / kVitWarps;
+    viterbi_kernel<<<(unsigned)grid, kVitWarps * 32, smem, (cudaStream_t)stream>>>(p, k);
+    LAMQ_CHECK_LAUNCH("lamq_viterbi_noalloc");
     return LAMQ_OK;
 }
