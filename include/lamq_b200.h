@@ -10,6 +10,9 @@
  *   lamq_viterbi           opgraph/codes.py:151-181   viterbi(X, values, L, k, chunk=None, start=None)
  *   lamq_ldlq_rowtrellis   opgraph/syntax.py:86-124   sweep(W, env, project, width=16, lazy=128) with the project of
  *                          opgraph/codes.py:442-450 and RowTrellisCode.step (codes.py:397-404)
+ *   lamq_xtx_accumulate,   quantize.py:1412-1470      H += Xᵀ(w⊙X), D += X_refᵀ(w⊙X) per calibration chunk, then
+ *   lamq_weighted_split,                              H/n_tok and D/n_tok − H in fp64 (inline in quantize_stage);
+ *   lamq_hessian_finalize  compiler.py:233-265        the unweighted H of `capture`
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -87,6 +90,34 @@ int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const doub
                          const uint8_t *dead, const double *S, const double *tables, const uint8_t *row_bits, int k_all,
                          int L, int width, int look, int lazy, int16_t *states, double *settled,
                          lamq_stream_t stream);
+
+/*
+ * Tensor-core contraction over tokens: acc[j][i] += Σ_t A[t][i]·B[t][j] (bf16 in, fp32 accumulate) for i, j < d.
+ * A, B: tokens x d bf16 (raw 16-bit words), row-major with leading dimensions lda, ldb (multiples of 8, 16-byte
+ * aligned). acc: d x d fp32 (ldacc), accumulated into (zero it before the first call). The sum is accumulated on chip
+ * over chunks of `chunk_tokens` tokens (a multiple of 64) and each chunk's partial is added into acc.
+ * symmetric != 0 (A and B the same tokens, C symmetric): only the blocks of rows j >= columns i are computed; read
+ * the result through lamq_hessian_finalize. status: a device int, 0 on entry; a bounded device wait that gives up
+ * sets it to LAMQ_ERR_TIMEOUT (then the result is invalid). H = XᵀX is A = B = X; the QEP moment D = X_refᵀX is A = X,
+ * B = X_ref (acc then holds D itself).
+ */
+int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb, int64_t tokens, int d,
+                        int symmetric, float *acc, int64_t ldacc, int64_t chunk_tokens, int *status,
+                        lamq_stream_t stream);
+
+/*
+ * Token weights (quantize.py:1389-1391, 593-629): the weighted tokens' share Σ_t (w_t − 1)·x_t ⊗ y_t as two extra
+ * rows per token for lamq_xtx_accumulate. For each r < nw, t = idx[r]: out_split row r = hi, row r + nw = lo of
+ * (w[t] − 1)·scaled[t] (fp32; hi = bf16(y), lo = bf16(y − hi)); out_plain rows r and r + nw = plain[t].
+ * out_split and out_plain: 2·nw x d bf16 (leading dimension d).
+ */
+int lamq_weighted_split(const uint16_t *scaled, int64_t lds, const uint16_t *plain, int64_t ldp, const float *w,
+                        const int32_t *idx, int64_t nw, int d, uint16_t *out_split, uint16_t *out_plain,
+                        lamq_stream_t stream);
+
+/* H[r][c] = accH[max(r,c)][min(r,c)] / n_tok (fp64, symmetric); with accD, D = accD / n_tok − H. d x d outputs. */
+int lamq_hessian_finalize(const float *accH, const float *accD, int d, int64_t ld, double n_tok, double *H, double *D,
+                          lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

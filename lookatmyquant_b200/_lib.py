@@ -27,6 +27,9 @@ SIGNATURES = {
     "lamq_viterbi_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "lamq_viterbi_noalloc": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P]),
+    "lamq_xtx_accumulate": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _I64, _I64, _P, _P]),
+    "lamq_weighted_split": (_I32, [_P, _I64, _P, _I64, _P, _P, _I64, _I32, _P, _P, _P]),
+    "lamq_hessian_finalize": (_I32, [_P, _P, _I32, _I64, _D, _P, _P, _P]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P]),
 }

@@ -1,0 +1,444 @@
+// Token-weighted Hessian (and QEP cross-moment) accumulation on tcgen05 tensor cores.
+//
+// Reference: quantize.py:1412-1470 (`quantize_stage`): per calibration chunk H += Xᵀ(w⊙X) and D += X_refᵀ(w⊙X) in
+// fp32, then H/n_tok and D/n_tok − H as fp64; compiler.py:233-265 (`capture`) is the unweighted form.
+//
+// The contraction C[j][i] += Σ_t A[t][i]·B[t][j] over tokens t runs as a persistent warp-specialised GEMM:
+//   warp 0     one thread issues TMA loads of 64-token × 128-column tiles of A and B (bf16, row-major tokens × d,
+//              so both operands are MN-major in shared memory, 128-byte swizzle) into a 6-stage ring;
+//   warp 1     one thread issues tcgen05.mma (M = N = 128, K = 16, bf16 × bf16 → fp32) into one of two TMEM
+//              accumulators, releasing each stage with tcgen05.commit;
+//   warps 2-5  drain a finished accumulator with tcgen05.ld into an fp32 tile held in their registers (one row of
+//              128 columns per thread, added with round-to-nearest), while the MMA thread fills the other one; at the
+//              end of a unit they add the tile into the fp32 d × d accumulator in global memory (coalesced: written
+//              transposed).
+// The tensor core's own fp32 accumulation truncates (it loses about half an ulp per MMA on average, always towards
+// zero), so TMEM only ever accumulates kDrainBlocks × 4 = 32 MMAs (512 tokens) before it is drained into the
+// registers: the bias stays near 1e-6 relative, where a whole chunk in TMEM would bias H by more than the 1e-5 bar.
+// A work unit is one 128 × 128 output tile over one chunk of tokens. Units are ordered by super-blocks of 12 × 12 tiles, then chunk,
+// then tile, so the ~148 concurrent CTAs share their A and B tiles through L2. For H only tiles with ti <= tj are
+// computed (H is symmetric); the finalize kernel mirrors them.
+//
+// Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
+// (A = X, B = X: exact products), and the weighted tokens add Σ_t (w_t − 1)·x_t x_tᵀ in a second pass over only
+// those tokens, with (w − 1)·x split into a bf16 pair hi + lo (hi = bf16(y), lo = bf16(y − hi)), which carries y to
+// 2⁻¹⁷ relative — the same result as the reference's fp32 w⊙X to well within its fp32 rounding.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "lamq_common.cuh"
+#include "sm100.cuh"
+
+namespace lamq {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KiB: two 64-column boxes of 64 tokens
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int HALF_BYTES = 64 * BK * 2;  // one TMA box: 64 columns x 64 tokens = 8 KiB (LBO between MN halves)
+constexpr int SB = 12;                   // tiles per super-block side
+constexpr int kDrainBlocks = 8;          // 64-token blocks accumulated in TMEM between drains (32 MMAs)
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;      // two 128 x 128 fp32 accumulators
+constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;
+
+struct GemmParams {
+    float *acc;
+    int64_t ldc;
+    int d;
+    int ntile;
+    int ngroup;
+    int nchunk;
+    int kblocks;            // total 64-token blocks
+    int kblocks_per_chunk;
+    int symmetric;
+    int64_t units;
+    int *status;
+};
+
+struct Unit {
+    int ti, tj, kb0, nkb;
+};
+
+__device__ __forceinline__ int group_tiles(int gi, int gj, const GemmParams &p) {
+    const int r0 = gi * SB, r1 = min(p.ntile, r0 + SB), c0 = gj * SB, c1 = min(p.ntile, c0 + SB);
+    if (!p.symmetric || gi < gj) return (r1 - r0) * (c1 - c0);
+    if (gi > gj) return 0;
+    const int m = r1 - r0;
+    return m * (m + 1) / 2;
+}
+
+// The u-th work unit: super-blocks in row-major order (only gi <= gj when symmetric), then chunks, then tiles.
+__device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
+    for (int gi = 0; gi < p.ngroup; ++gi) {
+        for (int gj = p.symmetric ? gi : 0; gj < p.ngroup; ++gj) {
+            const int nt = group_tiles(gi, gj, p);
+            const int64_t nu = (int64_t)nt * p.nchunk;
+            if (u >= nu) {
+                u -= nu;
+                continue;
+            }
+            const int chunk = (int)(u / nt), local = (int)(u % nt);
+            const int r0 = gi * SB, c0 = gj * SB, r1 = min(p.ntile, r0 + SB), c1 = min(p.ntile, c0 + SB);
+            if (p.symmetric && gi == gj) {
+                int rem = local;
+                const int m = r1 - r0;
+                out.ti = r0;
+                out.tj = r0;
+                for (int row = 0; row < m; ++row) {
+                    const int len = m - row;
+                    if (rem < len) {
+                        out.ti = r0 + row;
+                        out.tj = r0 + row + rem;
+                        break;
+                    }
+                    rem -= len;
+                }
+            } else {
+                const int w = c1 - c0;
+                out.ti = r0 + local / w;
+                out.tj = c0 + local % w;
+            }
+            out.kb0 = chunk * p.kblocks_per_chunk;
+            out.nkb = min(p.kblocks_per_chunk, p.kblocks - out.kb0);
+            return true;
+        }
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    xtx_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 5);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+    const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+    const uint32_t drain = smem_u32(bars + 2 * STAGES + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull0 + 8 * a, 1);
+            mbar_init(tempty0 + 8 * a, 128);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+        prefetch_tmap(&mapA);
+        prefetch_tmap(&mapB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            int64_t issued = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+                Unit U;
+                if (!unit_at(u, p, U)) break;
+                for (int kb = 0; kb < U.nkb; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full0 + 8 * stage;
+                    mbar_expect_tx(fb, STAGE_BYTES);
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+                    const int t = (U.kb0 + kb) * BK;
+                    tma_load_2d(sa, &mapA, U.ti * BM, t, fb);
+                    tma_load_2d(sa + HALF_BYTES, &mapA, U.ti * BM + 64, t, fb);
+                    tma_load_2d(sb, &mapB, U.tj * BN, t, fb);
+                    tma_load_2d(sb + HALF_BYTES, &mapB, U.tj * BN + 64, t, fb);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) {  // error path: let the copies already in flight land before the CTA exits
+                const int64_t outstanding = issued < STAGES ? issued : STAGES;
+                for (int64_t i = issued - outstanding; i < issued; ++i) {
+                    const int s = (int)(i % STAGES);
+                    const uint32_t ph = (uint32_t)((i / STAGES) & 1);
+                    const unsigned long long t0 = globaltimer();
+                    while (!mbar_try_wait(full0 + 8 * s, ph) && globaltimer() - t0 < kWaitTimeoutNs) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            const uint32_t idesc = idesc_bf16_f32(BM, BN, true, true);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t uses[2] = {0, 0};
+            int acc = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+                Unit U;
+                if (!unit_at(u, p, U)) break;
+                for (int sub = 0; ok && sub < U.nkb; sub += kDrainBlocks) {
+                    if (!mbar_wait(tempty0 + 8 * acc, (uses[acc] & 1) ^ 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    ++uses[acc];
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * BN;
+                    const int kend = min(U.nkb, sub + kDrainBlocks);
+                    for (int kb = sub; kb < kend; ++kb) {
+                        if (!mbar_wait(full0 + 8 * stage, phase, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            // 16 tokens = two 8-row groups of 128 bytes: advance 2 KiB per K step
+                            const uint64_t ad = smem_desc_sw128(sa + kk * 2048, HALF_BYTES, 1024);
+                            const uint64_t bd = smem_desc_sw128(sb + kk * 2048, HALF_BYTES, 1024);
+                            mma_f16_ss(d, ad, bd, idesc, (kb > sub || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit(empty0 + 8 * stage);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(tfull0 + 8 * acc);
+                    acc ^= 1;
+                }
+            }
+            // every MMA this thread issued completes before TMEM is released
+            mma_commit(drain);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitTimeoutNs) {
+            }
+        }
+    } else {  // ---- epilogue: warps 2..5 own TMEM lanes 32·(warp % 4) ..
+        const int q = warp & 3;
+        uint32_t uses[2] = {0, 0};
+        int acc = 0;
+        for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
+            Unit U;
+            if (!unit_at(u, p, U)) break;
+            float tile[BN];
+#pragma unroll
+            for (int c = 0; c < BN; ++c) tile[c] = 0.f;
+            bool ok = true;
+            for (int sub = 0; sub < U.nkb; sub += kDrainBlocks) {
+                if (!mbar_wait(tfull0 + 8 * acc, uses[acc] & 1, p.status)) {
+                    ok = false;
+                    break;
+                }
+                ++uses[acc];
+                tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + acc * BN;
+#pragma unroll
+                for (int c = 0; c < BN / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld16(tbase + c * 16, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) tile[c * 16 + e] = __fadd_rn(tile[c * 16 + e], __uint_as_float(r[e]));
+                }
+                tc_fence_before();
+                mbar_arrive(tempty0 + 8 * acc);
+                acc ^= 1;
+            }
+            if (!ok) break;
+            const int i = U.ti * BM + 32 * q + lane;
+            if (i < p.d) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) {
+                    const int j = U.tj * BN + c;
+                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, tile[c]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// Weighted tokens: out_plain rows r and r + nw hold plain[idx[r]]; out_split row r holds hi and row r + nw holds lo
+// of y = (w[idx[r]] − 1)·scaled[idx[r]] (fp32), hi = bf16(y), lo = bf16(y − hi).
+__global__ void weighted_split_kernel(const __nv_bfloat16 *__restrict__ scaled, int64_t lds,
+                                      const __nv_bfloat16 *__restrict__ plain, int64_t ldp,
+                                      const float *__restrict__ w, const int32_t *__restrict__ idx, int64_t nw, int d,
+                                      __nv_bfloat16 *__restrict__ out_split, __nv_bfloat16 *__restrict__ out_plain) {
+    const int64_t r = blockIdx.x;
+    if (r >= nw) return;
+    const int64_t t = idx[r];
+    const float f = __fsub_rn(w[t], 1.0f);
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        const float y = __fmul_rn(f, __bfloat162float(scaled[t * lds + c]));
+        const __nv_bfloat16 hi = __float2bfloat16_rn(y);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(y, __bfloat162float(hi)));
+        out_split[r * d + c] = hi;
+        out_split[(r + nw) * d + c] = lo;
+        const __nv_bfloat16 pv = plain[t * ldp + c];
+        out_plain[r * d + c] = pv;
+        out_plain[(r + nw) * d + c] = pv;
+    }
+}
+
+// H[r][c] = acc[max][min] / n_tok (the computed triangle, mirrored); D = accD / n_tok − H.
+__global__ void finalize_kernel(const float *__restrict__ accH, const float *__restrict__ accD, int64_t lda, int d,
+                                double inv_n, double *__restrict__ H, double *__restrict__ D) {
+    const int64_t n = (int64_t)d * d;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e / d), c = (int)(e % d);
+        const int hi = r > c ? r : c, lo = r > c ? c : r;
+        const double h = (double)accH[(int64_t)hi * lda + lo] * inv_n;
+        H[e] = h;
+        if (D != nullptr) D[e] = (double)accD[(int64_t)r * lda + c] * inv_n - h;
+    }
+}
+
+// ---- host
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// Tokens x d bf16 row-major (leading dimension ld elements): boxes of 64 columns x 64 tokens, 128-byte swizzle.
+int make_map(CUtensorMap *m, const void *base, int64_t tokens, int d, int64_t ld, const char *who) {
+    EncodeTiled enc = encode_fn();
+    if (enc == nullptr) {
+        set_error("%s: cuTensorMapEncodeTiled is unavailable", who);
+        return LAMQ_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)tokens};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)BK};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("%s: cuTensorMapEncodeTiled failed (%d)", who, (int)r);
+        return LAMQ_ERR_INVALID;
+    }
+    return LAMQ_OK;
+}
+
+int num_sms() {
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+}  // namespace
+
+}  // namespace lamq
+
+using namespace lamq;
+
+extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb, int64_t tokens,
+                                   int d, int symmetric, float *acc, int64_t ldacc, int64_t chunk_tokens, int *status,
+                                   lamq_stream_t stream) {
+    LAMQ_REQUIRE(tokens >= 0 && d > 0, "lamq_xtx_accumulate: bad shape");
+    if (tokens == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(A && B && acc && status, "lamq_xtx_accumulate: null pointer");
+    LAMQ_REQUIRE(d % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && lda >= d && ldb >= d,
+                 "lamq_xtx_accumulate: d and leading dimensions must be multiples of 8 (16-byte rows for TMA)");
+    LAMQ_REQUIRE(((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0, "lamq_xtx_accumulate: operands not 16-byte aligned");
+    LAMQ_REQUIRE(ldacc >= d, "lamq_xtx_accumulate: accumulator leading dimension below d");
+    LAMQ_REQUIRE(chunk_tokens >= BK && chunk_tokens % BK == 0, "lamq_xtx_accumulate: chunk_tokens must be a multiple of 64");
+    CUtensorMap ma, mb;
+    int st = make_map(&ma, A, tokens, d, lda, "lamq_xtx_accumulate");
+    if (st != LAMQ_OK) return st;
+    st = make_map(&mb, B, tokens, d, ldb, "lamq_xtx_accumulate");
+    if (st != LAMQ_OK) return st;
+    GemmParams p{};
+    p.acc = acc;
+    p.ldc = ldacc;
+    p.d = d;
+    p.ntile = (d + BM - 1) / BM;
+    p.ngroup = (p.ntile + SB - 1) / SB;
+    p.kblocks = (int)((tokens + BK - 1) / BK);
+    p.kblocks_per_chunk = (int)(chunk_tokens / BK);
+    p.nchunk = (p.kblocks + p.kblocks_per_chunk - 1) / p.kblocks_per_chunk;
+    p.symmetric = symmetric ? 1 : 0;
+    p.status = status;
+    const int64_t tiles = symmetric ? (int64_t)p.ntile * (p.ntile + 1) / 2 : (int64_t)p.ntile * p.ntile;
+    p.units = tiles * p.nchunk;
+    cudaError_t e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) {
+        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    const int64_t grid = p.units < num_sms() ? p.units : num_sms();
+    xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
+    LAMQ_CHECK_LAUNCH("lamq_xtx_accumulate");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_weighted_split(const uint16_t *scaled, int64_t lds, const uint16_t *plain, int64_t ldp,
+                                   const float *w, const int32_t *idx, int64_t nw, int d, uint16_t *out_split,
+                                   uint16_t *out_plain, lamq_stream_t stream) {
+    LAMQ_REQUIRE(nw >= 0 && d > 0, "lamq_weighted_split: bad shape");
+    if (nw == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(scaled && plain && w && idx && out_split && out_plain, "lamq_weighted_split: null pointer");
+    weighted_split_kernel<<<(unsigned)nw, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const __nv_bfloat16 *>(scaled), lds, reinterpret_cast<const __nv_bfloat16 *>(plain), ldp, w,
+        idx, nw, d, reinterpret_cast<__nv_bfloat16 *>(out_split), reinterpret_cast<__nv_bfloat16 *>(out_plain));
+    LAMQ_CHECK_LAUNCH("lamq_weighted_split");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_hessian_finalize(const float *accH, const float *accD, int d, int64_t ld, double n_tok, double *H,
+                                     double *D, lamq_stream_t stream) {
+    LAMQ_REQUIRE(d > 0 && ld >= d && n_tok > 0, "lamq_hessian_finalize: bad shape");
+    LAMQ_REQUIRE(accH && H && (accD == nullptr) == (D == nullptr), "lamq_hessian_finalize: null pointer");
+    const int64_t n = (int64_t)d * d;
+    const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    finalize_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(accH, accD, ld, d, 1.0 / n_tok, H, D);
+    LAMQ_CHECK_LAUNCH("lamq_hessian_finalize");
+    return LAMQ_OK;
+}

@@ -1,0 +1,114 @@
+"""Input statistics on B200: the token-weighted Hessian H and the QEP cross moment D.
+
+Reference: quantize.py:1412-1470 (inside `quantize_stage`): for every calibration chunk of activations X (the
+quantized stream) and X_ref (the reference stream), with per-token weights w of mean 1,
+
+    H += Xᵀ (w ⊙ X),   D += X_refᵀ (w ⊙ X),   n_tok += tokens        (fp32, on the GPU)
+    H = H / n_tok (fp64),   D = D / n_tok − H (fp64)
+
+and compiler.py:233-265 (`capture`), the unweighted H of the `measure` sweep. Here the contraction runs in the
+tcgen05 kernel of liblamq_b200.so (bf16 activations, fp32 accumulation); `Statistics` keeps the fp32 accumulators
+across chunks (and across ranks: the accumulators are what an all-reduce sums) and `finalize` produces the fp64
+H and D.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+
+CHUNK_TOKENS = 32768  # tokens accumulated on chip before each flush into the fp32 accumulator
+
+
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    if x.dtype != torch.bfloat16:
+        raise TypeError("activations must be bf16 (the model's dtype); got " + str(x.dtype))
+    if not x.is_cuda:
+        raise RuntimeError("activations must be on a CUDA device")
+    x = x.reshape(-1, x.shape[-1])
+    if x.stride(-1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    return x
+
+
+class Statistics:
+    """fp32 accumulators of one stage's H (and D with a reference stream), fed chunk by chunk."""
+
+    def __init__(self, d: int, cross: bool = False, device=None, chunk_tokens: int = CHUNK_TOKENS):
+        dev = torch.device(device or "cuda")
+        self.d, self.device, self.chunk_tokens = d, dev, chunk_tokens
+        self.accH = torch.zeros(d, d, dtype=torch.float32, device=dev)
+        self.accD = torch.zeros(d, d, dtype=torch.float32, device=dev) if cross else None
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.n_tok = 0
+
+    def _xtx(self, A, B, symmetric, acc, tokens):
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            check(lib.lamq_xtx_accumulate(ptr(A), A.stride(0), ptr(B), B.stride(0), tokens, self.d,
+                                          1 if symmetric else 0, ptr(acc), acc.stride(0), self.chunk_tokens,
+                                          ptr(self.status), stream_ptr(self.device)), "lamq_xtx_accumulate")
+
+    def add(self, x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor | None = None):
+        """One calibration chunk: x (tokens × d bf16, the stream the matrix will see), its token weights w (fp32, or
+        None for 1) and, for D, x_ref (the reference stream at the same tokens)."""
+        x = _bf16(x)
+        tokens = x.shape[0]
+        if x.shape[1] != self.d:
+            raise ValueError(f"activations have {x.shape[1]} features, expected {self.d}")
+        if (x_ref is not None) != (self.accD is not None):
+            raise ValueError("x_ref is required exactly when the statistics include D")
+        xr = None if x_ref is None else _bf16(x_ref)
+        self._xtx(x, x, True, self.accH, tokens)
+        if xr is not None:
+            self._xtx(x, xr, False, self.accD, tokens)
+        if w is not None:
+            w = w.reshape(-1).to(self.device, torch.float32).contiguous()
+            if w.numel() != tokens:
+                raise ValueError("one weight per token")
+            idx = torch.nonzero(w != 1.0).flatten().to(torch.int32)
+            nw = int(idx.numel())
+            if nw:
+                lib = _lib.load()
+                split = torch.empty(2 * nw, self.d, dtype=torch.bfloat16, device=self.device)
+                plain = torch.empty_like(split)
+                with torch.cuda.device(self.device):
+                    check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(x), x.stride(0), ptr(w), ptr(idx), nw,
+                                                  self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
+                          "lamq_weighted_split")
+                # Σ (w−1)·x xᵀ: A = x (plain), B = (w−1)·x (hi and lo rows)
+                self._xtx(plain, split, True, self.accH, 2 * nw)
+                if xr is not None:
+                    with torch.cuda.device(self.device):
+                        check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(xr), xr.stride(0), ptr(w), ptr(idx),
+                                                      nw, self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
+                              "lamq_weighted_split")
+                    # D[j][i] += Σ (w−1)·x[i]·x_ref[j]: A = (w−1)·x (hi and lo), B = x_ref
+                    self._xtx(split, plain, False, self.accD, 2 * nw)
+        self.n_tok += tokens
+        return self
+
+    def finalize(self, n_tok: int | None = None):
+        """(H, D) in fp64: H = acc/n_tok (mirrored from the computed triangle), D = accD/n_tok − H (or None)."""
+        n = self.n_tok if n_tok is None else n_tok
+        H = torch.empty(self.d, self.d, dtype=torch.float64, device=self.device)
+        D = torch.empty_like(H) if self.accD is not None else None
+        with torch.cuda.device(self.device):
+            check(_lib.load().lamq_hessian_finalize(ptr(self.accH), ptr(self.accD), self.d, self.d, float(n), ptr(H),
+                                                    ptr(D), stream_ptr(self.device)), "lamq_hessian_finalize")
+        return H, D
+
+    def check_status(self):
+        st = int(self.status.item())
+        if st:
+            _lib.check(st, "Hessian accumulation")
+
+
+def hessian(x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor | None = None,
+            chunk_tokens: int = CHUNK_TOKENS):
+    """One-shot H (and D with x_ref) of bf16 activations x (tokens × d) with token weights w."""
+    st = Statistics(x.shape[-1], cross=x_ref is not None, device=x.device, chunk_tokens=chunk_tokens)
+    st.add(x, w, x_ref)
+    return st.finalize()

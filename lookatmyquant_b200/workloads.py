@@ -40,3 +40,21 @@ def config1():
     H = X.T @ X / 16384
     seed, in_seed = seeds_for(0, "mlp.gate_proj", 0)
     return W, H, seed, in_seed
+
+
+def activations_bf16(tokens: int, d: int, seed: int, device="cuda") -> torch.Tensor:
+    """Config-2-style activations generated on the device: Gaussian with lognormal(0, 1) per-channel scale, bf16."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    std = torch.exp(torch.randn(d, generator=g, device=device))
+    out = torch.empty(tokens, d, dtype=torch.bfloat16, device=device)
+    step = max(1, (1 << 28) // (4 * d))
+    for a in range(0, tokens, step):
+        b = min(tokens, a + step)
+        out[a:b] = (torch.randn(b - a, d, generator=g, device=device) * std).to(torch.bfloat16)
+    return out
+
+
+def token_weights(tokens: int, seed: int, p: float = 0.08, big: float = 10.0, device="cuda") -> torch.Tensor:
+    """Config 2's token weights: `big` on a Bernoulli(p) mask of tokens, 1 elsewhere (fp32)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.where(torch.rand(tokens, generator=g, device=device) < p, big, 1.0).float()
