@@ -13,6 +13,8 @@
  *   lamq_xtx_accumulate,   quantize.py:1412-1470      H += Xᵀ(w⊙X), D += X_refᵀ(w⊙X) per calibration chunk, then
  *   lamq_weighted_split,                              H/n_tok and D/n_tok − H in fp64 (inline in quantize_stage);
  *   lamq_hessian_finalize  compiler.py:233-265        the unweighted H of `capture`
+ *   lamq_rht_rows,         opgraph/codes.py:97-132    rht(n, seed) applied as X = W·R_inᵀ (:430), Hr = R_in·H·R_inᵀ
+ *   lamq_transpose_f64                                (:439) and W_q = (S⊙V)·R_in, without forming R
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -118,6 +120,21 @@ int lamq_weighted_split(const uint16_t *scaled, int64_t lds, const uint16_t *pla
 /* H[r][c] = accH[max(r,c)][min(r,c)] / n_tok (fp64, symmetric); with accD, D = accD / n_tok − H. d x d outputs. */
 int lamq_hessian_finalize(const float *accH, const float *accD, int d, int64_t ld, double n_tok, double *H, double *D,
                           lamq_stream_t stream);
+
+/*
+ * Randomized Hadamard transform of each row (opgraph/codes.py:97-132, applied at codes.py:430,439): for every row v
+ * of `in` (rows x n, n = a·b), out = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)), with Ae (a x a) and Be (b x b) ±1
+ * matrices given as row-wise sign bits (abits: a x ceil(a/32) words, bit k of word w of row p set when
+ * Ae[p][32w + k] = -1; bbits likewise) and pre/post sign vectors of length n (or NULL). R = (A⊗B)/√n·diag(s) is
+ * Ae = A, Be = B, pre = s, scale = 1/√n; Rᵀ is Ae = Aᵀ, Be = Bᵀ, post = s. in may equal out. Orders a, b <= 256.
+ */
+int lamq_rht_rows(const double *in, int64_t ldi, double *out, int64_t ldo, int64_t rows, int a, int b,
+                  const uint32_t *abits, const uint32_t *bbits, const double *pre, const double *post, double scale,
+                  lamq_stream_t stream);
+
+/* out (cols x rows) = transpose of in (rows x cols), fp64; in and out must not alias. */
+int lamq_transpose_f64(const double *in, int64_t ldi, double *out, int64_t ldo, int rows, int cols,
+                       lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

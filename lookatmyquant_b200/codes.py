@@ -26,6 +26,7 @@ import torch
 from . import _lib
 from ._lib import check, ptr, stream_ptr
 from .frame import Environment
+from .rotation import Rotation
 
 TABLES = Path(__file__).resolve().parent / "tables"
 DEVICE = "cuda"
@@ -188,7 +189,8 @@ class TrellisCode:
 
 class TrellisWord:
     """One matrix's trellis word: W ≈ R_outᵀ·diag(S)·V[states]·R_in. The fields are device tensors:
-    `states` (rows × n int16), `scales` S (rows fp64), `settled` V[states] (fp64, units of S)."""
+    `states` (rows × n int16), `scales` S (rows fp64), `settled` V[states] (fp64, units of S); the rotations are
+    `Rotation`s (None: no rotation on that side)."""
 
     def __init__(self, states, scales, settled, values, L, k, in_seed, R_in, R_out=None, fixed_start=True, T=None):
         self.states, self.scales, self.settled, self.values = states, scales, settled, values
@@ -196,17 +198,19 @@ class TrellisWord:
         self.fixed_start, self.T = fixed_start, T
 
     def matrix(self, device=None, dtype=torch.float64) -> torch.Tensor:
-        """The dequantized matrix (reference Net.matrix, frame.py:112-134)."""
-        W = (self.settled * self.scales[:, None]) @ self.R_in
+        """The dequantized matrix (reference Net.matrix, frame.py:112-134): diag(S)·V[states]·R_in, then R_outᵀ·."""
+        W = self.settled * self.scales[:, None]
+        if self.R_in is not None:
+            W = self.R_in.rows_t(W)
         if self.R_out is not None:
-            W = self.R_out.T @ W
+            W = self.R_out.rows_t(W.T.contiguous()).T.contiguous()
         return W.to(device=device or W.device, dtype=dtype)
 
     def rate_bits(self) -> float:
         """Stored bits (frame.py:137-147): k per entry, plus L − k per sequence without a fixed start, 16 per row
         scale, one sign per input (and per output with an output rotation)."""
         m, n = self.states.shape
-        bits = float(m * n * self.k) + 16.0 * m + n + (m if self.R_out is not None else 0)
+        bits = float(m * n * self.k) + 16.0 * m + (n if self.R_in is not None else 0) + (m if self.R_out is not None else 0)
         if not self.fixed_start:
             bits += (m * n / self.T) * (self.L - self.k)
         return bits
@@ -244,22 +248,24 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
     dev = _dev(device)
     Ws = [W.to(dev, torch.float64) for W in Ws]
     n = Ws[0].shape[1]
-    R_in = rht(n, seeds[0] + 1 if in_seed is None else in_seed).to(dev) if incoherent else None
+    R_in = Rotation(n, seeds[0] + 1 if in_seed is None else in_seed, dev) if incoherent else None
     Xs, R_outs = [], []
     for W, s in zip(Ws, seeds):
+        X = R_in.rows(W) if incoherent else W
         if incoherent and out_rot:
-            R_out = rht(W.shape[0], s).to(dev)
-            Xs.append(R_out @ W @ R_in.T)
+            R_out = Rotation(W.shape[0], s, dev)
+            X = R_out.rows(X.T.contiguous()).T.contiguous()  # R_out·(W·R_inᵀ)
             R_outs.append(R_out)
         else:
-            Xs.append(W @ R_in.T if incoherent else W)
             R_outs.append(None)
-    X = torch.cat(Xs)
+        Xs.append(X)
+    X = torch.cat(Xs) if len(Xs) > 1 else Xs[0]
     S = X.pow(2).mean(1).sqrt().clamp(min=1e-12)
     if isinstance(code, RowTrellisCode):
         if H is None:
             raise NotImplementedError("row-trellis words without H (plain Viterbi per row) are not wired yet")
-        Hr = (R_in @ H.to(dev, torch.float64) @ R_in.T) if incoherent else H.to(dev, torch.float64)
+        Hd = H.to(dev, torch.float64)
+        Hr = R_in.conj(Hd) if incoherent else Hd
         env = Environment(Hr)
         _, states, settled = _row_trellis_sweep(X, S, env, code)
         fixed, T = True, None
@@ -267,11 +273,10 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
         raise NotImplementedError("the column-trellis sweep is not wired yet")
     else:
         raise TypeError(f"unsupported code {type(code).__name__}")
-    eye = torch.eye(n, dtype=torch.float64, device=dev)
     out, r0 = [], 0
     for W, R_out in zip(Ws, R_outs):
         r1 = r0 + W.shape[0]
         out.append(TrellisWord(states[r0:r1], S[r0:r1], settled[r0:r1], code.values, code.L, code.k,
-                               in_seed, R_in if R_in is not None else eye, R_out, fixed, T))
+                               in_seed, R_in, R_out, fixed, T))
         r0 = r1
     return out

@@ -1,0 +1,210 @@
+// Randomized Hadamard transforms applied through their Kronecker factors, in fp64.
+//
+// Reference: opgraph/codes.py:97-132 builds R = hadamard(n)·diag(s) = (A ⊗ B)/√n·diag(s) as a dense n × n matrix
+// (A Sylvester, B Sylvester or Paley, entries ±1) and applies it with dense products: X = W·R_inᵀ (codes.py:430),
+// Hr = R_in·H·R_inᵀ (codes.py:439), W_q = (S ⊙ V)·R_in (frame.py Net.matrix). Here a row v of length n = a·b, viewed
+// as an a × b matrix V, is transformed as (A ⊗ B)·vec(V) = vec(A·V·Bᵀ): b² + a² signed additions per a·b entries
+// instead of n² multiply-adds (9728 = 64 · 152: 216 per entry instead of 9728).
+//
+// One CTA transforms one row in shared memory, in place: phase 1 (one warp per row p of V) forms Z = V·Beᵀ, phase 2
+// (one warp per column q) forms Y = Ae·Z; each lane keeps the sign bits of the factor rows it produces in registers.
+// The general form computed is y = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)), so R (Ae = A, Be = B, pre = s) and Rᵀ
+// (Ae = Aᵀ, Be = Bᵀ, post = s) are both one pass.
+#include "lamq_common.cuh"
+
+namespace lamq {
+
+namespace {
+
+constexpr int kRhtThreads = 256;
+constexpr int kMaxFactor = 256;  // largest factor order supported (words of sign bits per factor row: 8)
+
+struct RhtParams {
+    const double *in;
+    int64_t ldi;
+    double *out;
+    int64_t ldo;
+    int64_t rows;
+    int a, b;
+    const uint32_t *abits;  // a x wa words: bit p' of row p set when Ae[p][p'] = -1
+    const uint32_t *bbits;  // b x wb words
+    int wa, wb;
+    const double *pre, *post;  // n signs or null
+    double scale;
+};
+
+// acc[c] (output index lane + 32c) += Σ_k sign(bits[c], k) · src[k·stride], k < len; bits[c][w] holds the signs of
+// k in [32w, 32w + 32) for the output this lane owns (bit set: negative).
+template <int NC>
+__device__ __forceinline__ void signed_sums(const double *__restrict__ src, int stride, int len,
+                                            const uint32_t (&bits)[NC][NC > 0 ? 8 : 8], double (&acc)[NC]) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        if (32 * w >= len) break;
+        uint32_t bw[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) bw[c] = bits[c][w];
+        const int lim = min(32, len - 32 * w);
+        if (lim == 32) {
+#pragma unroll
+            for (int bit = 0; bit < 32; ++bit) {
+                const long long v = __double_as_longlong(src[(32 * w + bit) * stride]);
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    acc[c] += __longlong_as_double(v ^ ((long long)((bw[c] >> bit) & 1u) << 63));
+            }
+        } else {
+            for (int bit = 0; bit < lim; ++bit) {
+                const long long v = __double_as_longlong(src[(32 * w + bit) * stride]);
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    acc[c] += __longlong_as_double(v ^ ((long long)((bw[c] >> bit) & 1u) << 63));
+            }
+        }
+    }
+}
+
+// NA = ceil(a/32), NB = ceil(b/32): output chunks per lane (and sign words per factor row) of the two phases.
+template <int NA, int NB>
+__global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
+    extern __shared__ __align__(16) double sv[];
+    const int n = p.a * p.b;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRhtThreads / 32;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const double *src = p.in + row * p.ldi;
+        for (int e = threadIdx.x; e < n; e += kRhtThreads) sv[e] = p.pre ? src[e] * p.pre[e] : src[e];
+        __syncthreads();
+        // phase 1: Z[pr][q] = Σ_q' Be[q][q'] · V[pr][q'], a warp per row pr of V, lanes over q
+        {
+            uint32_t bits[NB][8];
+#pragma unroll
+            for (int c = 0; c < NB; ++c) {
+                const int q = lane + 32 * c;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) bits[c][w] = (q < p.b && w < p.wb) ? __ldg(p.bbits + q * p.wb + w) : 0u;
+            }
+            for (int pr = warp; pr < p.a; pr += nwarps) {
+                double acc[NB];
+#pragma unroll
+                for (int c = 0; c < NB; ++c) acc[c] = 0.0;
+                signed_sums<NB>(sv + pr * p.b, 1, p.b, bits, acc);
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < NB; ++c) {
+                    const int q = lane + 32 * c;
+                    if (q < p.b) sv[pr * p.b + q] = acc[c];
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        // phase 2: Y[pr][q] = Σ_p' Ae[pr][p'] · Z[p'][q], a warp per column q, lanes over pr
+        {
+            uint32_t bits[NA][8];
+#pragma unroll
+            for (int c = 0; c < NA; ++c) {
+                const int pr = lane + 32 * c;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) bits[c][w] = (pr < p.a && w < p.wa) ? __ldg(p.abits + pr * p.wa + w) : 0u;
+            }
+            for (int q = warp; q < p.b; q += nwarps) {
+                double acc[NA];
+#pragma unroll
+                for (int c = 0; c < NA; ++c) acc[c] = 0.0;
+                signed_sums<NA>(sv + q, p.b, p.a, bits, acc);
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < NA; ++c) {
+                    const int pr = lane + 32 * c;
+                    if (pr < p.a) sv[pr * p.b + q] = acc[c];
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        double *dst = p.out + row * p.ldo;
+        for (int e = threadIdx.x; e < n; e += kRhtThreads) {
+            const double y = sv[e] * p.scale;
+            dst[e] = p.post ? y * p.post[e] : y;
+        }
+        __syncthreads();
+    }
+}
+
+constexpr int kTile = 32;
+
+__global__ void transpose_kernel(const double *__restrict__ in, int64_t ldi, double *__restrict__ out, int64_t ldo,
+                                 int rows, int cols) {
+    __shared__ double tile[kTile][kTile + 1];
+    const int bx = blockIdx.x * kTile, by = blockIdx.y * kTile;
+    for (int y = threadIdx.y; y < kTile; y += blockDim.y) {
+        const int r = by + y, c = bx + threadIdx.x;
+        if (r < rows && c < cols) tile[y][threadIdx.x] = in[(int64_t)r * ldi + c];
+    }
+    __syncthreads();
+    for (int y = threadIdx.y; y < kTile; y += blockDim.y) {
+        const int r = bx + y, c = by + threadIdx.x;
+        if (r < cols && c < rows) out[(int64_t)r * ldo + c] = tile[threadIdx.x][y];
+    }
+}
+
+template <int NA, int NB>
+int launch_rht(const RhtParams &p, cudaStream_t stream) {
+    const size_t smem = (size_t)p.a * p.b * sizeof(double);
+    cudaError_t e = cudaFuncSetAttribute(rht_rows_kernel<NA, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+        set_error("lamq_rht_rows: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t grid = p.rows < (int64_t)sms * 8 ? p.rows : (int64_t)sms * 8;
+    rht_rows_kernel<NA, NB><<<(unsigned)grid, kRhtThreads, smem, stream>>>(p);
+    LAMQ_CHECK_LAUNCH("lamq_rht_rows");
+    return LAMQ_OK;
+}
+
+}  // namespace
+
+}  // namespace lamq
+
+using namespace lamq;
+
+extern "C" int lamq_rht_rows(const double *in, int64_t ldi, double *out, int64_t ldo, int64_t rows, int a, int b,
+                             const uint32_t *abits, const uint32_t *bbits, const double *pre, const double *post,
+                             double scale, lamq_stream_t stream) {
+    LAMQ_REQUIRE(rows >= 0 && a >= 1 && b >= 1 && a <= kMaxFactor && b <= kMaxFactor,
+                 "lamq_rht_rows: factor orders must be 1..%d", kMaxFactor);
+    if (rows == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(in && out && abits && bbits, "lamq_rht_rows: null pointer");
+    LAMQ_REQUIRE(ldi >= (int64_t)a * b && ldo >= (int64_t)a * b, "lamq_rht_rows: leading dimension below n");
+    LAMQ_REQUIRE((size_t)a * b * sizeof(double) <= 200 * 1024, "lamq_rht_rows: n = %d too large for one CTA", a * b);
+    RhtParams p{in, ldi, out, ldo, rows, a, b, abits, bbits, (a + 31) / 32, (b + 31) / 32, pre, post, scale};
+    const int wa = p.wa, wb = p.wb;
+    cudaStream_t s = (cudaStream_t)stream;
+    // the output chunks per lane are template parameters so the sums and sign words stay in registers
+    const int na = wa <= 1 ? 1 : wa <= 2 ? 2 : wa <= 4 ? 4 : 8;
+    const int nb = wb;
+#define LAMQ_RHT_CASE(NA_, NB_) \
+    if (na == NA_ && nb == NB_) return launch_rht<NA_, NB_>(p, s);
+#define LAMQ_RHT_ROW(NA_) \
+    LAMQ_RHT_CASE(NA_, 1) LAMQ_RHT_CASE(NA_, 2) LAMQ_RHT_CASE(NA_, 3) LAMQ_RHT_CASE(NA_, 4) \
+    LAMQ_RHT_CASE(NA_, 5) LAMQ_RHT_CASE(NA_, 6) LAMQ_RHT_CASE(NA_, 7) LAMQ_RHT_CASE(NA_, 8)
+    LAMQ_RHT_ROW(1) LAMQ_RHT_ROW(2) LAMQ_RHT_ROW(4) LAMQ_RHT_ROW(8)
+#undef LAMQ_RHT_ROW
+#undef LAMQ_RHT_CASE
+    set_error("lamq_rht_rows: unsupported factor orders %d x %d", a, b);
+    return LAMQ_ERR_INVALID;
+}
+
+extern "C" int lamq_transpose_f64(const double *in, int64_t ldi, double *out, int64_t ldo, int rows, int cols,
+                                  lamq_stream_t stream) {
+    LAMQ_REQUIRE(rows >= 0 && cols >= 0, "lamq_transpose_f64: negative shape");
+    if (rows == 0 || cols == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(in && out && in != out, "lamq_transpose_f64: null or aliased pointer");
+    dim3 grid((cols + kTile - 1) / kTile, (rows + kTile - 1) / kTile), block(kTile, 8);
+    transpose_kernel<<<grid, block, 0, (cudaStream_t)stream>>>(in, ldi, out, ldo, rows, cols);
+    LAMQ_CHECK_LAUNCH("lamq_transpose_f64");
+    return LAMQ_OK;
+}

@@ -1,0 +1,152 @@
+"""Row-plan build of one decoder layer on B200: the lm2 build's per-layer work (quantize.py `quantize_stage`).
+
+Reference (ShinMegamiBoson/lookatmyquant), per stage of matrices that read one input (quantize.py:1404-1568):
+
+  1. H = Σ_t w_t x_t x_tᵀ / n_tok and the QEP moment D = Σ_t w_t x_ref,t x_tᵀ / n_tok − H  (:1412-1470)
+  2. M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ, target = W·M                              (:1330-1335, :1503)
+  3. per row group of the row plan, word('tr{b}x', target[rows], H, seed, in_seed, out_rot=False) (:530-565, :1531):
+     X = target·R_inᵀ, S = row RMS, Hr = R_in·H·R_inᵀ, U from Environment(Hr), the row-trellis LDLQ sweep
+     (codes.py:413-462), W_q = diag(S)·V[states]·R_in.
+
+Row groups are swept by one kernel for the whole stage (rows never interact under Refit; each row carries its own
+width k), the rotation is factored (rotation.py), H and D come from the tcgen05 kernel (hessian.py). With a process
+group, tokens are sharded for H and D (the fp32 accumulators are summed with one all-reduce per stage) and rows are
+sharded for the sweep (states and scales gathered at the end).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import codes
+from .codes import LAZY, stacked_tables
+from .frame import Environment
+from .hessian import Statistics
+from .rotation import Rotation
+
+ALPHA, LAM = 0.5, 0.1  # QEP strength of the lm2 build (--cross-alpha 0.5) and the ridge (quantize.py:93)
+
+
+@dataclass
+class StageSpec:
+    name: str
+    d: int
+    matrices: list  # (name, rows)
+    block: str      # "self_attn" or "mlp": the Hadamard seed block (compiler_arch.block_seed)
+
+
+def qwen3_4b_stages(hidden=2560, heads=32, kv_heads=8, head_dim=128, mlp=9728):
+    """The four stages of a Qwen3-4B-class decoder layer (quantize.py STAGES, :89-91)."""
+    return [StageSpec("attn_in", hidden, [("self_attn.q_proj", heads * head_dim), ("self_attn.k_proj", kv_heads * head_dim),
+                                          ("self_attn.v_proj", kv_heads * head_dim)], "self_attn"),
+            StageSpec("o_in", heads * head_dim, [("self_attn.o_proj", hidden)], "self_attn"),
+            StageSpec("mlp_in", hidden, [("mlp.gate_proj", mlp), ("mlp.up_proj", mlp)], "mlp"),
+            StageSpec("down_in", mlp, [("mlp.down_proj", hidden)], "mlp")]
+
+
+def row_plan(rows: int, seed: int, group: int = 64, widths=(1, 2, 3, 4), probs=(0.15, 0.45, 0.30, 0.10)) -> torch.Tensor:
+    """Per-row bit widths drawn per group of `group` rows (config 3's synthetic plan; rowgroup_alloc plans use runs of
+    64 rows)."""
+    g = torch.Generator().manual_seed(seed)
+    choice = torch.multinomial(torch.tensor(probs, dtype=torch.float64), (rows + group - 1) // group, replacement=True,
+                               generator=g)
+    return torch.tensor(widths, dtype=torch.uint8)[choice].repeat_interleave(group)[:rows]
+
+
+def cross_target(H: torch.Tensor, D: torch.Tensor, alpha: float = ALPHA, lam: float = LAM) -> torch.Tensor:
+    """M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ (quantize.py:1330-1335), fp64 on H's device."""
+    eye = torch.eye(len(H), dtype=H.dtype, device=H.device)
+    return eye + alpha * torch.linalg.solve(H + lam * torch.diag(H).mean() * eye, D.T).T
+
+
+@dataclass
+class StageResult:
+    states: dict = field(default_factory=dict)   # matrix name -> rows × n int16 (this rank's rows)
+    scales: dict = field(default_factory=dict)   # matrix name -> rows fp64
+    Wq: dict = field(default_factory=dict)       # matrix name -> rows × n fp64 (dequantized)
+    row_range: dict = field(default_factory=dict)
+
+
+def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Tensor, w: torch.Tensor | None,
+                bits: dict, layer: int = 0, group=None, dequantize: bool = True, tables=None,
+                n_tok_total: int | None = None) -> StageResult:
+    """One stage: statistics, QEP target, rotation, environment and the fused row-trellis sweep over every row of the
+    stage's matrices. `weights[name]` is rows × d (any float dtype, on the device), `bits[name]` the per-row widths.
+    With a process group, x/x_ref/w are this rank's token shard and each rank sweeps a contiguous share of rows."""
+    dev = x.device
+    world = group.size() if group is not None else 1
+    rank = group.rank() if group is not None else 0
+    st = Statistics(spec.d, cross=True, device=dev)
+    st.add(x, w, x_ref)
+    n_tok = st.n_tok
+    if group is not None:
+        torch.distributed.all_reduce(st.accH, group=group)
+        torch.distributed.all_reduce(st.accD, group=group)
+        n_tok = n_tok_total if n_tok_total is not None else n_tok * world
+    H, D = st.finalize(n_tok)
+    M = cross_target(H, D)
+    in_seed = 1000 * layer + 100 * {"self_attn": 2, "mlp": 3}[spec.block] + 1
+    rot = Rotation(spec.d, in_seed, dev)
+    env = Environment(rot.conj(H))
+    # all rows of the stage, this rank's contiguous share (whole 64-row groups)
+    names = [nm for nm, _ in spec.matrices]
+    total = sum(r for _, r in spec.matrices)
+    groups = (total + 63) // 64
+    g0, g1 = groups * rank // world, groups * (rank + 1) // world
+    r0, r1 = g0 * 64, min(total, g1 * 64)
+    Xs, ks, spans, off = [], [], {}, 0
+    for nm, rows in spec.matrices:
+        a, b = max(r0, off), min(r1, off + rows)
+        if a < b:
+            target = weights[nm][a - off:b - off].to(torch.float64) @ M
+            Xs.append(rot.rows(target))
+            ks.append(bits[nm][a - off:b - off])
+            spans[nm] = (a - off, b - off)
+        off += rows
+    res = StageResult(row_range=spans)
+    if not Xs:
+        return res
+    X = torch.cat(Xs) if len(Xs) > 1 else Xs[0]
+    row_bits = torch.cat(ks).to(dev, torch.uint8) if len(ks) > 1 else ks[0].to(dev, torch.uint8)
+    S = X.pow(2).mean(1).sqrt().clamp(min=1e-12)
+    states, settled = sweep_rows(X, S, env, row_bits, tables)
+    o = 0
+    for nm in names:
+        if nm not in spans:
+            continue
+        a, b = spans[nm]
+        res.states[nm] = states[o:o + b - a]
+        res.scales[nm] = S[o:o + b - a]
+        if dequantize:
+            res.Wq[nm] = rot.rows_t(settled[o:o + b - a] * S[o:o + b - a, None])
+        o += b - a
+    return res
+
+
+def sweep_rows(X, S, env, row_bits, tables=None):
+    """The fused row-trellis LDLQ sweep (lamq_ldlq_rowtrellis) with per-row widths; returns (states, settled)."""
+    from . import _lib
+    from ._lib import check, ptr, stream_ptr
+    dev = X.device
+    rows, n = X.shape
+    T = X.contiguous().clone()
+    states = torch.empty(rows, n, dtype=torch.int16, device=dev)
+    settled = torch.empty(rows, n, dtype=torch.float64, device=dev)
+    tables = stacked_tables(12, 256, dev) if tables is None else tables
+    dead = env.dead.to(dev, torch.uint8) if bool(env.dead.any()) else None
+    with torch.cuda.device(dev):
+        check(_lib.load().lamq_ldlq_rowtrellis(
+            ptr(T), n, rows, n, ptr(env.U), env.U.stride(0), ptr(dead), ptr(S.contiguous()), ptr(tables),
+            ptr(row_bits), 0, 12, codes.WIDTH, codes.LOOK, LAZY, ptr(states), ptr(settled), stream_ptr(dev)),
+            "lamq_ldlq_rowtrellis")
+    return states, settled
+
+
+def build_layer(stages, weights, acts, w, bits, layer: int = 0, group=None, dequantize: bool = True,
+                n_tok_total: int | None = None):
+    """All stages in order (true-sequential within the layer). `acts[stage] = (x, x_ref)`. Returns {stage: result}."""
+    tables = stacked_tables(12, 256, acts[stages[0].name][0].device)
+    return {s.name: build_stage(s, weights, *acts[s.name], w, bits, layer, group, dequantize, tables, n_tok_total)
+            for s in stages}
