@@ -72,7 +72,8 @@ int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *value
 
 /*
  * The block-LDLQ sweep with a row trellis as its projection (opgraph/syntax.py:86-124 with codes.py:397-404,442-450):
- * the lm2 build's per-matrix hot loop, fused into one kernel in which each row is settled by its own warp.
+ * the lm2 build's per-matrix hot loop, fused into one persistent kernel: tiles of 16 rows of one width per CTA, the
+ * trellis decode per warp, the end-of-run refit on fp64 tensor cores.
  *
  * T:        rows x n fp64 (ldT), in/out. On entry the targets in the rotated basis (X = W·R_inᵀ); columns flagged in
  *           `dead` are zeroed first (syntax.py:100-101). On exit each column as it stood just before it was settled —
@@ -86,12 +87,15 @@ int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *value
  *           width + look <= 32, lazy a multiple of width.
  * states:   rows x n int16 out (ldStates = n): the trellis states.
  * settled:  rows x n fp64 out or NULL: the settled table values, in units of the row scale.
- * Supported: L = 12.
+ * workspace: lamq_ldlq_rowtrellis_workspace_size(rows) bytes of device memory (the rows grouped by width into tiles
+ *           of 16, and a tile counter).
+ * Supported: L = 12; width + look <= 32; lazy <= 128 and a multiple of 4.
  */
+size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows);
 int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,
                          const uint8_t *dead, const double *S, const double *tables, const uint8_t *row_bits, int k_all,
-                         int L, int width, int look, int lazy, int16_t *states, double *settled,
-                         lamq_stream_t stream);
+                         int L, int width, int look, int lazy, int16_t *states, double *settled, void *workspace,
+                         size_t workspace_bytes, lamq_stream_t stream);
 
 /*
  * Tensor-core contraction over tokens: acc[j][i] += Σ_t A[t][i]·B[t][j] (bf16 in, fp32 accumulate) for i, j < d.

@@ -1,12 +1,20 @@
-// The block-LDLQ sweep with a row trellis (the lm2 build's per-matrix loop), fused into one kernel.
+// The block-LDLQ sweep with a row trellis (the lm2 build's per-matrix loop), fused into one persistent kernel.
 //
 // Reference: opgraph/syntax.py:86-124 (`sweep`), with the projection of opgraph/codes.py:442-450 and
-// RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so each row is settled
-// start to finish by one warp with no synchronisation beyond the warp: for every block of `width` columns the warp
-// decodes the block plus `look` columns ahead (in units of the row scale, from the row's previous state), settles the
-// block, solves z·U_BB = E and carries the error into the rest of the run; after each run of `lazy` columns it
-// carries the run's errors into all later columns. The look-ahead columns past a run's end are read before that
-// end-of-run update, exactly as the reference reads them (stale by design).
+// RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so rows are grouped by
+// their width k into tiles of 16 and each tile is swept start to finish by one CTA of 8 warps (2 rows per warp):
+//
+//   per run of `lazy` columns [b0, b1):
+//     the run's targets plus the `look` columns after it are copied from T into shared memory (Trun);
+//     per block of `width` columns, each warp, for each of its rows: decodes the block plus `look` columns ahead (in
+//       units of the row scale, from the row's last state; the look-ahead past b1 is stale by design, as in the
+//       reference), settles the block with the fp64 table values, writes the columns as they stood to T (what sweep
+//       returns), solves z·U_BB = E by substitution, keeps z in the block's Trun slots, and updates the rest of the
+//       run in shared memory (syntax.py:117-120);
+//     then the whole CTA applies the run to every later column, T[:, b1:] -= Z·U[b0:b1, b1:] (syntax.py:122-123), as
+//       an fp64 tensor-core GEMM (mma.sync m8n8k4 f64) over 16 rows, U staged through shared memory by cp.async so
+//       each U element crosses L2 once per 16 rows.
+// Tiles are taken from a work counter (persistent grid), so tiles of different widths and matrix sizes balance.
 #include <algorithm>
 
 #include "lamq_common.cuh"
@@ -16,109 +24,259 @@ namespace lamq {
 
 namespace {
 
-constexpr int kSweepWarps = 8;
+constexpr int kWarps = 8;
+constexpr int kRowsPerWarp = 2;
+constexpr int kTileRows = kWarps * kRowsPerWarp;  // 16
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxWin = 32;
+constexpr int kGemmCols = 64;                      // columns of U per GEMM stage (8 per warp)
+constexpr int kUStride = kGemmCols + 4;            // padded row of a staged U tile (conflict-free B fragments)
+constexpr int kMaxLazy = 128;
 
 struct SweepParams {
     double *T;
     int64_t ldT;
-    int64_t rows;
     int n;
+    const int32_t *rowlist;   // tiles of 16 row indices grouped by width, -1 = padding
+    const int *ntiles;        // device: number of tiles
+    int *counter;             // device: next tile to take
+    const uint8_t *row_bits;  // per-row width or null
+    int k_all;
     const double *U;
     int64_t ldU;
     const uint8_t *dead;
     const double *S;
     const double *tables;
-    const uint8_t *row_bits;
-    int k_all;
     int width, look, lazy;
+    int trun_stride;          // doubles per Trun row
     int16_t *states;
     double *settled;
 };
 
-__host__ __device__ constexpr size_t sweep_warp_smem(int win, int lazy) {
-    return 2 * 2048 * sizeof(float) + (size_t)win * 32 * sizeof(unsigned long long) + (size_t)lazy * sizeof(double);
+// Per-warp Viterbi scratch: two best buffers (2048 floats each, enough for k = 1) and 32 steps of back-pointers.
+constexpr size_t kWarpViterbiBytes = 2 * 2048 * sizeof(float) + kMaxWin * 32 * sizeof(unsigned long long);
+constexpr size_t kGemmBytes = 2 * (size_t)kMaxLazy * kUStride * sizeof(double);
+constexpr size_t kUnionBytes = (kWarps * kWarpViterbiBytes > kGemmBytes) ? kWarps * kWarpViterbiBytes : kGemmBytes;
+
+__device__ __forceinline__ void dmma_8x8x4(double &c0, double &c1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(c0), "+d"(c1)
+                 : "d"(a), "d"(b));
+}
+
+__device__ __forceinline__ void cp_async8(void *dst, const void *src, bool valid) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Stages U[b0 : b0+nr, c0 : c0+64] into Us (rows of kUStride doubles); columns at or past n read as zero.
+__device__ __forceinline__ void stage_u(double *Us, const SweepParams &p, int b0, int nr, int c0) {
+    for (int e = threadIdx.x; e < nr * kGemmCols; e += kThreads) {
+        const int i = e / kGemmCols, c = e % kGemmCols;
+        const bool ok = c0 + c < p.n;
+        cp_async8(Us + i * kUStride + c, p.U + (int64_t)(b0 + i) * p.ldU + (ok ? c0 + c : 0), ok);
+    }
+}
+
+// T[row][b1:] -= Z·U[b0:b1, b1:] for the tile's rows (Z in the Trun slots of the run's columns), fp64 tensor cores.
+__device__ void run_update(const SweepParams &p, double *Trun, const int *rows, double *gemm, int b0, int b1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nr = b1 - b0;  // a multiple of 4 (lazy is a multiple of width, runs before the last are full)
+    double *Us[2] = {gemm, gemm + (size_t)kMaxLazy * kUStride};
+    const int nchunks = (p.n - b1 + kGemmCols - 1) / kGemmCols;
+    stage_u(Us[0], p, b0, nr, b1);
+    cp_async_commit();
+    const int ar = lane >> 2, ak = lane & 3;  // A fragment: row ar, k ak; B fragment: k ak, column ar
+    const int r0 = rows[ar], r1 = rows[8 + ar];
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int c0 = b1 + ch * kGemmCols;
+        if (ch + 1 < nchunks) {
+            stage_u(Us[(ch + 1) & 1], p, b0, nr, c0 + kGemmCols);
+            cp_async_commit();
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const double *Ut = Us[ch & 1];
+        const int col = c0 + 8 * warp + 2 * ak;  // this thread's two output columns: col, col + 1
+        double c[2][2];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            const int r = mt ? r1 : r0;
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+                c[mt][e] = (r >= 0 && col + e < p.n) ? p.T[(int64_t)r * p.ldT + col + e] : 0.0;
+        }
+        const double *Ua = Ut + 8 * warp + ar;
+#pragma unroll 8
+        for (int ks = 0; ks < nr; ks += 4) {
+            const double b = Ua[(ks + ak) * kUStride];
+            const double a0 = -Trun[ar * p.trun_stride + ks + ak];
+            const double a1 = -Trun[(8 + ar) * p.trun_stride + ks + ak];
+            dmma_8x8x4(c[0][0], c[0][1], a0, b);
+            dmma_8x8x4(c[1][0], c[1][1], a1, b);
+        }
+        // D fragment: row ar (and 8 + ar), columns 2·ak, 2·ak + 1 of the warp's 8
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            const int r = mt ? r1 : r0;
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+                if (r >= 0 && col + e < p.n) p.T[(int64_t)r * p.ldT + col + e] = c[mt][e];
+        }
+        __syncthreads();  // the stage buffer is refilled two chunks later
+    }
 }
 
 template <int K>
-__device__ void sweep_row(const SweepParams &p, int64_t row, int lane, float *best0, float *best1,
-                          unsigned long long *args, double *Z) {
+__device__ void sweep_tile(const SweepParams &p, const int *rows, const double *rs, double *Trun, unsigned char *vregion,
+                           double *gemm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float cv[Trellis<K>::NB][Trellis<K>::RL];
     const double *tab = p.tables + (K - 1) * kStates;
     load_pred_values<K>(tab, lane, cv);
+    unsigned char *wv = vregion + (size_t)warp * kWarpViterbiBytes;
+    float *best0 = reinterpret_cast<float *>(wv);
+    float *best1 = best0 + 2048;
+    unsigned long long *args = reinterpret_cast<unsigned long long *>(best1 + 2048);
     const int n = p.n;
-    double *Trow = p.T + row * p.ldT;
-    const double s = p.S[row];
-    const double *U = p.U;
-    const int64_t ldU = p.ldU;
-    if (p.dead != nullptr)
-        for (int c = lane; c < n; c += 32)
-            if (p.dead[c]) Trow[c] = 0.0;
-    __syncwarp();
-    int state = 0;  // RowTrellisCode.step: every row's path starts at state 0 (codes.py:399-400)
+    int state[kRowsPerWarp] = {0, 0};  // every row's path starts at state 0 (codes.py:399-400)
     for (int b0 = 0; b0 < n; b0 += p.lazy) {
         const int b1 = min(b0 + p.lazy, n);
+        const int ncol = b1 - b0 + min(p.look, n - b1);
+        for (int e = threadIdx.x; e < kTileRows * ncol; e += kThreads) {
+            const int r = e / ncol, c = e % ncol;
+            Trun[r * p.trun_stride + c] = rows[r] >= 0 ? p.T[(int64_t)rows[r] * p.ldT + b0 + c] : 0.0;
+        }
+        __syncthreads();
         for (int j = b0; j < b1; j += p.width) {
             const int w = min(p.width, n - j);
             const int win = w + min(p.look, n - j - w);
-            const double tv = (lane < win) ? Trow[j + lane] : 0.0;
-            const float xv = __double2float_rn(__ddiv_rn(tv, s));  // (T / S).to(float32)
-            const int st = viterbi_window<K>(xv, win, true, state, cv, best0, best1, args, lane);
-            state = __shfl_sync(0xffffffffu, st, w - 1);
-            double e = 0.0;
-            if (lane < w) {
-                const double q = __ldg(tab + st);  // the fp64 table value (codes.py:404)
-                p.states[row * (int64_t)n + j + lane] = (int16_t)st;
-                if (p.settled != nullptr) p.settled[row * (int64_t)n + j + lane] = q;
-                e = __dsub_rn(tv, __dmul_rn(q, s));  // E = T - q·S (codes.py:449, syntax.py:115)
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+                const int r = warp * kRowsPerWarp + rr;
+                const int row = rows[r];
+                if (row < 0) continue;
+                double *tr = Trun + r * p.trun_stride;
+                const double s = rs[r];
+                const double tv = (lane < win) ? tr[j - b0 + lane] : 0.0;
+                const float xv = __double2float_rn(__ddiv_rn(tv, s));  // (T / S).to(float32)
+                const int st = viterbi_window<K>(xv, win, true, state[rr], cv, best0, best1, args, lane);
+                state[rr] = __shfl_sync(0xffffffffu, st, w - 1);
+                double e = 0.0;
+                if (lane < w) {
+                    const double q = __ldg(tab + st);  // the fp64 table value (codes.py:404)
+                    p.states[(int64_t)row * n + j + lane] = (int16_t)st;
+                    if (p.settled != nullptr) p.settled[(int64_t)row * n + j + lane] = q;
+                    p.T[(int64_t)row * p.ldT + j + lane] = tv;  // the column as it stood (sweep's return value)
+                    e = __dsub_rn(tv, __dmul_rn(q, s));        // E = T - q·S (codes.py:449, syntax.py:115)
+                }
+                // z·U_BB = E, U_BB upper triangular: column-by-column substitution (syntax.py:117)
+                double acc = e;
+                for (int i = 0; i < w; ++i) {
+                    const double zi =
+                        __ddiv_rn(__shfl_sync(0xffffffffu, acc, i), __ldg(p.U + (int64_t)(j + i) * p.ldU + j + i));
+                    if (lane > i && lane < w) acc = __dsub_rn(acc, __dmul_rn(zi, __ldg(p.U + (int64_t)(j + i) * p.ldU + j + lane)));
+                    if (lane == i) acc = zi;
+                }
+                __syncwarp();
+                if (lane < w) tr[j - b0 + lane] = acc;  // the block's slots now hold z
+                __syncwarp();
+                // the rest of the run: T[j+w : b1] -= z · U[block, j+w : b1] (syntax.py:118)
+                for (int c = j + w + lane; c < b1; c += 32) {
+                    double a = 0.0;
+                    for (int i = 0; i < w; ++i) a = fma(tr[j - b0 + i], __ldg(p.U + (int64_t)(j + i) * p.ldU + c), a);
+                    tr[c - b0] -= a;
+                }
+                __syncwarp();
             }
-            // z·U_BB = E, U_BB upper triangular: column-by-column substitution (syntax.py:117)
-            double acc = e;
-            for (int i = 0; i < w; ++i) {
-                const double zi = __ddiv_rn(__shfl_sync(0xffffffffu, acc, i), U[(int64_t)(j + i) * ldU + j + i]);
-                if (lane == i) Z[j - b0 + i] = zi;
-                if (lane > i && lane < w) acc = __dsub_rn(acc, __dmul_rn(zi, U[(int64_t)(j + i) * ldU + j + lane]));
-            }
-            __syncwarp();
-            // the rest of the run: T[j+w : b1] -= z · U[block, j+w : b1] (syntax.py:118)
-            for (int c = j + w + lane; c < b1; c += 32) {
-                double a = 0.0;
-                for (int i = 0; i < w; ++i) a = fma(Z[j - b0 + i], U[(int64_t)(j + i) * ldU + c], a);
-                Trow[c] -= a;
-            }
-            __syncwarp();
         }
-        if (b1 < n) {  // the columns after the run: T[b1:] -= Z · U[b0:b1, b1:] (syntax.py:122-123)
-            const int nr = b1 - b0;
-            for (int c = b1 + lane; c < n; c += 32) {
-                double a = 0.0;
-                for (int i = 0; i < nr; ++i) a = fma(Z[i], U[(int64_t)(b0 + i) * ldU + c], a);
-                Trow[c] -= a;
-            }
-            __syncwarp();
-        }
+        __syncthreads();
+        if (b1 < n) run_update(p, Trun, rows, gemm, b0, b1);
     }
 }
 
-__global__ void __launch_bounds__(kSweepWarps * 32, 1) sweep_rowtrellis_kernel(SweepParams p) {
+__global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * kSweepWarps + warp;
-    if (row >= p.rows) return;
-    const int win = p.width + p.look;
-    unsigned char *base = smem + (size_t)warp * sweep_warp_smem(win, p.lazy);
-    float *best0 = reinterpret_cast<float *>(base);
-    float *best1 = best0 + 2048;
-    unsigned long long *args = reinterpret_cast<unsigned long long *>(best1 + 2048);
-    double *Z = reinterpret_cast<double *>(args + win * 32);
-    const int k = p.row_bits != nullptr ? (int)p.row_bits[row] : p.k_all;
-    switch (k) {
-        case 1: sweep_row<1>(p, row, lane, best0, best1, args, Z); break;
-        case 2: sweep_row<2>(p, row, lane, best0, best1, args, Z); break;
-        case 3: sweep_row<3>(p, row, lane, best0, best1, args, Z); break;
-        case 4: sweep_row<4>(p, row, lane, best0, best1, args, Z); break;
-        default:  // an invalid width: mark the row's states invalid rather than guess
-            for (int c = lane; c < p.n; c += 32) p.states[row * (int64_t)p.n + c] = -1;
+    double *Trun = reinterpret_cast<double *>(smem);
+    unsigned char *uni = smem + (size_t)kTileRows * p.trun_stride * sizeof(double);
+    uni = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(uni) + 15) & ~uintptr_t(15));
+    __shared__ int rows[kTileRows];
+    __shared__ double rs[kTileRows];
+    __shared__ int tile_s, k_s;
+    const int ntiles = *p.ntiles;
+    for (;;) {
+        if (threadIdx.x == 0) tile_s = atomicAdd(p.counter, 1);
+        __syncthreads();
+        const int tile = tile_s;
+        if (tile >= ntiles) break;
+        if (threadIdx.x < kTileRows) {
+            const int row = p.rowlist[tile * kTileRows + threadIdx.x];
+            rows[threadIdx.x] = row;
+            rs[threadIdx.x] = row >= 0 ? p.S[row] : 1.0;
+            if (threadIdx.x == 0) k_s = p.row_bits ? (int)p.row_bits[row] : p.k_all;
+        }
+        __syncthreads();
+        // dead inputs: their targets start at zero (syntax.py:100-101)
+        if (p.dead != nullptr)
+            for (int e = threadIdx.x; e < kTileRows * p.n; e += kThreads) {
+                const int r = e / p.n, c = e % p.n;
+                if (rows[r] >= 0 && p.dead[c]) p.T[(int64_t)rows[r] * p.ldT + c] = 0.0;
+            }
+        __syncthreads();
+        switch (k_s) {
+            case 1: sweep_tile<1>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
+            case 2: sweep_tile<2>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
+            case 3: sweep_tile<3>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
+            default: sweep_tile<4>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
+        }
+        __syncthreads();
     }
+}
+
+// Groups rows by width into tiles of 16 (ascending row order inside each width, -1 padding) with one CTA.
+__global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_all, int32_t *rowlist, int *ntiles,
+                                  int *counter) {
+    __shared__ int base[5];
+    __shared__ int warp_sums[32];
+    int cursor = 0;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int k = 1; k <= 4; ++k) {
+        // ascending scan of rows with width k
+        int offset = 0;
+        for (int64_t a = 0; a < rows; a += nt) {
+            const int64_t r = a + tid;
+            const int kr = r < rows ? (row_bits ? (int)row_bits[r] : k_all) : 0;
+            const int flag = (kr == k) ? 1 : 0;
+            // block-wide exclusive scan of flag
+            const unsigned ballot = __ballot_sync(0xffffffffu, flag);
+            const int lane = tid & 31, wid = tid >> 5;
+            const int before_in_warp = __popc(ballot & ((1u << lane) - 1u));
+            if (lane == 0) warp_sums[wid] = __popc(ballot);
+            __syncthreads();
+            int before_warps = 0, total = 0;
+            for (int w = 0; w < nt / 32; ++w) {
+                if (w < wid) before_warps += warp_sums[w];
+                total += warp_sums[w];
+            }
+            if (flag) rowlist[cursor + offset + before_warps + before_in_warp] = (int32_t)r;
+            offset += total;
+            __syncthreads();
+        }
+        const int padded = (offset + kTileRows - 1) / kTileRows * kTileRows;
+        for (int i = offset + tid; i < padded; i += nt) rowlist[cursor + i] = -1;
+        cursor += padded;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        *ntiles = cursor / kTileRows;
+        *counter = 0;
+    }
+    (void)base;
 }
 
 }  // namespace
@@ -127,29 +285,51 @@ __global__ void __launch_bounds__(kSweepWarps * 32, 1) sweep_rowtrellis_kernel(S
 
 using namespace lamq;
 
+extern "C" size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows) {
+    if (rows <= 0) return 0;
+    return (size_t)(rows + 4 * kTileRows) * sizeof(int32_t) + 64;
+}
+
 extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,
                                     const uint8_t *dead, const double *S, const double *tables,
                                     const uint8_t *row_bits, int k_all, int L, int width, int look, int lazy,
-                                    int16_t *states, double *settled, lamq_stream_t stream) {
+                                    int16_t *states, double *settled, void *workspace, size_t workspace_bytes,
+                                    lamq_stream_t stream) {
     LAMQ_REQUIRE(L == kL, "lamq_ldlq_rowtrellis: only L = 12 is supported (got %d)", L);
     LAMQ_REQUIRE(rows >= 0 && n >= 0, "lamq_ldlq_rowtrellis: negative shape");
     if (rows == 0 || n == 0) return LAMQ_OK;
     LAMQ_REQUIRE(T && U && S && tables && states, "lamq_ldlq_rowtrellis: null pointer");
     LAMQ_REQUIRE(ldT >= n && ldU >= n, "lamq_ldlq_rowtrellis: leading dimension below n");
-    LAMQ_REQUIRE(width >= 1 && look >= 0 && width + look <= 32, "lamq_ldlq_rowtrellis: need width + look <= 32");
-    LAMQ_REQUIRE(lazy >= width && lazy % width == 0 && lazy <= 256,
-                 "lamq_ldlq_rowtrellis: lazy must be a multiple of width, at most 256");
+    LAMQ_REQUIRE(width >= 1 && look >= 0 && width + look <= kMaxWin, "lamq_ldlq_rowtrellis: need width + look <= 32");
+    LAMQ_REQUIRE(lazy >= width && lazy % width == 0 && lazy <= kMaxLazy && lazy % 4 == 0,
+                 "lamq_ldlq_rowtrellis: lazy must be a multiple of width and of 4, at most 128");
     LAMQ_REQUIRE(row_bits != nullptr || (k_all >= 1 && k_all <= 4), "lamq_ldlq_rowtrellis: k must be 1..4");
-    SweepParams p{T, ldT, rows, n, U, ldU, dead, S, tables, row_bits, k_all, width, look, lazy, states, settled};
-    const size_t smem = kSweepWarps * sweep_warp_smem(width + look, lazy);
+    const size_t need = lamq_ldlq_rowtrellis_workspace_size(rows);
+    LAMQ_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                 "lamq_ldlq_rowtrellis: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    int32_t *rowlist = reinterpret_cast<int32_t *>(workspace);
+    int *ntiles = reinterpret_cast<int *>(rowlist + rows + 4 * kTileRows);
+    int *counter = ntiles + 1;
+    group_rows_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(rows, row_bits, k_all, rowlist, ntiles, counter);
+    LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis (grouping)");
+    // Trun rows of lazy + look doubles, padded so 2·stride ≡ 24 (mod 32) banks: conflict-free A fragments
+    int ts = lazy + look;
+    while ((2 * ts) % 32 != 24) ++ts;
+    SweepParams p{T, ldT, n, rowlist, ntiles, counter, row_bits, k_all, U, ldU, dead, S, tables,
+                  width, look, lazy, ts, states, settled};
+    const size_t smem = (size_t)kTileRows * ts * sizeof(double) + 16 + kUnionBytes;
     cudaError_t e = cudaFuncSetAttribute(sweep_rowtrellis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) {
         set_error("lamq_ldlq_rowtrellis: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
     }
-    const int64_t grid = (rows + kSweepWarps - 1) / kSweepWarps;
-    sweep_rowtrellis_kernel<<<(unsigned)grid, kSweepWarps * 32, smem, (cudaStream_t)stream>>>(p);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t max_tiles = (rows + kTileRows - 1) / kTileRows + 4;
+    const int grid = (int)std::min<int64_t>(max_tiles, sms);
+    sweep_rowtrellis_kernel<<<grid, kThreads, smem, (cudaStream_t)stream>>>(p);
     LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis");
     return LAMQ_OK;
 }

@@ -39,7 +39,7 @@ def test_abi_version_and_errors_without_gpu(lib):
     assert st == _lib.LAMQ_ERR_INVALID
     assert b"L = 12" in lib.lamq_last_error()
     st = lib.lamq_ldlq_rowtrellis(None, 16, 4, 16, None, 16, None, None, None, None, 2, 12, 16, 20, 128,
-                                  None, None, None)
+                                  None, None, None, 0, None)
     assert st == _lib.LAMQ_ERR_INVALID
     assert lib.lamq_viterbi(None, 0, 8, None, 12, 2, None, None, None, 0, None) == _lib.LAMQ_OK  # empty input
 
