@@ -152,3 +152,32 @@ def build_layer(stages, weights, acts, w, bits, layer: int = 0, group=None, dequ
     tables = stacked_tables(12, 256, acts[stages[0].name][0].device)
     return {s.name: build_stage(s, weights, *acts[s.name], w, bits, layer, group, dequantize, tables, n_tok_total)
             for s in stages}
+
+
+def main():
+    """Builds one synthetic config-3 layer (the benchmark's workload) once and prints per-stage timings: the command
+    the per-kernel launch lists in profiles/ were captured with."""
+    import argparse
+    import json
+    import time
+    from .workloads import config3
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--tokens", type=int, default=384 * 2048)
+    ap.add_argument("--repeat", type=int, default=1)
+    a = ap.parse_args()
+    dev = torch.device("cuda")
+    stages, weights, acts, w, bits = config3(a.tokens, device=dev)
+    tables = stacked_tables(12, 256, dev)
+    for _ in range(a.repeat):
+        times = {}
+        for s in stages:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            build_stage(s, weights, *acts[s.name], w, bits, 0, None, True, tables)
+            torch.cuda.synchronize()
+            times[s.name] = round((time.perf_counter() - t0) * 1e3, 2)
+        print(json.dumps({"stage_ms": times, "total_ms": round(sum(times.values()), 2)}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
