@@ -180,9 +180,8 @@ class Config3:
         self.world = group.size() if group is not None else 1
         self.rank = group.rank() if group is not None else 0
         self.tokens = tokens
-        chunks = (tokens + 16383) // 16384
-        lo = (chunks * self.rank // self.world) * 16384
-        hi = min(tokens, (chunks * (self.rank + 1) // self.world) * 16384)
+        from lookatmyquant_b200.workloads import token_shard
+        lo, hi = token_shard(tokens, self.rank, self.world)
         self.lo, self.hi = lo, hi
         self.stages, self.weights, self.acts, self.w, self.bits = config3(tokens, device=device, lo=lo, hi=hi)
         self.m = sum(r for s in self.stages for _, r in s.matrices)
@@ -217,7 +216,8 @@ class Config3:
             buf = torch.zeros(cap, s.d, dtype=torch.int16, device=self.device)
             buf[:len(mine)] = mine
             allb = torch.empty(self.world * cap, s.d, dtype=torch.int16, device=self.device)
-            torch.distributed.all_gather_into_tensor(allb, buf, group=self.group)
+            # collectives have no int16 type: the shards travel as bytes
+            torch.distributed.all_gather_into_tensor(allb.view(torch.uint8), buf.view(torch.uint8), group=self.group)
 
     def e2e_step(self):
         """The build from host memory: every stage's weights and activations copied from pinned host buffers inside the

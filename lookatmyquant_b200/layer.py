@@ -55,6 +55,13 @@ def row_plan(rows: int, seed: int, group: int = 64, widths=(1, 2, 3, 4), probs=(
     return torch.tensor(widths, dtype=torch.uint8)[choice].repeat_interleave(group)[:rows]
 
 
+def row_shard(total: int, rank: int, world: int, group: int = 64) -> tuple[int, int]:
+    """Rows [r0, r1) of a stage that `rank` sweeps: whole runs of `group` rows, split as evenly as possible."""
+    groups = (total + group - 1) // group
+    g0, g1 = groups * rank // world, groups * (rank + 1) // world
+    return g0 * group, min(total, g1 * group)
+
+
 def cross_target(H: torch.Tensor, D: torch.Tensor, alpha: float = ALPHA, lam: float = LAM) -> torch.Tensor:
     """M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ (quantize.py:1330-1335), fp64 on H's device."""
     eye = torch.eye(len(H), dtype=H.dtype, device=H.device)
@@ -93,9 +100,7 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
     # all rows of the stage, this rank's contiguous share (whole 64-row groups)
     names = [nm for nm, _ in spec.matrices]
     total = sum(r for _, r in spec.matrices)
-    groups = (total + 63) // 64
-    g0, g1 = groups * rank // world, groups * (rank + 1) // world
-    r0, r1 = g0 * 64, min(total, g1 * 64)
+    r0, r1 = row_shard(total, rank, world)
     Xs, ks, spans, off = [], [], {}, 0
     for nm, rows in spec.matrices:
         a, b = max(r0, off), min(r1, off + rows)

@@ -63,6 +63,12 @@ def token_weights(tokens: int, seed: int, p: float = 0.08, big: float = 10.0, de
 ACT_CHUNK = 16384  # activations are generated in fixed chunks of tokens, so any token shard matches the whole
 
 
+def token_shard(tokens: int, rank: int, world: int, chunk: int = ACT_CHUNK) -> tuple[int, int]:
+    """Tokens [lo, hi) of `rank`: whole generation chunks, split as evenly as possible."""
+    chunks = (tokens + chunk - 1) // chunk
+    return chunk * (chunks * rank // world), min(tokens, chunk * (chunks * (rank + 1) // world))
+
+
 def stage_activations(tokens: int, d: int, seed: int, device="cuda", lo: int = 0, hi: int | None = None,
                       ref_noise: float = 0.02):
     """(x, x_ref) for tokens [lo, hi) of a stage: x Gaussian with lognormal(0, 1) channel scales (bf16), x_ref = x plus
