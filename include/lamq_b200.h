@@ -15,6 +15,9 @@
  *   lamq_hessian_finalize  compiler.py:233-265        the unweighted H of `capture`
  *   lamq_rht_rows,         opgraph/codes.py:97-132    rht(n, seed) applied as X = W·R_inᵀ (:430), Hr = R_in·H·R_inᵀ
  *   lamq_transpose_f64                                (:439) and W_q = (S⊙V)·R_in, without forming R
+ *   lamq_env_factor        opgraph/frame.py:515-522   Environment(H, damp): dead inputs, damping, U
+ *   lamq_cholesky_inverse_lower, lamq_ridge, lamq_dgemm
+ *                          quantize.py:1330-1335      cross_target: M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -139,6 +142,34 @@ int lamq_rht_rows(const double *in, int64_t ldi, double *out, int64_t ldo, int64
 /* out (cols x rows) = transpose of in (rows x cols), fp64; in and out must not alias. */
 int lamq_transpose_f64(const double *in, int64_t ldi, double *out, int64_t ldo, int rows, int cols,
                        lamq_stream_t stream);
+
+/*
+ * fp64 on the tensor cores. C = α·A·B + β·C (transB = 0, B is K x N) or C = α·A·Bᵀ + β·C (transB = 1, B is N x K),
+ * row-major.
+ */
+int lamq_dgemm(int transB, int M, int N, int K, double alpha, const double *A, int64_t lda, const double *B,
+               int64_t ldb, double beta, double *C, int64_t ldc, lamq_stream_t stream);
+
+/* Workspace bytes for lamq_env_factor and lamq_cholesky_inverse_lower of order n. */
+size_t lamq_factor_workspace_size(int n);
+
+/*
+ * A (n x n, symmetric positive definite, lower part read) is replaced by L⁻¹, L the lower Cholesky factor (strict
+ * upper part zero). status (device int, 0 on entry) becomes LAMQ_ERR_NOT_PD on a non-positive pivot.
+ */
+int lamq_cholesky_inverse_lower(double *A, int64_t lda, int n, void *workspace, size_t workspace_bytes, int *status,
+                                lamq_stream_t stream);
+
+/*
+ * Environment (opgraph/frame.py:515-522): dead inputs (zero diagonal) get a unit diagonal and are flagged in `dead`
+ * (n bytes, or NULL), H += damp·mean(diag H)·I, and U (n x n, upper) = the upper Cholesky factor of H⁻¹, computed as
+ * J·chol(J·H·J)⁻¹·J. H is not modified. status as for lamq_cholesky_inverse_lower.
+ */
+int lamq_env_factor(const double *H, int64_t ldh, int n, double damp, double *U, int64_t ldu, uint8_t *dead,
+                    void *workspace, size_t workspace_bytes, int *status, lamq_stream_t stream);
+
+/* A = H + lam·mean(diag H)·I (quantize.py:1334). */
+int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, int n, double lam, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -32,6 +32,11 @@ SIGNATURES = {
     "lamq_hessian_finalize": (_I32, [_P, _P, _I32, _I64, _D, _P, _P, _P]),
     "lamq_rht_rows": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _P, _P, _P, _D, _P]),
     "lamq_transpose_f64": (_I32, [_P, _I64, _P, _I64, _I32, _I32, _P]),
+    "lamq_dgemm": (_I32, [_I32, _I32, _I32, _I32, _D, _P, _I64, _P, _I64, _D, _P, _I64, _P]),
+    "lamq_factor_workspace_size": (_SZ, [_I32]),
+    "lamq_cholesky_inverse_lower": (_I32, [_P, _I64, _I32, _P, _SZ, _P, _P]),
+    "lamq_env_factor": (_I32, [_P, _I64, _I32, _D, _P, _I64, _P, _P, _SZ, _P, _P]),
+    "lamq_ridge": (_I32, [_P, _I64, _P, _I64, _I32, _D, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),

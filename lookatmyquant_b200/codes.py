@@ -269,6 +269,7 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
         Hr = R_in.conj(Hd) if incoherent else Hd
         env = Environment(Hr)
         _, states, settled = _row_trellis_sweep(X, S, env, code)
+        env.check()
         fixed, T = True, None
     elif isinstance(code, TrellisCode):
         raise NotImplementedError("the column-trellis sweep is not wired yet")

@@ -24,6 +24,7 @@ from . import codes
 from .codes import LAZY, stacked_tables
 from .frame import Environment
 from .hessian import Statistics
+from .linalg import CrossTarget
 from .rotation import Rotation
 
 ALPHA, LAM = 0.5, 0.1  # QEP strength of the lm2 build (--cross-alpha 0.5) and the ridge (quantize.py:93)
@@ -55,6 +56,15 @@ def row_plan(rows: int, seed: int, group: int = 64, widths=(1, 2, 3, 4), probs=(
     return torch.tensor(widths, dtype=torch.uint8)[choice].repeat_interleave(group)[:rows]
 
 
+_SIDE = {}
+
+
+def _side_stream(dev) -> torch.cuda.Stream:
+    if dev not in _SIDE:
+        _SIDE[dev] = torch.cuda.Stream(device=dev)
+    return _SIDE[dev]
+
+
 def row_shard(total: int, rank: int, world: int, group: int = 64) -> tuple[int, int]:
     """Rows [r0, r1) of a stage that `rank` sweeps: whole runs of `group` rows, split as evenly as possible."""
     groups = (total + group - 1) // group
@@ -63,9 +73,8 @@ def row_shard(total: int, rank: int, world: int, group: int = 64) -> tuple[int, 
 
 
 def cross_target(H: torch.Tensor, D: torch.Tensor, alpha: float = ALPHA, lam: float = LAM) -> torch.Tensor:
-    """M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ (quantize.py:1330-1335), fp64 on H's device."""
-    eye = torch.eye(len(H), dtype=H.dtype, device=H.device)
-    return eye + alpha * torch.linalg.solve(H + lam * torch.diag(H).mean() * eye, D.T).T
+    """M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ (quantize.py:1330-1335), fp64 on H's device (tensor cores)."""
+    return CrossTarget(H, D, alpha, lam).M
 
 
 @dataclass
@@ -93,19 +102,27 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
         torch.distributed.all_reduce(st.accD, group=group)
         n_tok = n_tok_total if n_tok_total is not None else n_tok * world
     H, D = st.finalize(n_tok)
-    M = cross_target(H, D)
     in_seed = 1000 * layer + 100 * {"self_attn": 2, "mlp": 3}[spec.block] + 1
-    rot = Rotation(spec.d, in_seed, dev)
-    env = Environment(rot.conj(H))
     # all rows of the stage, this rank's contiguous share (whole 64-row groups)
     names = [nm for nm, _ in spec.matrices]
     total = sum(r for _, r in spec.matrices)
     r0, r1 = row_shard(total, rank, world)
+    # the QEP map (a factorization of H + λμI) and the environment (a factorization of R·H·Rᵀ) are independent:
+    # the first runs on a side stream while the second runs on the main one
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0)
+    rot = Rotation(spec.d, in_seed, dev)
+    env = Environment(rot.conj(H))
+    main.wait_stream(side)
+    qep.record_stream(main)
     Xs, ks, spans, off = [], [], {}, 0
     for nm, rows in spec.matrices:
         a, b = max(r0, off), min(r1, off + rows)
         if a < b:
-            target = weights[nm][a - off:b - off].to(torch.float64) @ M
+            target = qep.apply(weights[nm][a - off:b - off].to(torch.float64))
             Xs.append(rot.rows(target))
             ks.append(bits[nm][a - off:b - off])
             spans[nm] = (a - off, b - off)
@@ -127,6 +144,8 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
         if dequantize:
             res.Wq[nm] = rot.rows_t(settled[o:o + b - a] * S[o:o + b - a, None])
         o += b - a
+    env.check()
+    qep.check()
     return res
 
 

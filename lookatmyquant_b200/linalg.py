@@ -1,0 +1,122 @@
+"""fp64 dense linear algebra of the build on the fp64 tensor cores (liblamq_b200: lamq_dgemm, lamq_env_factor,
+lamq_cholesky_inverse_lower, lamq_ridge).
+
+Reference: opgraph/frame.py:515-522 (`Environment`: U = chol(cholesky_inverse(chol(H)))ᵀ after dead inputs and
+damping) and quantize.py:1330-1335 (`cross_target`: M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ), torch.linalg in
+fp64 there. Here U = J·chol(J·H·J)⁻¹·J (the same unique factor) and the QEP target W·M is formed through the Cholesky
+factor of H + λ·mean(diag H)·I: W·M = W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+
+
+def _f64(M: torch.Tensor) -> torch.Tensor:
+    if M.dtype != torch.float64 or not M.is_cuda:
+        raise TypeError("fp64 CUDA tensors expected")
+    return M if M.stride(-1) == 1 else M.contiguous()
+
+
+def _status(dev):
+    return torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+def _raise_if_not_pd(status):
+    if int(status.item()) == _lib.LAMQ_ERR_NOT_PD:
+        raise AssertionError("H is not positive definite even with damping")
+    _lib.check(int(status.item()), "factorization")
+
+
+def gemm(A, B, C=None, transB=False, alpha=1.0, beta=0.0):
+    """C = α·A·B (or α·A·Bᵀ) + β·C, fp64 on the tensor cores."""
+    A, B = _f64(A), _f64(B)
+    M, K = A.shape
+    N = B.shape[0] if transB else B.shape[1]
+    if C is None:
+        C = torch.empty(M, N, dtype=torch.float64, device=A.device)
+        beta = 0.0
+    with torch.cuda.device(A.device):
+        check(_lib.load().lamq_dgemm(1 if transB else 0, M, N, K, float(alpha), ptr(A), A.stride(0), ptr(B),
+                                     B.stride(0), float(beta), ptr(C), C.stride(0), stream_ptr(A.device)),
+              "lamq_dgemm")
+    return C
+
+
+def env_factor(H: torch.Tensor, damp: float = 0.01):
+    """(U, dead, check): the environment factor of frame.py:515-522 on the GPU. `check()` raises the reference's
+    error if H was not positive definite (it synchronises; call it when the result is needed)."""
+    H = _f64(H)
+    n = H.shape[0]
+    dev = H.device
+    lib = _lib.load()
+    U = torch.empty(n, n, dtype=torch.float64, device=dev)
+    dead = torch.empty(n, dtype=torch.uint8, device=dev)
+    ws = torch.empty(lib.lamq_factor_workspace_size(n), dtype=torch.uint8, device=dev)
+    st = _status(dev)
+    with torch.cuda.device(dev):
+        check(lib.lamq_env_factor(ptr(H), H.stride(0), n, float(damp), ptr(U), n, ptr(dead), ptr(ws), ws.numel(),
+                                  ptr(st), stream_ptr(dev)), "lamq_env_factor")
+    return U, dead.bool(), lambda: _raise_if_not_pd(st)
+
+
+def cholesky_inverse_lower(A: torch.Tensor, deferred: bool = False):
+    """L⁻¹ for A = L·Lᵀ (lower triangular, fp64), on a copy of A. With `deferred`, returns (L⁻¹, check) and leaves the
+    positive-definiteness check (a synchronisation) to the caller."""
+    A = _f64(A).clone()
+    n = A.shape[0]
+    lib = _lib.load()
+    ws = torch.empty(lib.lamq_factor_workspace_size(n), dtype=torch.uint8, device=A.device)
+    st = _status(A.device)
+    with torch.cuda.device(A.device):
+        check(lib.lamq_cholesky_inverse_lower(ptr(A), A.stride(0), n, ptr(ws), ws.numel(), ptr(st),
+                                              stream_ptr(A.device)), "lamq_cholesky_inverse_lower")
+    if deferred:
+        return A, lambda: _raise_if_not_pd(st)
+    _raise_if_not_pd(st)
+    return A
+
+
+def ridge(H: torch.Tensor, lam: float) -> torch.Tensor:
+    """H + λ·mean(diag H)·I."""
+    H = _f64(H)
+    n = H.shape[0]
+    A = torch.empty_like(H)
+    with torch.cuda.device(H.device):
+        check(_lib.load().lamq_ridge(ptr(H), H.stride(0), ptr(A), n, n, float(lam), stream_ptr(H.device)),
+              "lamq_ridge")
+    return A
+
+
+class CrossTarget:
+    """The QEP map of quantize.py:1330-1335 for one stage: `apply(W)` = W·M with M = I + α·(solve(H + λ·mean(diag H)·I,
+    Dᵀ))ᵀ = I + α·D·(H + λμI)⁻¹. With `rows` (the rows the stage will map) above n, M is formed once; otherwise each
+    W is mapped as W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹."""
+
+    def __init__(self, H, D, alpha: float, lam: float, rows: int | None = None):
+        n = H.shape[0]
+        self.alpha = alpha
+        self.Linv, self.check = cholesky_inverse_lower(ridge(H, lam), deferred=True)
+        self.D = _f64(D)
+        self.M = None
+        if rows is None or rows > n:
+            P = gemm(self.D, self.Linv, transB=True)
+            M = torch.eye(n, dtype=torch.float64, device=H.device)
+            self.M = gemm(P, self.Linv, C=M, alpha=alpha, beta=1.0)
+
+    def record_stream(self, stream):
+        """Marks the map's tensors as used on `stream` (they were made on another stream)."""
+        for t in (self.Linv, self.D, self.M):
+            if t is not None:
+                t.record_stream(stream)
+
+    def apply(self, W: torch.Tensor) -> torch.Tensor:
+        W = _f64(W)
+        if self.M is not None:
+            return gemm(W, self.M)
+        P = gemm(W, self.D)
+        P2 = gemm(P, self.Linv, transB=True)
+        return gemm(P2, self.Linv, C=W.clone(), alpha=self.alpha, beta=1.0)
