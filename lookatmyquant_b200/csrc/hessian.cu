@@ -4,20 +4,20 @@
 // fp32, then H/n_tok and D/n_tok − H as fp64; compiler.py:233-265 (`capture`) is the unweighted form.
 //
 // The contraction C[j][i] += Σ_t A[t][i]·B[t][j] over tokens t runs as a persistent warp-specialised GEMM:
-//   warp 0     one thread issues TMA loads of 64-token × 128-column tiles of A and B (bf16, row-major tokens × d,
-//              so both operands are MN-major in shared memory, 128-byte swizzle) into a 6-stage ring;
-//   warp 1     one thread issues tcgen05.mma (M = N = 128, K = 16, bf16 × bf16 → fp32) into one of two TMEM
-//              accumulators, releasing each stage with tcgen05.commit;
-//   warps 2-5  drain a finished accumulator with tcgen05.ld into an fp32 tile held in their registers (one row of
-//              128 columns per thread, added with round-to-nearest), while the MMA thread fills the other one; at the
-//              end of a unit they add the tile into the fp32 d × d accumulator in global memory (coalesced: written
-//              transposed).
+//   warp 0     one thread issues TMA loads of 64-token tiles of A (128 columns) and B (256 columns) (bf16, row-major
+//              tokens × d, so both operands are MN-major in shared memory, 128-byte swizzle) into a 4-stage ring;
+//   warp 1     one thread issues tcgen05.mma (M = 128, N = 256, K = 16, bf16 × bf16 → fp32) into one of two TMEM
+//              accumulators (the whole 512 columns), releasing each stage with tcgen05.commit;
+//   warps 2-9  drain a finished accumulator with tcgen05.ld into an fp32 tile held in their registers (two warps per
+//              TMEM lane quadrant, one row of 128 columns per thread, added with round-to-nearest), while the MMA
+//              thread fills the other one; at the end of a unit they add the tile into the fp32 d × d accumulator in
+//              global memory (coalesced: written transposed).
 // The tensor core's own fp32 accumulation truncates (it loses about half an ulp per MMA on average, always towards
 // zero), so TMEM only ever accumulates kDrainBlocks × 4 = 32 MMAs (512 tokens) before it is drained into the
 // registers: the bias stays near 1e-6 relative, where a whole chunk in TMEM would bias H by more than the 1e-5 bar.
-// A work unit is one 128 × 128 output tile over one chunk of tokens. Units are ordered by super-blocks of 12 × 12 tiles, then chunk,
-// then tile, so the ~148 concurrent CTAs share their A and B tiles through L2. For H only tiles with ti <= tj are
-// computed (H is symmetric); the finalize kernel mirrors them.
+// A work unit is one 128 × 256 output tile over one chunk of tokens. Units are ordered by super-blocks of 12 × 12
+// tiles, then chunk, then tile, so the ~148 concurrent CTAs share their A and B tiles through L2. For H only tiles that
+// hold a pair i <= j are computed (H is symmetric); the finalize kernel mirrors them.
 //
 // Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
 // (A = X, B = X: exact products), and the weighted tokens add Σ_t (w_t − 1)·x_t x_tᵀ in a second pass over only
@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "lamq_common.cuh"
@@ -37,24 +38,25 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 128, BK = 64;
-constexpr int STAGES = 6;
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KiB: two 64-column boxes of 64 tokens
-constexpr int B_BYTES = BN * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;  // 32 KiB: four boxes
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int HALF_BYTES = 64 * BK * 2;  // one TMA box: 64 columns x 64 tokens = 8 KiB (LBO between MN halves)
-constexpr int SB = 12;                   // tiles per super-block side
+constexpr int HALF_BYTES = 64 * BK * 2;  // one TMA box: 64 columns x 64 tokens = 8 KiB (LBO between MN blocks)
+constexpr int SBI = 12, SBJ = 12;        // tiles per super-block (rows of 128, columns of 256)
 constexpr int kDrainBlocks = 8;          // 64-token blocks accumulated in TMEM between drains (32 MMAs)
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;      // two 128 x 128 fp32 accumulators
+constexpr int kEpiWarps = 8;             // two per TMEM lane quadrant, 128 columns each
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 512;      // two 128 x 256 fp32 accumulators
 constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;
 
 struct GemmParams {
     float *acc;
     int64_t ldc;
     int d;
-    int ntile;
-    int ngroup;
+    int nti, ntj;           // row tiles (128) and column tiles (256)
+    int ngi, ngj;           // super-blocks
     int nchunk;
     int kblocks;            // total 64-token blocks
     int kblocks_per_chunk;
@@ -67,44 +69,38 @@ struct Unit {
     int ti, tj, kb0, nkb;
 };
 
+// Symmetric C: row tile ti (rows 128·ti..) and column tile tj (columns 256·tj..) hold a pair i <= j iff tj >= ti / 2.
+__device__ __forceinline__ int row_first_tj(int ti, const GemmParams &p) { return p.symmetric ? ti / 2 : 0; }
+
 __device__ __forceinline__ int group_tiles(int gi, int gj, const GemmParams &p) {
-    const int r0 = gi * SB, r1 = min(p.ntile, r0 + SB), c0 = gj * SB, c1 = min(p.ntile, c0 + SB);
-    if (!p.symmetric || gi < gj) return (r1 - r0) * (c1 - c0);
-    if (gi > gj) return 0;
-    const int m = r1 - r0;
-    return m * (m + 1) / 2;
+    const int r0 = gi * SBI, r1 = min(p.nti, r0 + SBI), c0 = gj * SBJ, c1 = min(p.ntj, c0 + SBJ);
+    int n = 0;
+    for (int ti = r0; ti < r1; ++ti) n += max(0, c1 - max(c0, row_first_tj(ti, p)));
+    return n;
 }
 
-// The u-th work unit: super-blocks in row-major order (only gi <= gj when symmetric), then chunks, then tiles.
+// The u-th work unit: super-blocks in row-major order, then chunks, then the super-block's tiles in row-major order.
 __device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
-    for (int gi = 0; gi < p.ngroup; ++gi) {
-        for (int gj = p.symmetric ? gi : 0; gj < p.ngroup; ++gj) {
+    for (int gi = 0; gi < p.ngi; ++gi) {
+        for (int gj = 0; gj < p.ngj; ++gj) {
             const int nt = group_tiles(gi, gj, p);
             const int64_t nu = (int64_t)nt * p.nchunk;
             if (u >= nu) {
                 u -= nu;
                 continue;
             }
-            const int chunk = (int)(u / nt), local = (int)(u % nt);
-            const int r0 = gi * SB, c0 = gj * SB, r1 = min(p.ntile, r0 + SB), c1 = min(p.ntile, c0 + SB);
-            if (p.symmetric && gi == gj) {
-                int rem = local;
-                const int m = r1 - r0;
-                out.ti = r0;
-                out.tj = r0;
-                for (int row = 0; row < m; ++row) {
-                    const int len = m - row;
-                    if (rem < len) {
-                        out.ti = r0 + row;
-                        out.tj = r0 + row + rem;
-                        break;
-                    }
-                    rem -= len;
+            const int chunk = (int)(u / nt);
+            int rem = (int)(u % nt);
+            const int r0 = gi * SBI, r1 = min(p.nti, r0 + SBI), c0 = gj * SBJ, c1 = min(p.ntj, c0 + SBJ);
+            for (int ti = r0; ti < r1; ++ti) {
+                const int first = max(c0, row_first_tj(ti, p));
+                const int len = max(0, c1 - first);
+                if (rem < len) {
+                    out.ti = ti;
+                    out.tj = first + rem;
+                    break;
                 }
-            } else {
-                const int w = c1 - c0;
-                out.ti = r0 + local / w;
-                out.tj = c0 + local % w;
+                rem -= len;
             }
             out.kb0 = chunk * p.kblocks_per_chunk;
             out.nkb = min(p.kblocks_per_chunk, p.kblocks - out.kb0);
@@ -112,6 +108,18 @@ __device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
         }
     }
     return false;
+}
+
+// 32 lanes x 32 bits, 32 consecutive columns: thread t of the warp gets lane (base lane + t).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 128);
+            mbar_init(tempty0 + 8 * a, kEpiWarps * 32);
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -168,8 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int t = (U.kb0 + kb) * BK;
                     tma_load_2d(sa, &mapA, U.ti * BM, t, fb);
                     tma_load_2d(sa + HALF_BYTES, &mapA, U.ti * BM + 64, t, fb);
-                    tma_load_2d(sb, &mapB, U.tj * BN, t, fb);
-                    tma_load_2d(sb + HALF_BYTES, &mapB, U.tj * BN + 64, t, fb);
+#pragma unroll
+                    for (int q = 0; q < BN / 64; ++q) tma_load_2d(sb + q * HALF_BYTES, &mapB, U.tj * BN + 64 * q, t, fb);
                     ++issued;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -239,16 +247,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitTimeoutNs) {
             }
         }
-    } else {  // ---- epilogue: warps 2..5 own TMEM lanes 32·(warp % 4) ..
-        const int q = warp & 3;
+    } else {  // ---- epilogue: warps 2..9; warp w reads TMEM lanes 32·(w % 4).., columns 128·((w − 2) / 4)..
+        const int q = warp & 3, half = (warp - 2) >> 2;
         uint32_t uses[2] = {0, 0};
         int acc = 0;
         for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x) {
             Unit U;
             if (!unit_at(u, p, U)) break;
-            float tile[BN];
+            float tile[128];
 #pragma unroll
-            for (int c = 0; c < BN; ++c) tile[c] = 0.f;
+            for (int c = 0; c < 128; ++c) tile[c] = 0.f;
             bool ok = true;
             for (int sub = 0; sub < U.nkb; sub += kDrainBlocks) {
                 if (!mbar_wait(tfull0 + 8 * acc, uses[acc] & 1, p.status)) {
@@ -257,14 +265,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++uses[acc];
                 tc_fence_after();
-                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + acc * BN;
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + acc * BN + 128 * half;
 #pragma unroll
-                for (int c = 0; c < BN / 16; ++c) {
-                    uint32_t r[16];
-                    tmem_ld16(tbase + c * 16, r);
+                for (int c = 0; c < 128 / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) tile[c * 16 + e] = __fadd_rn(tile[c * 16 + e], __uint_as_float(r[e]));
+                    for (int e = 0; e < 32; ++e) tile[c * 32 + e] = __fadd_rn(tile[c * 32 + e], __uint_as_float(r[e]));
                 }
                 tc_fence_before();
                 mbar_arrive(tempty0 + 8 * acc);
@@ -274,8 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int i = U.ti * BM + 32 * q + lane;
             if (i < p.d) {
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    const int j = U.tj * BN + c;
+                for (int c = 0; c < 128; ++c) {
+                    const int j = U.tj * BN + 128 * half + c;
                     if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, tile[c]);
                 }
             }
@@ -399,14 +407,17 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     p.acc = acc;
     p.ldc = ldacc;
     p.d = d;
-    p.ntile = (d + BM - 1) / BM;
-    p.ngroup = (p.ntile + SB - 1) / SB;
+    p.nti = (d + BM - 1) / BM;
+    p.ntj = (d + BN - 1) / BN;
+    p.ngi = (p.nti + SBI - 1) / SBI;
+    p.ngj = (p.ntj + SBJ - 1) / SBJ;
     p.kblocks = (int)((tokens + BK - 1) / BK);
     p.kblocks_per_chunk = (int)(chunk_tokens / BK);
     p.nchunk = (p.kblocks + p.kblocks_per_chunk - 1) / p.kblocks_per_chunk;
     p.symmetric = symmetric ? 1 : 0;
     p.status = status;
-    const int64_t tiles = symmetric ? (int64_t)p.ntile * (p.ntile + 1) / 2 : (int64_t)p.ntile * p.ntile;
+    int64_t tiles = 0;
+    for (int ti = 0; ti < p.nti; ++ti) tiles += symmetric ? std::max(0, p.ntj - ti / 2) : p.ntj;
     p.units = tiles * p.nchunk;
     cudaError_t e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) {
