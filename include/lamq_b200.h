@@ -87,12 +87,12 @@ int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *value
  * tables:   4 x 2^L fp64: the trellis values for k = 1, 2, 3, 4 (row of k at (k-1)·2^L).
  * row_bits: rows bytes, each row's k in 1..4 (the row plan's widths); NULL means every row uses `k_all`.
  * width, look, lazy: RowTrellisCode's width and look-ahead and sweep's lazy run (16, 8, 128 in the reference);
- *           width + look <= 32, lazy a multiple of width.
+ *           width + look <= 24, lazy a multiple of width.
  * states:   rows x n int16 out (ldStates = n): the trellis states.
  * settled:  rows x n fp64 out or NULL: the settled table values, in units of the row scale.
  * workspace: lamq_ldlq_rowtrellis_workspace_size(rows) bytes of device memory (the rows grouped by width into tiles
  *           of 16, and a tile counter).
- * Supported: L = 12; width + look <= 32; lazy <= 128 and a multiple of 4.
+ * Supported: L = 12; width + look <= 24; lazy <= 128 and a multiple of 4.
  */
 size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows);
 int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,

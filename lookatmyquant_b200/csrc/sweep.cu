@@ -2,11 +2,12 @@
 //
 // Reference: opgraph/syntax.py:86-124 (`sweep`), with the projection of opgraph/codes.py:442-450 and
 // RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so rows are grouped by
-// their width k into tiles of 16 and each tile is swept start to finish by one CTA of 8 warps (2 rows per warp):
+// their width k into tiles of 16 and each tile is swept start to finish by one CTA of 16 warps: 8 warp pairs, each
+// decoding 2 rows in turn (trellis_pair.cuh: 64 states per thread, fp32x2 arithmetic):
 //
 //   per run of `lazy` columns [b0, b1):
 //     the run's targets plus the `look` columns after it are copied from T into shared memory (Trun);
-//     per block of `width` columns, each warp, for each of its rows: decodes the block plus `look` columns ahead (in
+//     per block of `width` columns, each pair, for each of its rows: decodes the block plus `look` columns ahead (in
 //       units of the row scale, from the row's last state; the look-ahead past b1 is stale by design, as in the
 //       reference), settles the block with the fp64 table values, writes the columns as they stood to T (what sweep
 //       returns), solves z·U_BB = E by substitution, keeps z in the block's Trun slots, and updates the rest of the
@@ -18,17 +19,19 @@
 #include <algorithm>
 
 #include "lamq_common.cuh"
+#include "trellis_pair.cuh"
 #include "trellis_warp.cuh"
 
 namespace lamq {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kRowsPerWarp = 2;
-constexpr int kTileRows = kWarps * kRowsPerWarp;  // 16
+constexpr int kWarps = 16;
+constexpr int kPairs = kWarps / 2;
+constexpr int kRowsPerPair = 2;
+constexpr int kTileRows = kPairs * kRowsPerPair;  // 16
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxWin = 32;
+constexpr int kMaxWin = 24;  // RowTrellisCode windows: width 16 + look 8
 constexpr int kGemmCols = 64;                      // columns of U per GEMM stage (8 per warp)
 constexpr int kUStride = kGemmCols + 4;            // padded row of a staged U tile (conflict-free B fragments)
 constexpr int kMaxLazy = 128;
@@ -53,10 +56,17 @@ struct SweepParams {
     double *settled;
 };
 
-// Per-warp Viterbi scratch: two best buffers (2048 floats each, enough for k = 1) and 32 steps of back-pointers.
-constexpr size_t kWarpViterbiBytes = 2 * 2048 * sizeof(float) + kMaxWin * 32 * sizeof(unsigned long long);
+// Per-pair Viterbi scratch, carved per width: two best buffers of R floats and kMaxWin steps of back-pointers (WORDS x
+// 64 words each) — at most 22 KiB (k = 1) — and 8 words for the final reduction. The GEMM at the end of each run
+// reuses this space.
+template <int K>
+constexpr size_t pair_bytes() {
+    return 2 * (size_t)PairTrellis<K>::R * sizeof(float) + (size_t)kMaxWin * 64 * PairTrellis<K>::WORDS * sizeof(uint32_t);
+}
+constexpr size_t kPairMax = pair_bytes<1>() > pair_bytes<2>() ? pair_bytes<1>() : pair_bytes<2>();
+constexpr size_t kPairViterbiBytes = kPairMax + 8 * sizeof(float);
 constexpr size_t kGemmBytes = 2 * (size_t)kMaxLazy * kUStride * sizeof(double);
-constexpr size_t kUnionBytes = (kWarps * kWarpViterbiBytes > kGemmBytes) ? kWarps * kWarpViterbiBytes : kGemmBytes;
+constexpr size_t kUnionBytes = (kPairs * kPairViterbiBytes > kGemmBytes) ? kPairs * kPairViterbiBytes : kGemmBytes;
 
 __device__ __forceinline__ void dmma_8x8x4(double &c0, double &c1, double a, double b) {
     asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
@@ -90,7 +100,8 @@ __device__ void run_update(const SweepParams &p, double *Trun, const int *rows, 
     stage_u(Us[0], p, b0, nr, b1);
     cp_async_commit();
     const int ar = lane >> 2, ak = lane & 3;  // A fragment: row ar, k ak; B fragment: k ak, column ar
-    const int r0 = rows[ar], r1 = rows[8 + ar];
+    const int mt = warp >> 3, cg = warp & 7;   // this warp: rows 8·mt.., columns 8·cg.. of each 64-column chunk
+    const int r0 = rows[8 * mt + ar];
     for (int ch = 0; ch < nchunks; ++ch) {
         const int c0 = b1 + ch * kGemmCols;
         if (ch + 1 < nchunks) {
@@ -102,49 +113,40 @@ __device__ void run_update(const SweepParams &p, double *Trun, const int *rows, 
         }
         __syncthreads();
         const double *Ut = Us[ch & 1];
-        const int col = c0 + 8 * warp + 2 * ak;  // this thread's two output columns: col, col + 1
-        double c[2][2];
+        const int col = c0 + 8 * cg + 2 * ak;  // this thread's two output columns: col, col + 1
+        double c[2];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            const int r = mt ? r1 : r0;
-#pragma unroll
-            for (int e = 0; e < 2; ++e)
-                c[mt][e] = (r >= 0 && col + e < p.n) ? p.T[(int64_t)r * p.ldT + col + e] : 0.0;
-        }
-        const double *Ua = Ut + 8 * warp + ar;
+        for (int e = 0; e < 2; ++e) c[e] = (r0 >= 0 && col + e < p.n) ? p.T[(int64_t)r0 * p.ldT + col + e] : 0.0;
+        const double *Ua = Ut + 8 * cg + ar;
+        const double *Za = Trun + (8 * mt + ar) * p.trun_stride + ak;
 #pragma unroll 8
-        for (int ks = 0; ks < nr; ks += 4) {
-            const double b = Ua[(ks + ak) * kUStride];
-            const double a0 = -Trun[ar * p.trun_stride + ks + ak];
-            const double a1 = -Trun[(8 + ar) * p.trun_stride + ks + ak];
-            dmma_8x8x4(c[0][0], c[0][1], a0, b);
-            dmma_8x8x4(c[1][0], c[1][1], a1, b);
-        }
-        // D fragment: row ar (and 8 + ar), columns 2·ak, 2·ak + 1 of the warp's 8
+        for (int ks = 0; ks < nr; ks += 4) dmma_8x8x4(c[0], c[1], -Za[ks], Ua[(ks + ak) * kUStride]);
+        // D fragment: row ar, columns 2·ak, 2·ak + 1 of the warp's 8
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            const int r = mt ? r1 : r0;
-#pragma unroll
-            for (int e = 0; e < 2; ++e)
-                if (r >= 0 && col + e < p.n) p.T[(int64_t)r * p.ldT + col + e] = c[mt][e];
-        }
+        for (int e = 0; e < 2; ++e)
+            if (r0 >= 0 && col + e < p.n) p.T[(int64_t)r0 * p.ldT + col + e] = c[e];
         __syncthreads();  // the stage buffer is refilled two chunks later
     }
 }
 
 template <int K>
 __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *rs, double *Trun, unsigned char *vregion,
-                           double *gemm) {
+                           double *gemm, int *row_state) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float cv[Trellis<K>::NB][Trellis<K>::RL];
+    const int pair = warp >> 1, pt = (warp & 1) * 32 + lane, bar = 1 + pair;
+    const bool lead = (warp & 1) == 0;  // the pair's first warp settles and refits its rows
+    u64 cv[PairTrellis<K>::NB][PairTrellis<K>::RT / 2];
     const double *tab = p.tables + (K - 1) * kStates;
-    load_pred_values<K>(tab, lane, cv);
-    unsigned char *wv = vregion + (size_t)warp * kWarpViterbiBytes;
+    load_pair_values<K>(tab, pt, cv);
+    unsigned char *wv = vregion + (size_t)pair * kPairViterbiBytes;
     float *best0 = reinterpret_cast<float *>(wv);
-    float *best1 = best0 + 2048;
-    unsigned long long *args = reinterpret_cast<unsigned long long *>(best1 + 2048);
+    float *best1 = best0 + PairTrellis<K>::R;
+    uint32_t *args = reinterpret_cast<uint32_t *>(best1 + PairTrellis<K>::R);
+    float *red = reinterpret_cast<float *>(wv + kPairMax);
+    // each row's last state, shared by the pair; outside the Viterbi scratch, which the run's GEMM reuses
+    int *pstate = row_state + pair * kRowsPerPair;
     const int n = p.n;
-    int state[kRowsPerWarp] = {0, 0};  // every row's path starts at state 0 (codes.py:399-400)
+    if (pt < kRowsPerPair) pstate[pt] = 0;  // every row's path starts at state 0 (codes.py:399-400)
     for (int b0 = 0; b0 < n; b0 += p.lazy) {
         const int b1 = min(b0 + p.lazy, n);
         const int ncol = b1 - b0 + min(p.look, n - b1);
@@ -156,43 +158,55 @@ __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *
         for (int j = b0; j < b1; j += p.width) {
             const int w = min(p.width, n - j);
             const int win = w + min(p.look, n - j - w);
-#pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-                const int r = warp * kRowsPerWarp + rr;
+#pragma unroll 1
+            for (int rr = 0; rr < kRowsPerPair; ++rr) {
+                const int r = pair * kRowsPerPair + rr;
                 const int row = rows[r];
                 if (row < 0) continue;
                 double *tr = Trun + r * p.trun_stride;
                 const double s = rs[r];
                 const double tv = (lane < win) ? tr[j - b0 + lane] : 0.0;
                 const float xv = __double2float_rn(__ddiv_rn(tv, s));  // (T / S).to(float32)
-                const int st = viterbi_window<K>(xv, win, true, state[rr], cv, best0, best1, args, lane);
-                state[rr] = __shfl_sync(0xffffffffu, st, w - 1);
-                double e = 0.0;
-                if (lane < w) {
-                    const double q = __ldg(tab + st);  // the fp64 table value (codes.py:404)
-                    p.states[(int64_t)row * n + j + lane] = (int16_t)st;
-                    if (p.settled != nullptr) p.settled[(int64_t)row * n + j + lane] = q;
-                    p.T[(int64_t)row * p.ldT + j + lane] = tv;  // the column as it stood (sweep's return value)
-                    e = __dsub_rn(tv, __dmul_rn(q, s));        // E = T - q·S (codes.py:449, syntax.py:115)
+                const int st = viterbi_window_pair<K>(xv, win, pstate[rr], pt, bar, cv, best0, best1, args, red);
+                if (lead) {
+                    const int last = __shfl_sync(0xffffffffu, st, w - 1);
+                    double e = 0.0;
+                    if (lane < w) {
+                        const double q = __ldg(tab + st);  // the fp64 table value (codes.py:404)
+                        p.states[(int64_t)row * n + j + lane] = (int16_t)st;
+                        if (p.settled != nullptr) p.settled[(int64_t)row * n + j + lane] = q;
+                        p.T[(int64_t)row * p.ldT + j + lane] = tv;  // the column as it stood (sweep's return value)
+                        e = __dsub_rn(tv, __dmul_rn(q, s));        // E = T - q·S (codes.py:449, syntax.py:115)
+                    }
+                    // z·U_BB = E, U_BB upper triangular: column-by-column substitution (syntax.py:117). Lane c keeps
+                    // column c of U_BB in registers and the reciprocal of its diagonal, so the dependent chain is one
+                    // multiply and one fused update per column.
+                    double ucol[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        ucol[i] = (i < w && lane < w) ? __ldg(p.U + (int64_t)(j + i) * p.ldU + j + lane) : 0.0;
+                    const double rdiag = (lane < w) ? 1.0 / __ldg(p.U + (int64_t)(j + lane) * p.ldU + j + lane) : 0.0;
+                    double acc = e;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        if (i < w) {
+                            const double zi = __shfl_sync(0xffffffffu, acc * rdiag, i);
+                            if (lane > i && lane < w) acc = fma(-zi, ucol[i], acc);
+                            if (lane == i) acc = zi;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane < w) tr[j - b0 + lane] = acc;  // the block's slots now hold z
+                    if (lane == 0) pstate[rr] = last;
                 }
-                // z·U_BB = E, U_BB upper triangular: column-by-column substitution (syntax.py:117)
-                double acc = e;
-                for (int i = 0; i < w; ++i) {
-                    const double zi =
-                        __ddiv_rn(__shfl_sync(0xffffffffu, acc, i), __ldg(p.U + (int64_t)(j + i) * p.ldU + j + i));
-                    if (lane > i && lane < w) acc = __dsub_rn(acc, __dmul_rn(zi, __ldg(p.U + (int64_t)(j + i) * p.ldU + j + lane)));
-                    if (lane == i) acc = zi;
-                }
-                __syncwarp();
-                if (lane < w) tr[j - b0 + lane] = acc;  // the block's slots now hold z
-                __syncwarp();
-                // the rest of the run: T[j+w : b1] -= z · U[block, j+w : b1] (syntax.py:118)
-                for (int c = j + w + lane; c < b1; c += 32) {
+                pair_sync(bar);  // z and the new start state are visible to the pair
+                // the rest of the run: T[j+w : b1] -= z · U[block, j+w : b1] (syntax.py:118), both warps of the pair
+                for (int c = j + w + pt; c < b1; c += 64) {
                     double a = 0.0;
                     for (int i = 0; i < w; ++i) a = fma(tr[j - b0 + i], __ldg(p.U + (int64_t)(j + i) * p.ldU + c), a);
                     tr[c - b0] -= a;
                 }
-                __syncwarp();
+                pair_sync(bar);  // the row's next window reads the updated run and the new start state
             }
         }
         __syncthreads();
@@ -206,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
     unsigned char *uni = smem + (size_t)kTileRows * p.trun_stride * sizeof(double);
     uni = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(uni) + 15) & ~uintptr_t(15));
     __shared__ int rows[kTileRows];
+    __shared__ int row_state[kTileRows];
     __shared__ double rs[kTileRows];
     __shared__ int tile_s, k_s;
     const int ntiles = *p.ntiles;
@@ -229,10 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
             }
         __syncthreads();
         switch (k_s) {
-            case 1: sweep_tile<1>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
-            case 2: sweep_tile<2>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
-            case 3: sweep_tile<3>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
-            default: sweep_tile<4>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni)); break;
+            case 1: sweep_tile<1>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
+            case 2: sweep_tile<2>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
+            case 3: sweep_tile<3>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
+            default: sweep_tile<4>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
         }
         __syncthreads();
     }
@@ -300,7 +315,7 @@ extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n,
     if (rows == 0 || n == 0) return LAMQ_OK;
     LAMQ_REQUIRE(T && U && S && tables && states, "lamq_ldlq_rowtrellis: null pointer");
     LAMQ_REQUIRE(ldT >= n && ldU >= n, "lamq_ldlq_rowtrellis: leading dimension below n");
-    LAMQ_REQUIRE(width >= 1 && look >= 0 && width + look <= kMaxWin, "lamq_ldlq_rowtrellis: need width + look <= 32");
+    LAMQ_REQUIRE(width >= 1 && look >= 0 && width + look <= kMaxWin, "lamq_ldlq_rowtrellis: need width + look <= 24");
     LAMQ_REQUIRE(lazy >= width && lazy % width == 0 && lazy <= kMaxLazy && lazy % 4 == 0,
                  "lamq_ldlq_rowtrellis: lazy must be a multiple of width and of 4, at most 128");
     LAMQ_REQUIRE(row_bits != nullptr || (k_all >= 1 && k_all <= 4), "lamq_ldlq_rowtrellis: k must be 1..4");

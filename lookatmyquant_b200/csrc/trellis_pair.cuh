@@ -1,0 +1,276 @@
+// Viterbi over the 12-bit bitshift trellis by a pair of warps (64 threads) per sequence, with packed fp32x2 arithmetic.
+//
+// The recursion is that of trellis_warp.cuh (opgraph/codes.py:151-181 restated over "best" arrays):
+//   cost_t[s] = best_t[s >> k] + (x_t − C[s])²,   best_t[r] = min_{h < 2^k} cost_{t−1}[h·R + r]   (smallest h on ties)
+// Thread p (0..63) of the pair owns RT = R/64 consecutive r and keeps the 64 table values C[h·R + r] of its
+// predecessors in registers as fp32 pairs (half the registers of one warp per row, so twice the warps fit on an SM).
+// (x − C)² is computed two states at a time with sub/mul.rn.f32x2 and the add to the best predecessor cost with
+// add.rn.f32: every value is rounded exactly as the reference's scalar fp32 sub, mul and add (explicit rounding, never
+// fused). The minimum over the 2^k predecessors is a knock-out tournament whose decisions are the sign bits of fp32
+// differences (the fp32 pipe, not the half-rate compare/select pipe) appended to the back-pointer words by funnel
+// shifts: 2^k − 1 bits per r, decoded on the traceback. The pair exchanges the R best values through shared memory
+// (double buffered, one named barrier per step), stored in 16-byte units swizzled by writer thread so that writes and
+// reads are free of bank conflicts for every k.
+#pragma once
+
+#include "lamq_common.cuh"
+
+namespace lamq {
+
+template <int K>
+struct PairTrellis {
+    static constexpr int NB = 1 << K;
+    static constexpr int R = 1 << (12 - K);
+    static constexpr int RT = R / 64;                           // r values per thread
+    static constexpr int DIST = (RT >> K) > 0 ? (RT >> K) : 1;  // distinct best values a thread reads per h
+    static constexpr int UNITS = RT / 4;                        // 16-byte units a thread writes
+    static constexpr int SH = (UNITS >= 8) ? 3 : (UNITS == 4) ? 2 : (UNITS == 2) ? 1 : 0;
+    static constexpr int NBITS = RT * (NB - 1);                 // tournament bits per thread per step
+    static constexpr int WORDS = (NBITS + 31) / 32;
+    static_assert(NB * RT == 64, "each thread covers 64 predecessor states");
+    static_assert(WORDS <= 2, "at most two back-pointer words per thread per step");
+};
+
+template <int K>
+__device__ __forceinline__ int pslot(int r) {
+    if constexpr (PairTrellis<K>::UNITS <= 1) {
+        return r;
+    } else {
+        int u = r >> 2;
+        u ^= (u >> PairTrellis<K>::SH) & 7;  // a bijection for SH >= 1
+        return (u << 2) | (r & 3);
+    }
+}
+
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 pk2(float lo, float hi) {
+    u64 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk2(u64 v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
+    u64 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+    u64 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+    u64 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+__device__ __forceinline__ void pair_sync(int bar) { asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory"); }
+
+// cv[h][j] = (C[h·R + p·RT + 2j], C[h·R + p·RT + 2j + 1]) as fp32 (rounded from the fp64 table like values.float()).
+template <int K>
+__device__ __forceinline__ void load_pair_values(const double *__restrict__ table, int p,
+                                                 u64 (&cv)[PairTrellis<K>::NB][PairTrellis<K>::RT / 2]) {
+    using T = PairTrellis<K>;
+#pragma unroll
+    for (int h = 0; h < T::NB; ++h)
+#pragma unroll
+        for (int j = 0; j < T::RT / 2; ++j) {
+            const int s = h * T::R + p * T::RT + 2 * j;
+            cv[h][j] = pk2((float)__ldg(table + s), (float)__ldg(table + s + 1));
+        }
+}
+
+template <int K>
+__device__ __forceinline__ void init_best_pair(float *best, int p, bool has_start, int start) {
+    using T = PairTrellis<K>;
+    const int r0 = start & (T::R - 1);
+    const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+    for (int i = 0; i < T::RT; i += 4) {
+        const int r = p * T::RT + i;
+        float4 v;
+        v.x = (!has_start || r + 0 == r0) ? 0.f : inf;
+        v.y = (!has_start || r + 1 == r0) ? 0.f : inf;
+        v.z = (!has_start || r + 2 == r0) ? 0.f : inf;
+        v.w = (!has_start || r + 3 == r0) ? 0.f : inf;
+        *reinterpret_cast<float4 *>(best + pslot<K>(r)) = v;
+    }
+}
+
+// Appends the decision bit of one comparison — the sign of c_b − c_a, set exactly when c_b < c_a (for these
+// non-negative costs the rounded difference has the sign of the exact one; ties and inf − inf give 0, keeping a) —
+// to the back-pointer word of sequence index `seq` (compile-time), by a funnel shift.
+template <int K>
+__device__ __forceinline__ void push_bit(uint32_t (&words)[PairTrellis<K>::WORDS], int seq, float d) {
+    words[seq >> 5] = __funnelshift_l(__float_as_uint(d), words[seq >> 5], 1);
+}
+
+// Knock-out minimum of NB costs (pairs, then pairs of winners, …), the left (smaller h) winning ties: the first
+// minimum, as torch.min picks it. Appends the NB − 1 decision bits in order (level 1 left to right, then level 2, …).
+template <int K>
+__device__ __forceinline__ float tournament(float (&m)[PairTrellis<K>::NB], uint32_t (&words)[PairTrellis<K>::WORDS],
+                                            int seq) {
+    constexpr int NB = PairTrellis<K>::NB;
+    int q = 0;
+#pragma unroll
+    for (int n = NB; n > 1; n >>= 1) {
+#pragma unroll
+        for (int g = 0; g < n / 2; ++g) {
+            push_bit<K>(words, seq + q, __fsub_rn(m[2 * g + 1], m[2 * g]));
+            ++q;
+            m[g] = fminf(m[2 * g], m[2 * g + 1]);
+        }
+    }
+    return m[0];
+}
+
+// One add-compare-select step for the thread's RT values of r: best_t into bout, the decision bits into words.
+template <int K>
+__device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *__restrict__ bout, float xp, int p,
+                                         const u64 (&cv)[PairTrellis<K>::NB][PairTrellis<K>::RT / 2],
+                                         uint32_t (&words)[PairTrellis<K>::WORDS]) {
+    using T = PairTrellis<K>;
+    constexpr int CH = (T::DIST >= 4) ? 4 : 1;                // best values loaded per chunk per h
+    constexpr int CI = (T::DIST >= 4) ? (4 << K) : T::RT;     // r values per chunk
+    const u64 xx = pk2(xp, xp);
+#pragma unroll
+    for (int w = 0; w < T::WORDS; ++w) words[w] = 0u;
+#pragma unroll
+    for (int c0 = 0; c0 < T::RT; c0 += CI) {
+        float bv[T::NB][CH];
+#pragma unroll
+        for (int h = 0; h < T::NB; ++h) {
+            const int base = h * (T::R >> K) + ((p * T::RT + c0) >> K);
+            if constexpr (CH == 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(bin + pslot<K>(base));
+                bv[h][0] = v.x; bv[h][1] = v.y; bv[h][2] = v.z; bv[h][3] = v.w;
+            } else {
+                bv[h][0] = bin[pslot<K>(base)];
+            }
+        }
+        float nb4[4];
+#pragma unroll
+        for (int i = 0; i < CI; i += 2) {
+            const int ii = c0 + i;
+            float clo[T::NB], chi[T::NB];
+#pragma unroll
+            for (int h = 0; h < T::NB; ++h) {
+                const float b = bv[h][(CH == 4) ? (i >> K) : 0];
+                const u64 d = sub2(xx, cv[h][ii >> 1]);  // (x − C) for r = ii and ii + 1
+                float slo, shi;
+                upk2(mul2(d, d), slo, shi);
+                clo[h] = __fadd_rn(b, slo);
+                chi[h] = __fadd_rn(b, shi);
+            }
+            nb4[i & 3] = tournament<K>(clo, words, ii * (T::NB - 1));
+            nb4[(i & 3) + 1] = tournament<K>(chi, words, (ii + 1) * (T::NB - 1));
+            if ((i & 3) == 2)
+                *reinterpret_cast<float4 *>(bout + pslot<K>(p * T::RT + ii - 2)) =
+                    make_float4(nb4[0], nb4[1], nb4[2], nb4[3]);
+        }
+    }
+}
+
+// The chosen predecessor h of r at a step, decoded from the owner thread's tournament bits (args: WORDS x 64 words).
+template <int K>
+__device__ __forceinline__ int decode_choice(const uint32_t *__restrict__ args, int r) {
+    using T = PairTrellis<K>;
+    const int owner = r / T::RT, i = r % T::RT;
+    int g = 0, before = 0;
+#pragma unroll
+    for (int l = 1; l < K; ++l) before += T::NB >> l;  // comparisons below the top level
+#pragma unroll
+    for (int lvl = K; lvl >= 1; --lvl) {
+        const int seq = i * (T::NB - 1) + before + g;
+        const int w = seq >> 5;
+        const int nbw = (T::NBITS - 32 * w) < 32 ? (T::NBITS - 32 * w) : 32;
+        const uint32_t word = args[w * 64 + owner];
+        g = 2 * g + (int)((word >> (nbw - 1 - (seq & 31))) & 1u);
+        if (lvl > 1) before -= T::NB >> (lvl - 1);
+    }
+    return g;
+}
+
+// First state of minimum final cost over the pair (smallest state on ties); red holds 4 words of pair scratch.
+template <int K>
+__device__ __forceinline__ int final_argmin_pair(const float *__restrict__ best, float xl, int p, int bar,
+                                                 const u64 (&cv)[PairTrellis<K>::NB][PairTrellis<K>::RT / 2],
+                                                 float *red) {
+    using T = PairTrellis<K>;
+    const u64 xx = pk2(xl, xl);
+    float m = __int_as_float(0x7f800000);
+    int ms = 0x7fffffff;
+#pragma unroll
+    for (int h = 0; h < T::NB; ++h) {
+#pragma unroll
+        for (int i = 0; i < T::RT; i += 2) {
+            const float b = best[pslot<K>(h * (T::R >> K) + ((p * T::RT + i) >> K))];
+            const u64 d = sub2(xx, cv[h][i >> 1]);
+            const u64 c = add2(pk2(b, b), mul2(d, d));
+            float lo, hi;
+            upk2(c, lo, hi);
+            const int s = h * T::R + p * T::RT + i;  // states visited in increasing order
+            if (lo < m || ms == 0x7fffffff) { m = lo; ms = s; }
+            if (hi < m) { m = hi; ms = s + 1; }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, off);
+        const int os = __shfl_xor_sync(0xffffffffu, ms, off);
+        if (om < m || (om == m && os < ms)) { m = om; ms = os; }
+    }
+    const int w = p >> 5;
+    if ((p & 31) == 0) {
+        red[2 * w] = m;
+        reinterpret_cast<int *>(red)[2 * w + 1] = ms;
+    }
+    pair_sync(bar);
+    const float m0 = red[0], m1 = red[2];
+    const int s0 = reinterpret_cast<int *>(red)[1], s1 = reinterpret_cast<int *>(red)[3];
+    const int fs = (m1 < m0 || (m1 == m0 && s1 < s0)) ? s1 : s0;
+    pair_sync(bar);  // red is reused by the next window
+    return fs;
+}
+
+// Decodes one window x_0..x_{T−1} (lane t of each warp holds x_t, T <= 32) with the pair; lane t of the pair's first
+// warp returns the state at position t. best0/best1: two R-float buffers; args: T x WORDS x 64 words; red: 4 words.
+template <int K>
+__device__ __forceinline__ int viterbi_window_pair(float xv, int T, int start, int p, int bar,
+                                                   const u64 (&cv)[PairTrellis<K>::NB][PairTrellis<K>::RT / 2],
+                                                   float *best0, float *best1, uint32_t *args, float *red) {
+    using Tr = PairTrellis<K>;
+    init_best_pair<K>(best0, p, true, start);
+    pair_sync(bar);
+    float *bin = best0, *bout = best1;
+    for (int t = 1; t < T; ++t) {
+        const float xp = __shfl_sync(0xffffffffu, xv, t - 1);
+        uint32_t words[Tr::WORDS];
+        acs_pair<K>(bin, bout, xp, p, cv, words);
+#pragma unroll
+        for (int w = 0; w < Tr::WORDS; ++w) args[(t * Tr::WORDS + w) * 64 + p] = words[w];
+        pair_sync(bar);
+        float *tmp = bin;
+        bin = bout;
+        bout = tmp;
+    }
+    const float xl = __shfl_sync(0xffffffffu, xv, T - 1);
+    const int fs = final_argmin_pair<K>(bin, xl, p, bar, cv, red);
+    if (p >= 32) return 0;  // only the first warp needs the path
+    // traceback: every lane walks the path (broadcast reads); lane t keeps position t
+    const int lane = p & 31;
+    int s = fs;
+    int mine = (lane == T - 1) ? s : 0;
+    for (int t = T - 1; t > 0; --t) {
+        const int r = s >> K;
+        s = decode_choice<K>(args + t * Tr::WORDS * 64, r) * Tr::R + r;
+        if (lane == t - 1) mine = s;
+    }
+    return mine;
+}
+
+}  // namespace lamq

@@ -80,7 +80,7 @@ def test_kernel_mixed_row_widths(golden):
     assert np.array_equal(states + 4096 * table_index[:, None], g["states"].astype(np.int64))
 
 
-@pytest.mark.parametrize("width,look", [(16, 8), (8, 4), (16, 0), (4, 12)])
+@pytest.mark.parametrize("width,look", [(16, 8), (8, 4), (16, 0), (4, 12), (8, 16)])
 def test_kernel_other_windows(width, look):
     rng = np.random.default_rng(width * 100 + look)
     m, n, k = 40, 192, 2
