@@ -15,8 +15,11 @@
 // The tensor core's own fp32 accumulation truncates (it loses about half an ulp per MMA on average, always towards
 // zero), so TMEM only ever accumulates kDrainBlocks × 4 = 32 MMAs (512 tokens) before it is drained into the
 // registers: the bias stays near 1e-6 relative, where a whole chunk in TMEM would bias H by more than the 1e-5 bar.
-// A work unit is one 128 × 256 output tile over one chunk of tokens. Units are ordered by super-blocks of 12 × 12
-// tiles, then chunk, then tile, so the ~148 concurrent CTAs share their A and B tiles through L2. For H only tiles that
+// A work unit is one 128 × 256 output tile over one chunk of tokens. The tiles are listed band by band (bands of about
+// 16 row tiles, column by column inside a band) and cut into windows of exactly one tile per CTA; units run window by
+// window, chunk by chunk inside a window. So each wave of CTAs computes one window over one chunk: a compact block of
+// about 16 × 9 tiles whose CTAs read the same A and B tiles at about the same time and share them through L2. For H
+// only tiles that
 // hold a pair i <= j are computed (H is symmetric); the finalize kernel mirrors them.
 //
 // Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
@@ -44,70 +47,90 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KiB: two 64-column boxes of 64 token
 constexpr int B_BYTES = BN * BK * 2;  // 32 KiB: four boxes
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int HALF_BYTES = 64 * BK * 2;  // one TMA box: 64 columns x 64 tokens = 8 KiB (LBO between MN blocks)
-constexpr int SBI = 12, SBJ = 12;        // tiles per super-block (rows of 128, columns of 256)
+constexpr int kBandTarget = 16;          // row tiles per band (bands are evened out to at most this many)
 constexpr int kDrainBlocks = 8;          // 64-token blocks accumulated in TMEM between drains (32 MMAs)
 constexpr int kEpiWarps = 8;             // two per TMEM lane quadrant, 128 columns each
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;      // two 128 x 256 fp32 accumulators
 constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;
+// The wave gate keeps the CTAs in step: CTA b runs units b, b + G, b + 2G, … (G CTAs), and its producer starts wave w
+// only once the producers have issued every load of waves 0 … w − 1. Without it the CTAs drift apart over the
+// waves (a CTA that misses in L2 falls behind and then misses more), the CTAs that share an A or B tile no longer
+// read it at about the same time, and DRAM re-reads the operands several times over. The gate is a throttle, not a
+// correctness condition: a wait longer than kGateTimeoutNs (CTAs not co-resident, a producer that stopped on an
+// error) switches the gate off for the rest of the launch.
+constexpr unsigned long long kGateTimeoutNs = 20000000ull;
+constexpr int kGateSlots = 64;
 
 struct GemmParams {
     float *acc;
     int64_t ldc;
     int d;
     int nti, ntj;           // row tiles (128) and column tiles (256)
-    int ngi, ngj;           // super-blocks
+    int band;               // row tiles per band
+    int64_t ntiles;         // tiles computed
+    int win;                // tiles per window (= CTAs)
     int nchunk;
     int kblocks;            // total 64-token blocks
     int kblocks_per_chunk;
     int symmetric;
     int64_t units;
     int *status;
+    unsigned int *gate;     // units whose loads have all been issued (the wave gate), zeroed before the launch
 };
 
 struct Unit {
     int ti, tj, kb0, nkb;
 };
 
-// Symmetric C: row tile ti (rows 128·ti..) and column tile tj (columns 256·tj..) hold a pair i <= j iff tj >= ti / 2.
-__device__ __forceinline__ int row_first_tj(int ti, const GemmParams &p) { return p.symmetric ? ti / 2 : 0; }
-
-__device__ __forceinline__ int group_tiles(int gi, int gj, const GemmParams &p) {
-    const int r0 = gi * SBI, r1 = min(p.nti, r0 + SBI), c0 = gj * SBJ, c1 = min(p.ntj, c0 + SBJ);
-    int n = 0;
-    for (int ti = r0; ti < r1; ++ti) n += max(0, c1 - max(c0, row_first_tj(ti, p)));
-    return n;
+// Tiles of column tj inside the band of row tiles [b0, b1). Symmetric C: row tile ti (rows 128·ti..) and column tile
+// tj (columns 256·tj..) hold a pair i <= j iff tj >= ti / 2, that is ti < 2·tj + 2.
+__device__ __forceinline__ int band_column(int b0, int b1, int tj, const GemmParams &p) {
+    return p.symmetric ? max(0, min(b1, 2 * tj + 2) - b0) : b1 - b0;
 }
 
-// The u-th work unit: super-blocks in row-major order, then chunks, then the super-block's tiles in row-major order.
-__device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
-    for (int gi = 0; gi < p.ngi; ++gi) {
-        for (int gj = 0; gj < p.ngj; ++gj) {
-            const int nt = group_tiles(gi, gj, p);
-            const int64_t nu = (int64_t)nt * p.nchunk;
-            if (u >= nu) {
-                u -= nu;
-                continue;
+// The idx-th tile of the band raster (bands top to bottom, columns left to right, rows top to bottom).
+__device__ void tile_at(int64_t idx, const GemmParams &p, int &ti, int &tj) {
+    for (int b0 = 0; b0 < p.nti; b0 += p.band) {
+        const int b1 = min(p.nti, b0 + p.band);
+        for (int c = 0; c < p.ntj; ++c) {
+            const int n = band_column(b0, b1, c, p);
+            if (idx < n) {
+                ti = b0 + (int)idx;
+                tj = c;
+                return;
             }
-            const int chunk = (int)(u / nt);
-            int rem = (int)(u % nt);
-            const int r0 = gi * SBI, r1 = min(p.nti, r0 + SBI), c0 = gj * SBJ, c1 = min(p.ntj, c0 + SBJ);
-            for (int ti = r0; ti < r1; ++ti) {
-                const int first = max(c0, row_first_tj(ti, p));
-                const int len = max(0, c1 - first);
-                if (rem < len) {
-                    out.ti = ti;
-                    out.tj = first + rem;
-                    break;
-                }
-                rem -= len;
-            }
-            out.kb0 = chunk * p.kblocks_per_chunk;
-            out.nkb = min(p.kblocks_per_chunk, p.kblocks - out.kb0);
-            return true;
+            idx -= n;
         }
     }
-    return false;
+    ti = tj = 0;  // not reached: idx < ntiles
+}
+
+// The u-th work unit: windows of p.win consecutive tiles in order, then chunks, then the window's tiles.
+__device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
+    const int64_t full = p.ntiles / p.win, per_full = (int64_t)p.win * p.nchunk;
+    int64_t idx;
+    int chunk;
+    if (u < full * per_full) {
+        const int64_t w = u / per_full, rem = u % per_full;
+        chunk = (int)(rem / p.win);
+        idx = w * p.win + rem % p.win;
+    } else {
+        const int64_t last = p.ntiles - full * p.win, rem = u - full * per_full;
+        if (last == 0 || rem >= last * p.nchunk) return false;
+        chunk = (int)(rem / last);
+        idx = full * p.win + rem % last;
+    }
+    tile_at(idx, p, out.ti, out.tj);
+    out.kb0 = chunk * p.kblocks_per_chunk;
+    out.nkb = min(p.kblocks_per_chunk, p.kblocks - out.kb0);
+    return true;
+}
+
+__device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int *p) {
+    unsigned int v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // 32 lanes x 32 bits, 32 consecutive columns: thread t of the warp gets lane (base lane + t).
@@ -161,10 +184,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             int64_t issued = 0;
-            bool ok = true;
-            for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+            bool ok = true, gate = p.gate != nullptr;
+            int64_t wave = 0;
+            for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++wave) {
                 Unit U;
                 if (!unit_at(u, p, U)) break;
+                if (gate && wave > 0) {
+                    const unsigned int target = (unsigned int)(wave * gridDim.x);
+                    const unsigned long long t0 = globaltimer();
+                    while (ld_relaxed_u32(p.gate) < target) {
+                        if (globaltimer() - t0 > kGateTimeoutNs) {
+                            gate = false;
+                            break;
+                        }
+                        __nanosleep(256);
+                    }
+                }
                 for (int kb = 0; kb < U.nkb; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status)) {
                         ok = false;
@@ -184,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         phase ^= 1;
                     }
                 }
+                if (ok && p.gate != nullptr) atomicAdd(p.gate, 1u);
             }
             if (!ok) {  // error path: let the copies already in flight land before the CTA exits
                 const int64_t outstanding = issued < STAGES ? issued : STAGES;
@@ -370,6 +406,44 @@ int make_map(CUtensorMap *m, const void *base, int64_t tokens, int d, int64_t ld
     return LAMQ_OK;
 }
 
+constexpr int kMaxDevices = 64;
+__device__ unsigned int g_gate[kGateSlots];  // one array per device (module globals are per device)
+
+// A wave-gate counter for one launch on the current device: slots are handed out round robin (launches in flight at
+// once take different slots) and zeroed on the launch's stream.
+int gate_counter(cudaStream_t stream, unsigned int **out) {
+    static std::mutex mu;
+    static unsigned int *base[kMaxDevices] = {};
+    static unsigned int next[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("lamq_xtx_accumulate: no usable current device");
+        return LAMQ_ERR_CUDA;
+    }
+    unsigned int *slot;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (base[dev] == nullptr) {
+            void *sym = nullptr;
+            e = cudaGetSymbolAddress(&sym, g_gate);
+            if (e != cudaSuccess || sym == nullptr) {
+                set_error("lamq_xtx_accumulate: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+                return LAMQ_ERR_CUDA;
+            }
+            base[dev] = reinterpret_cast<unsigned int *>(sym);
+        }
+        slot = base[dev] + (next[dev]++ % kGateSlots);
+    }
+    e = cudaMemsetAsync(slot, 0, sizeof(unsigned int), stream);
+    if (e != cudaSuccess) {
+        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    *out = slot;
+    return LAMQ_OK;
+}
+
 int num_sms() {
     static int sms = 0;
     if (sms == 0) {
@@ -409,8 +483,10 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     p.d = d;
     p.nti = (d + BM - 1) / BM;
     p.ntj = (d + BN - 1) / BN;
-    p.ngi = (p.nti + SBI - 1) / SBI;
-    p.ngj = (p.ntj + SBJ - 1) / SBJ;
+    {
+        const int nb = (p.nti + kBandTarget - 1) / kBandTarget;
+        p.band = (p.nti + nb - 1) / nb;
+    }
     p.kblocks = (int)((tokens + BK - 1) / BK);
     p.kblocks_per_chunk = (int)(chunk_tokens / BK);
     p.nchunk = (p.kblocks + p.kblocks_per_chunk - 1) / p.kblocks_per_chunk;
@@ -419,12 +495,16 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     int64_t tiles = 0;
     for (int ti = 0; ti < p.nti; ++ti) tiles += symmetric ? std::max(0, p.ntj - ti / 2) : p.ntj;
     p.units = tiles * p.nchunk;
+    p.ntiles = tiles;
     cudaError_t e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) {
         set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
     }
     const int64_t grid = p.units < num_sms() ? p.units : num_sms();
+    p.win = (int)grid;
+    st = gate_counter((cudaStream_t)stream, &p.gate);
+    if (st != LAMQ_OK) return st;
     xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
     LAMQ_CHECK_LAUNCH("lamq_xtx_accumulate");
     return LAMQ_OK;
