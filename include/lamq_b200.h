@@ -16,8 +16,9 @@
  *   lamq_rht_rows,         opgraph/codes.py:97-132    rht(n, seed) applied as X = W·R_inᵀ (:430), Hr = R_in·H·R_inᵀ
  *   lamq_transpose_f64                                (:439) and W_q = (S⊙V)·R_in, without forming R
  *   lamq_env_factor        opgraph/frame.py:515-522   Environment(H, damp): dead inputs, damping, U
- *   lamq_cholesky_inverse_lower, lamq_ridge, lamq_dgemm
+ *   lamq_cholesky_inverse_lower, lamq_ridge, lamq_dgemm, lamq_cross_apply
  *                          quantize.py:1330-1335      cross_target: M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ
+ *                          quantize.py:1503           target = W @ M
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -167,6 +168,21 @@ int lamq_cholesky_inverse_lower(double *A, int64_t lda, int n, void *workspace, 
  */
 int lamq_env_factor(const double *H, int64_t ldh, int n, double damp, double *U, int64_t ldu, uint8_t *dead,
                     void *workspace, size_t workspace_bytes, int *status, lamq_stream_t stream);
+
+/* Workspace bytes for lamq_cross_apply over `rows` rows of order n. */
+size_t lamq_cross_apply_workspace_size(int rows, int n);
+
+/*
+ * The QEP target W·M of quantize.py:1330-1335 and :1503 without forming M:
+ *   out = W + alpha·((W·D)·Linvᵀ)·Linv,   M = I + alpha·D·(Linvᵀ·Linv) = I + alpha·(solve(A, Dᵀ))ᵀ,
+ * with Linv the inverse of the lower Cholesky factor of A = H + λ·mean(diag H)·I, lower triangular with a zero strict
+ * upper part as lamq_cholesky_inverse_lower leaves it (the two triangular products skip its zero blocks and cost
+ * half a GEMM each). W is rows x n; with W = NULL it is the identity (rows must equal n) and out = M. out may not
+ * alias W or D.
+ */
+int lamq_cross_apply(const double *W, int64_t ldw, int rows, int n, const double *D, int64_t ldd, const double *Linv,
+                     int64_t ldl, double alpha, double *out, int64_t ldo, void *workspace, size_t workspace_bytes,
+                     lamq_stream_t stream);
 
 /* A = H + lam·mean(diag H)·I (quantize.py:1334). */
 int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, int n, double lam, lamq_stream_t stream);

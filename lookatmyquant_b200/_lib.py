@@ -37,6 +37,8 @@ SIGNATURES = {
     "lamq_cholesky_inverse_lower": (_I32, [_P, _I64, _I32, _P, _SZ, _P, _P]),
     "lamq_env_factor": (_I32, [_P, _I64, _I32, _D, _P, _I64, _P, _P, _SZ, _P, _P]),
     "lamq_ridge": (_I32, [_P, _I64, _P, _I64, _I32, _D, _P]),
+    "lamq_cross_apply_workspace_size": (_SZ, [_I32, _I32]),
+    "lamq_cross_apply": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _D, _P, _I64, _P, _SZ, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),

@@ -225,6 +225,15 @@ __global__ void copy_block_kernel(const double *src, int64_t lds, double *dst, i
     }
 }
 
+// The n x n identity.
+__global__ void identity_kernel(double *A, int64_t lda, int n) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)n * n;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e / n), c = (int)(e % n);
+        A[(int64_t)r * lda + c] = (r == c) ? 1.0 : 0.0;
+    }
+}
+
 // Zero the strict upper triangle of an n x n matrix.
 __global__ void zero_upper_kernel(double *A, int64_t lda, int n) {
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)n * n;
@@ -408,6 +417,45 @@ extern "C" int lamq_env_factor(const double *H, int64_t ldh, int n, double damp,
     flip_kernel<<<grid_for((int64_t)n * n), 256, 0, s>>>(X, n, U, ldu, n);
     LAMQ_CHECK_LAUNCH("lamq_env_factor flip back");
     return LAMQ_OK;
+}
+
+extern "C" size_t lamq_cross_apply_workspace_size(int rows, int n) {
+    if (rows <= 0 || n <= 0) return 0;
+    return 2 * (size_t)rows * n * sizeof(double);
+}
+
+extern "C" int lamq_cross_apply(const double *W, int64_t ldw, int rows, int n, const double *D, int64_t ldd,
+                                const double *Linv, int64_t ldl, double alpha, double *out, int64_t ldo,
+                                void *workspace, size_t workspace_bytes, lamq_stream_t stream) {
+    LAMQ_REQUIRE(rows >= 0 && n >= 0 && ldd >= n && ldl >= n && ldo >= n && (W == nullptr || ldw >= n),
+                 "lamq_cross_apply: bad shape");
+    LAMQ_REQUIRE(W != nullptr || rows == n, "lamq_cross_apply: W = NULL (the identity) needs rows == n");
+    if (rows == 0 || n == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(D && Linv && out && workspace, "lamq_cross_apply: null pointer");
+    LAMQ_REQUIRE(out != W && out != D, "lamq_cross_apply: out aliases an input");
+    LAMQ_REQUIRE(workspace_bytes >= lamq_cross_apply_workspace_size(rows, n), "lamq_cross_apply: workspace too small");
+    cudaStream_t s = (cudaStream_t)stream;
+    double *P = reinterpret_cast<double *>(workspace);  // W·D
+    double *P2 = P + (size_t)rows * n;                  // (W·D)·Linvᵀ
+    const double *Pin = D;
+    int64_t ldp = ldd;
+    int st;
+    if (W != nullptr) {
+        st = dgemm(s, 0, rows, n, n, 1.0, W, ldw, D, ldd, 0.0, P, n);
+        if (st) return st;
+        Pin = P;
+        ldp = n;
+        copy_block_kernel<<<grid_for((int64_t)rows * n), 256, 0, s>>>(W, ldw, out, ldo, rows, n);
+        LAMQ_CHECK_LAUNCH("lamq_cross_apply copy");
+    } else {
+        identity_kernel<<<grid_for((int64_t)n * n), 256, 0, s>>>(out, ldo, n);
+        LAMQ_CHECK_LAUNCH("lamq_cross_apply identity");
+    }
+    // P2 = P·Linvᵀ: the stored B (Linv) is lower, so NT skips k > column
+    st = dgemm(s, 1, rows, n, n, 1.0, Pin, ldp, Linv, ldl, 0.0, P2, n, 0, 0, 1);
+    if (st) return st;
+    // out += alpha·P2·Linv: NN with a lower B skips k < column
+    return dgemm(s, 0, rows, n, n, alpha, P2, n, Linv, ldl, 1.0, out, ldo, 0, 0, 1);
 }
 
 extern "C" int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, int n, double lam,

@@ -93,8 +93,8 @@ def ridge(H: torch.Tensor, lam: float) -> torch.Tensor:
 
 class CrossTarget:
     """The QEP map of quantize.py:1330-1335 for one stage: `apply(W)` = W·M with M = I + α·(solve(H + λ·mean(diag H)·I,
-    Dᵀ))ᵀ = I + α·D·(H + λμI)⁻¹. With `rows` (the rows the stage will map) above n, M is formed once; otherwise each
-    W is mapped as W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹."""
+    Dᵀ))ᵀ = I + α·D·(H + λμI)⁻¹ (lamq_cross_apply). With `rows` (the rows the stage will map) above n, M is formed
+    once; otherwise each W is mapped as W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹."""
 
     def __init__(self, H, D, alpha: float, lam: float, rows: int | None = None):
         n = H.shape[0]
@@ -103,9 +103,7 @@ class CrossTarget:
         self.D = _f64(D)
         self.M = None
         if rows is None or rows > n:
-            P = gemm(self.D, self.Linv, transB=True)
-            M = torch.eye(n, dtype=torch.float64, device=H.device)
-            self.M = gemm(P, self.Linv, C=M, alpha=alpha, beta=1.0)
+            self.M = self._apply(None, n)
 
     def record_stream(self, stream):
         """Marks the map's tensors as used on `stream` (they were made on another stream)."""
@@ -113,10 +111,20 @@ class CrossTarget:
             if t is not None:
                 t.record_stream(stream)
 
+    def _apply(self, W, rows):
+        n = self.D.shape[0]
+        dev = self.D.device
+        lib = _lib.load()
+        out = torch.empty(rows, n, dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.lamq_cross_apply_workspace_size(rows, n), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            check(lib.lamq_cross_apply(ptr(W), 0 if W is None else W.stride(0), rows, n, ptr(self.D),
+                                       self.D.stride(0), ptr(self.Linv), self.Linv.stride(0), float(self.alpha),
+                                       ptr(out), n, ptr(ws), ws.numel(), stream_ptr(dev)), "lamq_cross_apply")
+        return out
+
     def apply(self, W: torch.Tensor) -> torch.Tensor:
         W = _f64(W)
         if self.M is not None:
             return gemm(W, self.M)
-        P = gemm(W, self.D)
-        P2 = gemm(P, self.Linv, transB=True)
-        return gemm(P2, self.Linv, C=W.clone(), alpha=self.alpha, beta=1.0)
+        return self._apply(W, W.shape[0])

@@ -31,7 +31,7 @@ def test_gemm(M, N, K, transB):
     assert np.abs(got - ref).max() < 1e-12 * np.abs(ref).max() * np.sqrt(K)
 
 
-@pytest.mark.parametrize("n", [1, 100, 128, 300, 1024, 2560])
+@pytest.mark.parametrize("n", [1, 33, 65, 100, 128, 300, 1024, 2560])
 def test_cholesky_inverse(n):
     from lookatmyquant_b200.linalg import cholesky_inverse_lower
     H = spd(n, n) + 0.01 * np.eye(n)
@@ -67,7 +67,7 @@ def test_not_positive_definite_raises():
         cholesky_inverse_lower(torch.as_tensor(H).cuda())
 
 
-@pytest.mark.parametrize("n,rows", [(256, 1000), (512, 100)])
+@pytest.mark.parametrize("n,rows", [(256, 1000), (512, 100), (300, 77), (200, 500)])
 def test_cross_target(n, rows):
     from lookatmyquant_b200.linalg import CrossTarget
     H = spd(n, 7)
