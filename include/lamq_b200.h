@@ -19,6 +19,10 @@
  *   lamq_cholesky_inverse_lower, lamq_ridge, lamq_dgemm, lamq_cross_apply
  *                          quantize.py:1330-1335      cross_target: M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ
  *                          quantize.py:1503           target = W @ M
+ *   lamq_pack_trellis,     compiler_artifact.py:225-297  pack_trellis / unpack_trellis (valid_path checked on pack)
+ *   lamq_unpack_trellis
+ *   lamq_decode_trellis    compiler_artifact.py:433-442  decode_rotated: table[state]·scale per group row
+ *   lamq_trellis_product   runtime_mlx/fast_q35.py:69-172 the product kernel: y = S ⊙ (V[state]·(R_in x)) per group
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -186,6 +190,41 @@ int lamq_cross_apply(const double *W, int64_t ldw, int rows, int n, const double
 
 /* A = H + lam·mean(diag H)·I (quantize.py:1334). */
 int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, int n, double lam, lamq_stream_t stream);
+
+/*
+ * Packed trellis rows (opgraph-packed-1, compiler_artifact.py:225-297). A row of n states (L-bit states, k-bit
+ * symbols, 1 <= k <= 8, k < L <= 12) is stored as the symbols state & (2^k − 1), padded forward with zeros to a
+ * multiple of 32 columns, reversed, and packed little-endian k bits each: lamq_trellis_words_per_row(n, k) = ⌈n/32⌉·k
+ * uint32 words per row, rows back to back.
+ */
+int64_t lamq_trellis_words_per_row(int n, int k);
+
+/*
+ * pack_trellis (compiler_artifact.py:276-284) of rows x n int16 states. status (device int, 0 on entry) becomes
+ * LAMQ_ERR_NOT_PATH when a row is not a trellis path from state 0 (valid_path, :261-267); the words are written anyway.
+ */
+int lamq_pack_trellis(const int16_t *states, int64_t lds, int64_t rows, int n, int k, int L, uint32_t *codes,
+                      int *status, lamq_stream_t stream);
+
+/* unpack_trellis (compiler_artifact.py:287-297): the int16 states of packed rows. */
+int lamq_unpack_trellis(const uint32_t *codes, int64_t rows, int n, int k, int L, int16_t *states, int64_t lds,
+                        lamq_stream_t stream);
+
+/*
+ * decode_rotated (compiler_artifact.py:433-442) for one row group: out[map[r]][j] = table[state_rj]·scales[r] in fp32
+ * (map NULL: row r). table has 2^L fp32 entries, scales one fp32 per group row.
+ */
+int lamq_decode_trellis(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales,
+                        const float *table, const uint32_t *map, float *out, int64_t ldo, lamq_stream_t stream);
+
+/*
+ * The product of one packed row group with nvec input vectors (runtime_mlx/fast_q35.py:69-172):
+ * y[v][map[r]] = scales[r]·Σ_j table[state_rj]·x[v][j], fp32. x (nvec x n, leading dimension ldx) is the input
+ * after the group's input rotation R_in; y rows have leading dimension ldy.
+ */
+int lamq_trellis_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales,
+                         const float *table, const uint32_t *map, const float *x, int64_t ldx, int nvec, float *y,
+                         int64_t ldy, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

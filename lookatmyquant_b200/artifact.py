@@ -1,0 +1,216 @@
+"""Packed trellis rows on B200: the opgraph-packed-1 trellis encoding and the product with packed rows
+(liblamq_b200: lamq_pack_trellis, lamq_unpack_trellis, lamq_decode_trellis, lamq_trellis_product).
+
+Reference (ShinMegamiBoson/lookatmyquant):
+  valid_path, pack_trellis, unpack_trellis      compiler_artifact.py:261-297
+  _input_signs                                  compiler_artifact.py:300-304
+  encode_entry (state-based row-group entries)  compiler_artifact.py:307-360, grouped_matrix_specs :143-167
+  decode_rotated                                compiler_artifact.py:433-442
+  the product y = S ⊙ (V[state]·(R_in x))       runtime_mlx/fast_q35.py:69-172 (Metal there)
+
+Tensors live on the device; uint32 words and row maps are held in int32 tensors (the same bits). Invalid input raises
+the reference's ValueError messages. There is no host fallback: every entry point runs in liblamq_b200.so.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, ptr, stream_ptr
+from .rotation import Rotation
+
+TABLE_ENTRIES = 4096
+STATE_BITS = 12
+DENSE_PRODUCT_VECTORS = 64  # from this many input vectors on, a group is decoded once and multiplied densely
+
+
+def _dev(t: torch.Tensor) -> torch.device:
+    if not t.is_cuda:
+        raise RuntimeError("packed trellis tensors must be on a CUDA device")
+    return t.device
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    """uint32 words or row ids held as int32 (the same bits)."""
+    if t.dtype in (torch.int32,):
+        return t.contiguous()
+    if hasattr(torch, "uint32") and t.dtype == torch.uint32:
+        return t.contiguous().view(torch.int32)
+    return t.to(torch.int64).to(torch.int32).contiguous()
+
+
+def words_per_row(columns: int, bits: int) -> int:
+    return int(_lib.load().lamq_trellis_words_per_row(columns, bits))
+
+
+def pack_trellis(states: torch.Tensor, bits: int, state_bits: int = STATE_BITS) -> torch.Tensor:
+    """compiler_artifact.pack_trellis: rows x n states (a trellis path from state 0 per row) → rows x ⌈n/32⌉·bits
+    words (int32 holding uint32)."""
+    dev = _dev(states)
+    if states.ndim != 2 or states.shape[1] == 0:
+        raise ValueError("states are not a row trellis from zero")
+    st = states.to(torch.int16) if states.dtype != torch.int16 else states
+    if bool(((states < 0) | (states >= 1 << state_bits)).any()):
+        raise ValueError("states are not a row trellis from zero")
+    st = st.contiguous()
+    rows, n = st.shape
+    codes = torch.empty(rows, words_per_row(n, bits), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        check(_lib.load().lamq_pack_trellis(ptr(st), st.stride(0), rows, n, bits, state_bits, ptr(codes), ptr(status),
+                                            stream_ptr(dev)), "lamq_pack_trellis")
+    if int(status.item()) == _lib.LAMQ_ERR_NOT_PATH:
+        raise ValueError("states are not a row trellis from zero")
+    return codes
+
+
+def unpack_trellis(codes: torch.Tensor, bits: int, columns: int, state_bits: int = STATE_BITS) -> torch.Tensor:
+    """compiler_artifact.unpack_trellis: the rows x columns states (int16) of packed rows."""
+    dev = _dev(codes)
+    codes = _i32(codes)
+    rows = codes.shape[0]
+    if codes.shape != (rows, words_per_row(columns, bits)):
+        raise ValueError("code dimensions disagree with width")
+    out = torch.empty(rows, columns, dtype=torch.int16, device=dev)
+    with torch.cuda.device(dev):
+        check(_lib.load().lamq_unpack_trellis(ptr(codes), rows, columns, bits, state_bits, ptr(out), columns,
+                                              stream_ptr(dev)), "lamq_unpack_trellis")
+    return out
+
+
+def input_signs(columns: int, seed: int) -> torch.Tensor:
+    """compiler_artifact._input_signs: int8 ±1 from torch's CPU generator (the quantizer's exact definition)."""
+    u = torch.rand(columns, generator=torch.Generator().manual_seed(int(seed)), dtype=torch.float64)
+    return torch.where(u < 0.5, -1, 1).to(torch.int8)
+
+
+def grouped_matrix_meta(name: str, shape, groups, state_bits: int = STATE_BITS) -> dict:
+    """The matrix metadata of compiler_artifact.grouped_matrix_specs for trellis row groups."""
+    rows, columns = map(int, shape)
+    if sum(int(g["rows"]) for g in groups) != rows:
+        raise ValueError("groups must cover the matrix")
+    records = []
+    for i, g in enumerate(groups):
+        m, bits = int(g["rows"]), int(g["bits"])
+        if m <= 0 or not 1 <= bits <= 8:
+            raise ValueError("empty group or unsupported width")
+        records.append({"key": f"{name}.g{i}", "kind": "trellis", "bits": bits, "rows": m, "columns": columns,
+                        "padded_columns": (columns + 31) // 32 * 32, "state_bits": state_bits, "start_state": 0})
+    return {"kind": "grouped", "shape": [rows, columns], "signs": name + ".signs", "groups": records}
+
+
+def encode_entry(name: str, entry: dict, signs: torch.Tensor | None = None):
+    """compiler_artifact.encode_entry for a state-based row-group entry (quantize_row_groups' saved form: states with
+    4096·table_index offsets, fp32 scales, in_seed, concatenated fp32 tables, row_groups). Returns (tensors, meta) with
+    the packed codes computed on the device."""
+    states = entry["states"]
+    if states.ndim != 2:
+        raise ValueError("saved entry must be a matrix")
+    dev = _dev(states)
+    m, n = states.shape
+    scales = entry["scales"].to(dev)
+    if scales.shape != (m,) or scales.dtype != torch.float32:
+        raise ValueError("saved row scales must be fp32, one per row")
+    if not bool(torch.isfinite(scales).all()):
+        raise ValueError("nonfinite row scales")
+    table = entry["table"].to(dev)
+    if table.ndim != 1 or table.dtype != torch.float32 or not bool(torch.isfinite(table).all()):
+        raise ValueError("saved table must be a finite fp32 vector")
+    signs = input_signs(n, entry["in_seed"]) if signs is None else signs.to(torch.int8).cpu()
+    if signs.shape != (n,) or not bool(((signs == 1) | (signs == -1)).all()):
+        raise ValueError("invalid input signs")
+    enc = states.to(torch.int64)
+    if table.numel() % TABLE_ENTRIES or bool((enc < 0).any()) or bool((enc >= table.numel()).any()):
+        raise ValueError("invalid saved trellis table or states")
+    group_ids = enc[:, 0] // TABLE_ENTRIES
+    if not bool((enc // TABLE_ENTRIES == group_ids[:, None]).all()):
+        raise ValueError("a row crosses table identities")
+    if entry.get("row_groups") is None:
+        raise ValueError("state-based entries without row_groups: save explicit row_groups metadata")
+    tensors = {name + ".signs": signs}
+    descriptors, covered = [], []
+    for i, g in enumerate(entry["row_groups"]):
+        rows = torch.as_tensor(g["rows"], dtype=torch.int64).to(dev)
+        bits, ti = int(g["bits"]), int(g["table_index"])
+        if rows.ndim != 1 or bool((rows < 0).any()) or bool((rows >= m).any()) or not bool((group_ids[rows] == ti).all()):
+            raise ValueError("invalid row group")
+        key = f"{name}.g{i}"
+        tensors.update({key + ".rows": rows.to(torch.int32), key + ".codes": pack_trellis(enc[rows] - ti * TABLE_ENTRIES, bits),
+                        key + ".scales": scales[rows].contiguous(),
+                        key + ".table": table[ti * TABLE_ENTRIES:(ti + 1) * TABLE_ENTRIES].contiguous()})
+        descriptors.append({"rows": int(rows.numel()), "bits": bits})
+        covered.append(rows)
+    if not torch.equal(torch.cat(covered).sort().values, torch.arange(m, device=dev)):
+        raise ValueError("row groups must cover every row exactly once")
+    return tensors, grouped_matrix_meta(name, [m, n], descriptors)
+
+
+def decode_rotated(tensors: dict, meta: dict) -> torch.Tensor:
+    """compiler_artifact.decode_rotated for trellis groups: the fp32 table·scale values before the input transform."""
+    m, n = meta["shape"]
+    dev = _dev(tensors[meta["groups"][0]["key"] + ".codes"])
+    out = torch.empty(m, n, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    for g in meta["groups"]:
+        if g["kind"] != "trellis":
+            raise NotImplementedError("scalar groups are not part of the trellis path")
+        key = g["key"]
+        codes, rows = _i32(tensors[key + ".codes"]), _i32(tensors[key + ".rows"])
+        scales, table = tensors[key + ".scales"].contiguous(), tensors[key + ".table"].contiguous()
+        with torch.cuda.device(dev):
+            check(lib.lamq_decode_trellis(ptr(codes), rows.numel(), n, g["bits"], g["state_bits"], ptr(scales),
+                                          ptr(table), ptr(rows), ptr(out), n, stream_ptr(dev)), "lamq_decode_trellis")
+    return out
+
+
+class TrellisProduct:
+    """y = W·x for a packed grouped matrix, W = diag(S)·V[state]·R_in (the product of runtime_mlx/fast_q35.py):
+    x is rotated once (R_in x, fp64 through the Kronecker factors, then fp32) and every row group multiplies its packed
+    rows with it (lamq_trellis_product). With DENSE_PRODUCT_VECTORS or more vectors, each group is decoded once into
+    bf16 and the product runs as a dense bf16 GEMM with fp32 accumulation."""
+
+    def __init__(self, tensors: dict, meta: dict, device=None):
+        self.meta = meta
+        self.m, self.n = meta["shape"]
+        self.device = torch.device(device or "cuda")
+        self.rot = Rotation.from_signs(tensors[meta["signs"]].to(torch.float64), self.device)
+        self.groups = []
+        for g in meta["groups"]:
+            key = g["key"]
+            self.groups.append((g, _i32(tensors[key + ".codes"]).to(self.device),
+                                _i32(tensors[key + ".rows"]).to(self.device),
+                                tensors[key + ".scales"].to(self.device).contiguous(),
+                                tensors[key + ".table"].to(self.device).contiguous()))
+        self._dense = None
+
+    def rotate(self, x: torch.Tensor) -> torch.Tensor:
+        """R_in x for each row of x (nvec x n), fp32."""
+        return self.rot.rows(x.to(self.device, torch.float64).contiguous()).to(torch.float32)
+
+    def dense_rotated(self) -> torch.Tensor:
+        """decode_rotated as bf16 (cached): V[state]·S before the input transform."""
+        if self._dense is None:
+            tensors = {}
+            for g, codes, rows, scales, table in self.groups:
+                tensors.update({g["key"] + ".codes": codes, g["key"] + ".rows": rows, g["key"] + ".scales": scales,
+                                g["key"] + ".table": table})
+            self._dense = decode_rotated(tensors, self.meta).to(torch.bfloat16)
+        return self._dense
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        squeeze = x.ndim == 1
+        x = x.reshape(-1, self.n)
+        xr = self.rotate(x)
+        nvec = xr.shape[0]
+        if nvec >= DENSE_PRODUCT_VECTORS:
+            y = (xr.to(torch.bfloat16) @ self.dense_rotated().T).float()
+            return y[0] if squeeze else y
+        y = torch.empty(nvec, self.m, dtype=torch.float32, device=self.device)
+        lib = _lib.load()
+        for g, codes, rows, scales, table in self.groups:
+            with torch.cuda.device(self.device):
+                check(lib.lamq_trellis_product(ptr(codes), rows.numel(), self.n, g["bits"], g["state_bits"],
+                                               ptr(scales), ptr(table), ptr(rows), ptr(xr), xr.stride(0), nvec,
+                                               ptr(y), y.stride(0), stream_ptr(self.device)), "lamq_trellis_product")
+        return y[0] if squeeze else y

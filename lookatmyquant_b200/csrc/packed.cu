@@ -1,0 +1,233 @@
+// The packed trellis format of opgraph-packed-1 on the device: packing int16 states into the reversed k-bit stream,
+// unpacking, decoding rows to weights, and the product of packed rows with input vectors.
+//
+// Reference: compiler_artifact.py:225-297 (`pack_symbols`, `unpack_symbols`, `valid_path`, `pack_trellis`,
+// `unpack_trellis`), :433-442 (`decode_rotated`), and the product kernel of runtime_mlx/fast_q35.py:69-172.
+//
+// Format. A row of n states with k-bit symbols is padded forward to N = 32·⌈n/32⌉ columns (zero symbols after the
+// last real column) and reversed, so symbol p of the stream is the symbol of column N − 1 − p. Symbol p occupies bits
+// [p·k, p·k + k) of the row's little-endian bit stream of N·k bits = N/32·k uint32 words. A trellis path from state 0
+// has state_j = the L bits of the stream at bit (N − 1 − j)·k (bits past the end read as zero), so every state is
+// read straight from the stream, without a walk along the row.
+#include <algorithm>
+
+#include "lamq_common.cuh"
+
+namespace lamq {
+namespace {
+
+__device__ __forceinline__ uint32_t stream_bits(const uint32_t *__restrict__ row, int wpr, int64_t bit, int width) {
+    const int64_t w = bit >> 5;
+    const int off = (int)(bit & 31);
+    const uint32_t lo = (w < wpr) ? __ldg(row + w) : 0u;
+    const uint32_t hi = (w + 1 < wpr) ? __ldg(row + w + 1) : 0u;
+    const uint64_t v = ((uint64_t)hi << 32 | lo) >> off;
+    return (uint32_t)v & ((1u << width) - 1u);
+}
+
+// One thread per output word: gathers the symbols that overlap bits [32w, 32w + 32) of row r and checks the path at
+// the columns of those symbols (compiler_artifact.py:261-267).
+__global__ void pack_trellis_kernel(const int16_t *__restrict__ states, int64_t lds, int64_t rows, int n, int k, int L,
+                                    uint32_t *__restrict__ codes, int *status) {
+    const int N = (n + 31) / 32 * 32;
+    const int wpr = N / 32 * k;
+    const int64_t total = rows * wpr;
+    const uint32_t kmask = (1u << k) - 1u, tail = (1u << (L - k)) - 1u;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / wpr;
+        const int w = (int)(e % wpr);
+        const int16_t *srow = states + r * lds;
+        uint32_t word = 0;
+        bool bad = false;
+        const int p0 = (32 * w) / k, p1 = (32 * w + 31) / k;
+        for (int p = p0; p <= p1; ++p) {
+            const int j = N - 1 - p;
+            uint32_t sym = 0;
+            if (j < n) {
+                const int s = srow[j];
+                if (s < 0 || s >= (1 << L)) bad = true;
+                if (j == 0) {
+                    if (s >= (1 << k)) bad = true;
+                } else {
+                    const int prev = srow[j - 1];
+                    if (((uint32_t)s >> k) != ((uint32_t)prev & tail)) bad = true;
+                }
+                sym = (uint32_t)s & kmask;
+            }
+            const int shift = p * k - 32 * w;
+            word |= shift >= 0 ? (sym << shift) : (sym >> -shift);
+        }
+        codes[e] = word;
+        if (bad) atomicCAS(status, 0, LAMQ_ERR_NOT_PATH);
+    }
+}
+
+// state_j of every (row, column); with `table`, out = table[state]·scale[r] (fp32, compiler_artifact.py:440) at row
+// map[r] (or r), else the states as int16.
+__global__ void unpack_trellis_kernel(const uint32_t *__restrict__ codes, int64_t rows, int n, int k, int L,
+                                      int16_t *__restrict__ states, int64_t lds, const float *__restrict__ table,
+                                      const float *__restrict__ scales, const uint32_t *__restrict__ map,
+                                      float *__restrict__ out, int64_t ldo) {
+    const int N = (n + 31) / 32 * 32;
+    const int wpr = N / 32 * k;
+    const int64_t total = rows * n;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / n;
+        const int j = (int)(e % n);
+        const uint32_t s = stream_bits(codes + r * wpr, wpr, (int64_t)(N - 1 - j) * k, L);
+        if (table == nullptr) {
+            states[r * lds + j] = (int16_t)s;
+        } else {
+            const int64_t orow = map ? (int64_t)map[r] : r;
+            out[orow * ldo + j] = __fmul_rn(__ldg(table + s), __ldg(scales + r));
+        }
+    }
+}
+
+// y[v][map[r]] = scale[r] · Σ_j table[state_rj] · x[v][j] for NV input vectors. A warp takes kRowsPerWarp rows at a
+// time and walks their columns 32 at a time (lane = column): each lane reads the one or two stream words that hold its
+// column's state (the warp's 32 columns share k + 1 words, which L1 serves), looks the value up in the table (shared
+// memory), and multiplies it into the NV vectors' sums; x values are reused across the rows.
+constexpr int kRowsPerWarp = 4;
+constexpr int kProductWarps = 8;
+
+template <int NV>
+__global__ void __launch_bounds__(kProductWarps * 32) trellis_product_kernel(
+    const uint32_t *__restrict__ codes, int64_t rows, int n, int k, int L, const float *__restrict__ scales,
+    const float *__restrict__ table, const uint32_t *__restrict__ map, const float *__restrict__ x, int64_t ldx,
+    float *__restrict__ y, int64_t ldy) {
+    __shared__ float tab[4096];
+    const int nt = 1 << L;
+    for (int i = threadIdx.x; i < nt; i += blockDim.x) tab[i] = table[i];
+    __syncthreads();
+    const int N = (n + 31) / 32 * 32;
+    const int wpr = N / 32 * k;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t groups = (rows + kRowsPerWarp - 1) / kRowsPerWarp;
+    for (int64_t g = (int64_t)blockIdx.x * kProductWarps + warp; g < groups; g += (int64_t)gridDim.x * kProductWarps) {
+        const int64_t r0 = g * kRowsPerWarp;
+        float acc[kRowsPerWarp][NV];
+#pragma unroll
+        for (int a = 0; a < kRowsPerWarp; ++a)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+            const int j = j0 + lane;
+            if (j < n) {
+                float val[kRowsPerWarp];
+#pragma unroll
+                for (int a = 0; a < kRowsPerWarp; ++a) {
+                    const int64_t r = min(r0 + a, rows - 1);
+                    val[a] = tab[stream_bits(codes + r * wpr, wpr, (int64_t)(N - 1 - j) * k, L)];
+                }
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    const float xv = __ldg(x + (int64_t)v * ldx + j);
+#pragma unroll
+                    for (int a = 0; a < kRowsPerWarp; ++a) acc[a][v] = fmaf(val[a], xv, acc[a][v]);
+                }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < kRowsPerWarp; ++a) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                float s = acc[a][v];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                acc[a][v] = s;
+            }
+            const int64_t r = r0 + a;
+            if (lane == 0 && r < rows) {
+                const int64_t orow = map ? (int64_t)map[r] : r;
+                const float sc = scales[r];
+#pragma unroll
+                for (int v = 0; v < NV; ++v) y[(int64_t)v * ldy + orow] = acc[a][v] * sc;
+            }
+        }
+    }
+}
+
+int grid_for(int64_t work, int threads) {
+    return (int)std::min<int64_t>((work + threads - 1) / threads, 148 * 32);
+}
+
+template <int NV>
+void launch_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales, const float *table,
+                    const uint32_t *map, const float *x, int64_t ldx, float *y, int64_t ldy, cudaStream_t s) {
+    const int64_t groups = (rows + kRowsPerWarp - 1) / kRowsPerWarp;
+    const int grid = (int)std::min<int64_t>((groups + kProductWarps - 1) / kProductWarps, 148 * 8);
+    trellis_product_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, k, L, scales, table, map, x, ldx, y,
+                                                                   ldy);
+}
+
+}  // namespace
+}  // namespace lamq
+
+using namespace lamq;
+
+// Symbols of 1-8 bits (pack_symbols' range) and states of more bits than a symbol, at most 12 (a table of <= 4096).
+#define LAMQ_CHECK_FORMAT(fn)                                                                                   \
+    LAMQ_REQUIRE(rows >= 0 && n > 0, fn ": bad shape");                                                         \
+    LAMQ_REQUIRE(k >= 1 && k <= 8 && L > k && L <= 12, fn ": unsupported widths (k %d, L %d)", k, L)
+
+extern "C" int64_t lamq_trellis_words_per_row(int n, int k) { return n <= 0 || k <= 0 ? 0 : (int64_t)(n + 31) / 32 * k; }
+
+extern "C" int lamq_pack_trellis(const int16_t *states, int64_t lds, int64_t rows, int n, int k, int L, uint32_t *codes,
+                                 int *status, lamq_stream_t stream) {
+    LAMQ_CHECK_FORMAT("lamq_pack_trellis");
+    LAMQ_REQUIRE(lds >= n, "lamq_pack_trellis: leading dimension below n");
+    if (rows == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(states && codes && status, "lamq_pack_trellis: null pointer");
+    const int64_t work = rows * lamq_trellis_words_per_row(n, k);
+    pack_trellis_kernel<<<grid_for(work, 256), 256, 0, (cudaStream_t)stream>>>(states, lds, rows, n, k, L, codes, status);
+    LAMQ_CHECK_LAUNCH("lamq_pack_trellis");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_unpack_trellis(const uint32_t *codes, int64_t rows, int n, int k, int L, int16_t *states,
+                                   int64_t lds, lamq_stream_t stream) {
+    LAMQ_CHECK_FORMAT("lamq_unpack_trellis");
+    LAMQ_REQUIRE(lds >= n, "lamq_unpack_trellis: leading dimension below n");
+    if (rows == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(codes && states, "lamq_unpack_trellis: null pointer");
+    unpack_trellis_kernel<<<grid_for(rows * n, 256), 256, 0, (cudaStream_t)stream>>>(
+        codes, rows, n, k, L, states, lds, nullptr, nullptr, nullptr, nullptr, 0);
+    LAMQ_CHECK_LAUNCH("lamq_unpack_trellis");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_decode_trellis(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales,
+                                   const float *table, const uint32_t *map, float *out, int64_t ldo,
+                                   lamq_stream_t stream) {
+    LAMQ_CHECK_FORMAT("lamq_decode_trellis");
+    LAMQ_REQUIRE(ldo >= n, "lamq_decode_trellis: leading dimension below n");
+    if (rows == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(codes && scales && table && out, "lamq_decode_trellis: null pointer");
+    unpack_trellis_kernel<<<grid_for(rows * n, 256), 256, 0, (cudaStream_t)stream>>>(
+        codes, rows, n, k, L, nullptr, 0, table, scales, map, out, ldo);
+    LAMQ_CHECK_LAUNCH("lamq_decode_trellis");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_trellis_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales,
+                                    const float *table, const uint32_t *map, const float *x, int64_t ldx, int nvec,
+                                    float *y, int64_t ldy, lamq_stream_t stream) {
+    LAMQ_CHECK_FORMAT("lamq_trellis_product");
+    LAMQ_REQUIRE(nvec >= 0 && ldx >= n, "lamq_trellis_product: bad vector shape");
+    if (rows == 0 || nvec == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(codes && scales && table && x && y, "lamq_trellis_product: null pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    for (int v = 0; v < nvec;) {
+        const int left = nvec - v;
+        const float *xv = x + (int64_t)v * ldx;
+        float *yv = y + (int64_t)v * ldy;
+        if (left >= 16) launch_product<16>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 16;
+        else if (left >= 8) launch_product<8>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 8;
+        else if (left >= 4) launch_product<4>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 4;
+        else if (left >= 2) launch_product<2>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 2;
+        else launch_product<1>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 1;
+        LAMQ_CHECK_LAUNCH("lamq_trellis_product");
+    }
+    return LAMQ_OK;
+}

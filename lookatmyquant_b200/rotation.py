@@ -41,6 +41,14 @@ class Rotation:
         self.Abits, self.Bbits = _sign_bits(A).to(dev), _sign_bits(B).to(dev)
         self.Atbits, self.Btbits = _sign_bits(A.T.contiguous()).to(dev), _sign_bits(B.T.contiguous()).to(dev)
 
+    @classmethod
+    def from_signs(cls, signs: torch.Tensor, device=None) -> "Rotation":
+        """The rotation of a stored `.signs` vector (±1, compiler_artifact.py:300-304) instead of a seed."""
+        rot = cls(int(signs.numel()), 0, device)
+        rot.seed = None
+        rot.signs = signs.reshape(-1).to(rot.device, torch.float64)
+        return rot
+
     def _run(self, M, out, transpose: bool):
         if M.dtype != torch.float64 or not M.is_cuda:
             raise TypeError("rotations run on fp64 CUDA tensors")

@@ -384,3 +384,13 @@ def unpack_trellis(codes, bits: int, columns: int, state_bits: int = 12) -> np.n
         state = ((state << bits) | sym[:, i]) & mask
         out[:, i] = state
     return out
+
+
+def decode_rotated_groups(groups, shape, columns: int, state_bits: int = 12) -> np.ndarray:
+    """compiler_artifact.py:433-442 for trellis groups: groups = [(rows, codes, bits, scales, table)] → fp32 table·scale
+    values (before the input transform)."""
+    out = np.empty(shape, dtype=np.float32)
+    for rows, codes, bits, scales, table in groups:
+        idx = unpack_trellis(codes, bits, columns, state_bits)
+        out[np.asarray(rows, dtype=np.int64)] = np.asarray(table, np.float32)[idx] * np.asarray(scales, np.float32)[:, None]
+    return out

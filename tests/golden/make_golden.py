@@ -68,6 +68,7 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", choices=["artifact"], help="write only this fixture (the others stay as committed)")
     args = ap.parse_args()
     C = setup_reference(args.reference.resolve())
     import torch
@@ -75,6 +76,9 @@ def main():
     import compiler_artifact as CA
     from opgraph.frame import Environment
 
+    if args.only == "artifact":
+        write_artifact_fixture(C, Q, CA, torch)
+        return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
     digests = {}
@@ -188,7 +192,36 @@ def main():
            "Wq": net.matrix(dtype=torch.float64).float().numpy(), "settled": net.cores["W"].data.numpy().reshape(m, n),
            "S": net.cores["W.S"].data.numpy()}
     np.savez_compressed(HERE / "column_trellis.npz", **col)
+    write_artifact_fixture(C, Q, CA, torch)
     print("golden vectors written to", HERE)
+
+
+def write_artifact_fixture(C, Q, CA, torch):
+    """7. opgraph-packed-1 (compiler_artifact.py:307-360, :433-442): the reference's own encode_entry of a row-group
+    entry (quantize_row_groups' saved form) and decode_rotated of it, with ragged widths and a row count that is not a
+    multiple of 32."""
+    m, n = 200, 200
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(12), dtype=torch.float64)).float().double()
+    H = calib_H(n, 1024, 43)
+    perm = torch.randperm(m, generator=torch.Generator().manual_seed(13))
+    groups = [{"rows": perm[:40], "bits": 1}, {"rows": perm[40:110], "bits": 2}, {"rows": perm[110:170], "bits": 3},
+              {"rows": perm[170:], "bits": 4}]
+    trellis = {b: C.RowTrellisCode(12, b, T=256, width=16, look=8) for b in (1, 2, 3, 4)}
+    in_seed = 4401
+
+    def round_group(rows, bits):
+        return Q.word(f"tr{bits}x", W[rows], H, 4400, trellis, in_seed, False)
+
+    Wq, rate, entry = Q.quantize_row_groups(W, groups, round_group, in_seed, True)
+    tensors, meta = CA.encode_entry("w", entry)
+    art = {"states": entry["states"].numpy(), "scales": entry["scales"].numpy(), "table": entry["table"].numpy(),
+           "in_seed": np.array(in_seed), "signs": tensors["w.signs"], "decoded": CA.decode_rotated(tensors, meta)}
+    for i in range(len(groups)):
+        art[f"g{i}_rows"] = tensors[f"w.g{i}.rows"]
+        art[f"g{i}_codes"] = tensors[f"w.g{i}.codes"]
+        art[f"g{i}_scales"] = tensors[f"w.g{i}.scales"]
+        art[f"g{i}_bits"] = np.array(meta["groups"][i]["bits"])
+    np.savez_compressed(HERE / "artifact.npz", **art)
 
 
 if __name__ == "__main__":

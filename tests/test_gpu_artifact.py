@@ -1,0 +1,106 @@
+"""Packed trellis rows on the GPU against the reference's own encode_entry / decode_rotated output (tests/golden/
+artifact.npz, made by make_golden.py from compiler_artifact.py) and the oracle's pack_trellis (compiler_artifact.py:
+225-297): bit-exact words, states and decoded values; the product against a dense fp64 product."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.core as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _u32(t):
+    return t.cpu().numpy().view(np.uint32)
+
+
+def _path(rows, n, k, seed, L=12):
+    """Random trellis paths from state 0: each state shifts the previous one by k bits and appends a symbol."""
+    rng = np.random.default_rng(seed)
+    sym = rng.integers(0, 1 << k, size=(rows, n))
+    st = np.zeros((rows, n), dtype=np.int64)
+    s = np.zeros(rows, dtype=np.int64)
+    for j in range(n):
+        s = ((s << k) | sym[:, j]) & ((1 << L) - 1)
+        st[:, j] = s
+    return st
+
+
+def test_pack_unpack_match_reference_groups(golden):
+    from lookatmyquant_b200 import artifact as A
+    g = golden("artifact")
+    for i in range(4):
+        rows, bits = g[f"g{i}_rows"].astype(np.int64), int(g[f"g{i}_bits"])
+        ti = int(g["states"][rows[0], 0]) // 4096
+        states = torch.as_tensor(g["states"][rows].astype(np.int64) - 4096 * ti).cuda()
+        codes = A.pack_trellis(states, bits)
+        assert np.array_equal(_u32(codes), g[f"g{i}_codes"])
+        back = A.unpack_trellis(codes, bits, 200)
+        assert np.array_equal(back.cpu().numpy().astype(np.int64), states.cpu().numpy())
+
+
+def test_encode_entry_and_decode_rotated_match_reference(golden):
+    from lookatmyquant_b200 import artifact as A
+    g = golden("artifact")
+    perm_rows = [torch.as_tensor(g[f"g{i}_rows"].astype(np.int64)) for i in range(4)]
+    bits = [int(g[f"g{i}_bits"]) for i in range(4)]
+    entry = {"states": torch.as_tensor(g["states"]).cuda(), "scales": torch.as_tensor(g["scales"]),
+             "in_seed": int(g["in_seed"]), "table": torch.as_tensor(g["table"]),
+             "row_groups": [{"rows": r, "bits": b, "table_index": i} for i, (r, b) in enumerate(zip(perm_rows, bits))]}
+    tensors, meta = A.encode_entry("w", entry)
+    assert np.array_equal(tensors["w.signs"].numpy(), g["signs"])
+    for i in range(4):
+        assert np.array_equal(_u32(tensors[f"w.g{i}.rows"]), g[f"g{i}_rows"])
+        assert np.array_equal(_u32(tensors[f"w.g{i}.codes"]), g[f"g{i}_codes"])
+        assert np.array_equal(tensors[f"w.g{i}.scales"].cpu().numpy(), g[f"g{i}_scales"])
+    assert [gr["bits"] for gr in meta["groups"]] == bits and meta["shape"] == [200, 200]
+    dec = A.decode_rotated(tensors, meta)
+    assert np.array_equal(dec.cpu().numpy(), g["decoded"])
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4])
+@pytest.mark.parametrize("n", [1, 31, 32, 200, 2560 + 7])
+def test_pack_matches_oracle_on_random_paths(k, n):
+    from lookatmyquant_b200 import artifact as A
+    st = _path(37, n, k, 100 * k + n)
+    codes = A.pack_trellis(torch.as_tensor(st).cuda(), k)
+    assert np.array_equal(_u32(codes), O.pack_trellis(st, k))
+    assert np.array_equal(A.unpack_trellis(codes, k, n).cpu().numpy().astype(np.int64), st)
+
+
+def test_pack_rejects_a_broken_path():
+    from lookatmyquant_b200 import artifact as A
+    st = _path(4, 100, 2, 1)
+    st[2, 50] ^= 1 << 11  # the state's high bits no longer continue the previous state
+    with pytest.raises(ValueError, match="not a row trellis from zero"):
+        A.pack_trellis(torch.as_tensor(st).cuda(), 2)
+    st = _path(4, 100, 2, 2)
+    st[1, 0] = 5  # the first state must come from state 0
+    with pytest.raises(ValueError, match="not a row trellis from zero"):
+        A.pack_trellis(torch.as_tensor(st).cuda(), 2)
+
+
+@pytest.mark.parametrize("nvec", [1, 3, 16, 21, 64])
+def test_product_matches_dense(golden, nvec):
+    from lookatmyquant_b200 import artifact as A
+    from lookatmyquant_b200.rotation import Rotation
+    g = golden("artifact")
+    tensors = {"w.signs": torch.as_tensor(g["signs"])}
+    groups = []
+    for i in range(4):
+        key = f"w.g{i}"
+        tensors.update({key + ".rows": torch.as_tensor(g[f"g{i}_rows"].view(np.int32)).cuda(),
+                        key + ".codes": torch.as_tensor(g[f"g{i}_codes"].view(np.int32)).cuda(),
+                        key + ".scales": torch.as_tensor(g[f"g{i}_scales"]).cuda()})
+        ti = int(g["states"][int(g[f"g{i}_rows"][0]), 0]) // 4096
+        tensors[key + ".table"] = torch.as_tensor(g["table"][4096 * ti:4096 * (ti + 1)]).cuda()
+        groups.append({"rows": len(g[f"g{i}_rows"]), "bits": int(g[f"g{i}_bits"])})
+    meta = A.grouped_matrix_meta("w", [200, 200], groups)
+    prod = A.TrellisProduct(tensors, meta)
+    x = torch.randn(nvec, 200, dtype=torch.float64, generator=torch.Generator().manual_seed(nvec)).cuda()
+    y = prod(x).double().cpu().numpy()
+    xr = Rotation.from_signs(torch.as_tensor(g["signs"]).double()).rows(x).cpu().numpy()
+    ref = xr @ g["decoded"].astype(np.float64).T
+    tol = 1e-2 if nvec >= A.DENSE_PRODUCT_VECTORS else 1e-5  # bf16 dense path vs the fp32 packed product
+    assert np.abs(y - ref).max() <= tol * np.abs(ref).max()

@@ -129,3 +129,20 @@ def test_trellis_states_inverts_table():
     v = table(3)
     st = np.random.default_rng(2).integers(0, 4096, size=(4, 9))
     assert np.array_equal(O.trellis_states(v[st], v), st.astype(np.int16))
+
+
+def test_packed_artifact_matches_reference(golden):
+    """The reference's own encode_entry and decode_rotated (compiler_artifact.py:307-360, :433-442) on row groups."""
+    g = golden("artifact")
+    groups = []
+    for i in range(4):
+        rows, bits = g[f"g{i}_rows"].astype(np.int64), int(g[f"g{i}_bits"])
+        ti = int(g["states"][rows[0], 0]) // 4096
+        states = g["states"][rows].astype(np.int64) - 4096 * ti
+        assert np.array_equal(O.pack_trellis(states, bits), g[f"g{i}_codes"])
+        assert np.array_equal(O.unpack_trellis(g[f"g{i}_codes"], bits, 200), states)
+        groups.append((rows, g[f"g{i}_codes"], bits, g[f"g{i}_scales"], g["table"][4096 * ti:4096 * (ti + 1)]))
+    assert np.array_equal(O.decode_rotated_groups(groups, (200, 200), 200), g["decoded"])
+    import torch
+    u = torch.rand(200, generator=torch.Generator().manual_seed(int(g["in_seed"])), dtype=torch.float64).numpy()
+    assert np.array_equal(g["signs"], np.where(u < .5, -1, 1).astype(np.int8))
