@@ -10,6 +10,7 @@
  *   lamq_viterbi           opgraph/codes.py:151-181   viterbi(X, values, L, k, chunk=None, start=None)
  *   lamq_ldlq_rowtrellis   opgraph/syntax.py:86-124   sweep(W, env, project, width=16, lazy=128) with the project of
  *                          opgraph/codes.py:442-450 and RowTrellisCode.step (codes.py:397-404)
+ *   lamq_ldlq_coltrellis   opgraph/syntax.py:86-124   the same sweep with TrellisCode.project (codes.py:363-383)
  *   lamq_xtx_accumulate,   quantize.py:1412-1470      H += Xᵀ(w⊙X), D += X_refᵀ(w⊙X) per calibration chunk, then
  *   lamq_weighted_split,                              H/n_tok and D/n_tok − H in fp64 (inline in quantize_stage);
  *   lamq_hessian_finalize  compiler.py:233-265        the unweighted H of `capture`
@@ -104,6 +105,24 @@ int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const doub
                          const uint8_t *dead, const double *S, const double *tables, const uint8_t *row_bits, int k_all,
                          int L, int width, int look, int lazy, int16_t *states, double *settled, void *workspace,
                          size_t workspace_bytes, lamq_stream_t stream);
+
+/*
+ * The column-trellis LDLQ sweep: sweep (opgraph/syntax.py:86-124) with TrellisCode.project (opgraph/codes.py:363-383),
+ * the `measure` path's trellis words. Per block of `width` columns, each column is cut into runs of Tm consecutive rows
+ * and every run goes onto its nearest free-start trellis path (fp32 costs of T/S, as lamq_viterbi); then the block
+ * LDLQ refit under U as in lamq_ldlq_rowtrellis.
+ * T:        rows x n fp64, in: the target X (rotated on both sides); out: each column as it stood just before it was
+ *           settled (sweep's return value).
+ * table:    2^L fp64 trellis values of this k.
+ * states:   rows x n int16 out; settled: rows x n fp64 out or NULL (table values, units of the row scale).
+ * workspace: lamq_ldlq_coltrellis_workspace_size(rows, n, Tm, L, k, width, lazy) bytes.
+ * Supported: L = 12, k in 1..4, rows a multiple of Tm, width <= 32, lazy a multiple of width.
+ */
+size_t lamq_ldlq_coltrellis_workspace_size(int64_t rows, int n, int Tm, int L, int k, int width, int lazy);
+int lamq_ldlq_coltrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU, const uint8_t *dead,
+                         const double *S, const double *table, int k, int L, int Tm, int width, int lazy,
+                         int16_t *states, double *settled, void *workspace, size_t workspace_bytes,
+                         lamq_stream_t stream);
 
 /*
  * Tensor-core contraction over tokens: acc[j][i] += Σ_t A[t][i]·B[t][j] (bf16 in, fp32 accumulate) for i, j < d.

@@ -241,6 +241,40 @@ def _row_trellis_sweep(X, S, env, code, row_bits=None, settled_out=True):
     return T, states, settled
 
 
+def _col_trellis_sweep(X, S, env, code, settled_out=True):
+    """lamq_ldlq_coltrellis: the column-trellis sweep of X (rows × n fp64, device); returns (before, states, settled)."""
+    dev = X.device
+    rows, n = X.shape
+    if rows % code.T:
+        raise ValueError(f"{rows} rows are not a whole number of runs of {code.T}")
+    T = X.contiguous().clone()
+    states = torch.empty(rows, n, dtype=torch.int16, device=dev)
+    settled = torch.empty(rows, n, dtype=torch.float64, device=dev) if settled_out else None
+    table = code.values.to(dev, torch.float64).contiguous()
+    dead = env.dead.to(dev, torch.uint8) if bool(env.dead.any()) else None
+    lib = _lib.load()
+    ws = torch.empty(lib.lamq_ldlq_coltrellis_workspace_size(rows, n, code.T, code.L, code.k, code.width, LAZY),
+                     dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        check(lib.lamq_ldlq_coltrellis(ptr(T), n, rows, n, ptr(env.U), env.U.stride(0), ptr(dead), ptr(S.contiguous()),
+                                       ptr(table), code.k, code.L, code.T, code.width, LAZY, ptr(states), ptr(settled),
+                                       ptr(ws), ws.numel(), stream_ptr(dev)), "lamq_ldlq_coltrellis")
+    return T, states, settled
+
+
+def _round_to_nearest(X, S, code):
+    """The code applied directly, without H (codes.py:460-461 with `settled` None): each row from state 0 (row trellis,
+    codes.py:406-409) or each run of T outputs down a column (column trellis, codes.py:371-378)."""
+    xs = X / S[:, None]
+    if isinstance(code, RowTrellisCode):
+        st = viterbi(xs, code.values, code.L, code.k, start=torch.zeros(len(xs), dtype=torch.long, device=xs.device))
+    else:
+        o, w = xs.shape
+        st = viterbi(code._seqs(xs), code.values, code.L, code.k)
+        st = st.reshape(o // code.T, w, code.T).permute(0, 2, 1).reshape(o, w)
+    return st.to(torch.int16), code.values.to(X.device, torch.float64)[st]
+
+
 def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list[int], incoherent: bool = True,
                in_seed: int | None = None, out_rot: bool = True, device=None) -> list[TrellisWord]:
     """(Gauge: incoherence →) Split(scale, per row, by RMS) → (block LDLQ sweep →) the trellis code, for matrices that
@@ -262,19 +296,17 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
         Xs.append(X)
     X = torch.cat(Xs) if len(Xs) > 1 else Xs[0]
     S = X.pow(2).mean(1).sqrt().clamp(min=1e-12)
-    if isinstance(code, RowTrellisCode):
-        if H is None:
-            raise NotImplementedError("row-trellis words without H (plain Viterbi per row) are not wired yet")
-        Hd = H.to(dev, torch.float64)
-        Hr = R_in.conj(Hd) if incoherent else Hd
-        env = Environment(Hr)
-        _, states, settled = _row_trellis_sweep(X, S, env, code)
-        env.check()
-        fixed, T = True, None
-    elif isinstance(code, TrellisCode):
-        raise NotImplementedError("the column-trellis sweep is not wired yet")
-    else:
+    if not isinstance(code, (RowTrellisCode, TrellisCode)):
         raise TypeError(f"unsupported code {type(code).__name__}")
+    if H is None:
+        states, settled = _round_to_nearest(X, S, code)
+    else:
+        Hd = H.to(dev, torch.float64)
+        env = Environment(R_in.conj(Hd) if incoherent else Hd)
+        sweep = _row_trellis_sweep if isinstance(code, RowTrellisCode) else _col_trellis_sweep
+        _, states, settled = sweep(X, S, env, code)
+        env.check()
+    fixed, T = (True, None) if isinstance(code, RowTrellisCode) else (False, code.T)
     out, r0 = [], 0
     for W, R_out in zip(Ws, R_outs):
         r1 = r0 + W.shape[0]
