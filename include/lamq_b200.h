@@ -24,6 +24,8 @@
  *   lamq_unpack_trellis
  *   lamq_decode_trellis    compiler_artifact.py:433-442  decode_rotated: table[state]·scale per group row
  *   lamq_trellis_product   runtime_mlx/fast_q35.py:69-172 the product kernel: y = S ⊙ (V[state]·(R_in x)) per group
+ *   lamq_kl_reference,     compiler.py:176-187        the KL probe: ref_lp once, then per probe the KL of the held
+ *   lamq_kl_head                                      positions' log_softmax(lm_head(h)) to it
  */
 #ifndef LAMQ_B200_H
 #define LAMQ_B200_H
@@ -209,6 +211,26 @@ int lamq_cross_apply(const double *W, int64_t ldw, int rows, int n, const double
 
 /* A = H + lam·mean(diag H)·I (quantize.py:1334). */
 int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, int n, double lam, lamq_stream_t stream);
+
+/*
+ * The KL probe's head (compiler.py:176-187): logits z = H·Eᵀ of held positions (H: ntok x d final hidden states, E: V x
+ * d LM head, bf16, K contiguous; the logits rounded to bf16 as the model's lm_head returns them), their log-softmax
+ * and the KL to a reference distribution, in tcgen05 passes over the vocabulary that write no logits.
+ * lamq_kl_reference (once per held set): from the reference model's H, writes the reference distribution
+ *   pdist = softmax(z_ref) (ntok x V fp32, leading dimension ldp, rows 16-byte aligned), lse_ref (ntok fp32) and the
+ *   per-position sums stat_a = Σ_v p·z_ref, stat_p = Σ_v p (fp64).
+ * lamq_kl_head (every probe): KL_t = Σ_v p·(log p − log_softmax(z)) = A − B + (lse − lse_ref)·P per position into
+ *   kl_pos (fp32), and kl_out[0] = Σ w·KL / Σ w, kl_out[1] = Σ w·KL, kl_out[2] = Σ w (fp64; w NULL: all ones).
+ * workspace: lamq_kl_workspace_size(ntok) bytes. status: device int, LAMQ_ERR_TIMEOUT if a bounded wait gave up.
+ */
+size_t lamq_kl_workspace_size(int64_t ntok);
+int lamq_kl_reference(const uint16_t *H, int64_t ldh, int64_t ntok, int d, const uint16_t *E, int64_t lde, int V,
+                      float *pdist, int64_t ldp, float *lse_ref, double *stat_a, double *stat_p, void *workspace,
+                      size_t workspace_bytes, int *status, lamq_stream_t stream);
+int lamq_kl_head(const uint16_t *H, int64_t ldh, int64_t ntok, int d, const uint16_t *E, int64_t lde, int V,
+                 const float *pdist, int64_t ldp, const float *lse_ref, const double *stat_a, const double *stat_p,
+                 const float *w, float *kl_pos, double *kl_out, void *workspace, size_t workspace_bytes, int *status,
+                 lamq_stream_t stream);
 
 /*
  * Packed trellis rows (opgraph-packed-1, compiler_artifact.py:225-297). A row of n states (L-bit states, k-bit

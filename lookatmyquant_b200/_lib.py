@@ -40,6 +40,9 @@ SIGNATURES = {
     "lamq_cross_apply_workspace_size": (_SZ, [_I32, _I32]),
     "lamq_cross_apply": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _D, _P, _I64, _P, _SZ, _P]),
     "lamq_trellis_words_per_row": (_I64, [_I32, _I32]),
+    "lamq_kl_workspace_size": (_SZ, [_I64]),
+    "lamq_kl_reference": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _SZ, _P, _P]),
+    "lamq_kl_head": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
     "lamq_ldlq_coltrellis_workspace_size": (_SZ, [_I64, _I32, _I32, _I32, _I32, _I32, _I32]),
     "lamq_ldlq_coltrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P,
                                      _P, _SZ, _P]),

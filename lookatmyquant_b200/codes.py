@@ -3,21 +3,22 @@
 Same names, argument meaning and errors as the reference module, so the reference's callers can bind to it:
 
     viterbi(X, values, L, k, chunk=None, start=None)            opgraph/codes.py:151-181
-    trellis_values(L, k, T=320, seed=0, refine=None, fit=None)  opgraph/codes.py:187-220 (the shipped fitted tables)
+    trellis_values(L, k, T=320, seed=0, refine=None, fit=None)  opgraph/codes.py:187-220 (shipped or fitted on the GPU)
     hadamard_factors(n), hadamard(n), rht(n, seed)             opgraph/codes.py:97-132
     is_trellis_path(states, L, k)                               opgraph/codes.py:246-248
     RowTrellisCode(L, k, T=256, width=16, look=8, seed=0)       opgraph/codes.py:386-410
     TrellisCode(L, k, T=320, width=16, seed=0)                  opgraph/codes.py:363-383
     ldlq_words(Ws, H, code, seeds, incoherent=True, in_seed=None, out_rot=True)   opgraph/codes.py:413-462
 
-The compute runs in liblamq_b200.so (sm_100a): the Viterbi decode and the fused row-trellis sweep are hand-written
-kernels. The words come back as `TrellisWord`s exposing what the reference's callers read from a Net (`matrix()`,
+The compute runs in liblamq_b200.so (sm_100a): the Viterbi decode and the row- and column-trellis sweeps are
+hand-written kernels. The words come back as `TrellisWord`s exposing what the reference's callers read from a Net (`matrix()`,
 `rate_bits()`, the states and the row scales).
 """
 
 from __future__ import annotations
 
 import math
+import os
 from pathlib import Path
 
 import numpy as np
@@ -43,16 +44,59 @@ def _dev(device=None) -> torch.device:
 # ----------------------------------------------------------------------------- tables
 
 
+def _table_cache() -> Path:
+    return Path(os.environ.get("LAMQ_TABLE_CACHE", Path.home() / ".cache" / "lookatmyquant_b200" / "tables"))
+
+
 def trellis_values(L: int, k: int, T: int = 320, seed: int = 0, refine: int | None = None, fit: str | None = None
                    ) -> torch.Tensor:
     """The 2^L trellis values for (L, k, T, seed, fit), fp64 on the CPU (codes.py:187-220). The reference's fitted e-means
-    tables ship with this package; a table that was never fitted raises instead of being fitted here."""
+    tables for T = 256 ship with this package; any other table is fitted once on the GPU (fit_trellis_values) and kept in
+    the table cache ($LAMQ_TABLE_CACHE, default ~/.cache/lookatmyquant_b200/tables), as the reference keeps its fits in
+    its cache directory."""
     fit = fit or "ema"
     name = f"trellis_L{L}_k{k}_T{T}_s{seed}{'' if fit == 'lloyd' else '_' + fit}.f64"
-    path = TABLES / name
-    if not path.exists():
-        raise FileNotFoundError(f"no fitted trellis table {name} in {TABLES}")
-    return torch.from_numpy(np.fromfile(path, dtype="<f8").copy())
+    if refine is None:
+        for path in (TABLES / name, _table_cache() / name):
+            if path.exists():
+                return torch.from_numpy(np.fromfile(path, dtype="<f8").copy())
+    v = fit_trellis_values(L, k, T, seed, refine, fit)
+    if refine is None:
+        _table_cache().mkdir(parents=True, exist_ok=True)
+        tmp = _table_cache() / (name + f".{os.getpid()}.tmp")
+        tmp.write_bytes(v.numpy().astype("<f8").tobytes())
+        os.replace(tmp, _table_cache() / name)
+    return v
+
+
+def fit_trellis_values(L: int, k: int, T: int, seed: int = 0, refine: int | None = None, fit: str = "ema",
+                       device=None) -> torch.Tensor:
+    """Fits a table as codes.py:187-220 does: the states' values start as unit-Gaussian quantiles in a random order and
+    move to the mean of the Gaussian samples the Viterbi assigns to each state — six Lloyd steps over one set of 4096
+    sequences ("lloyd"), or ("ema") 16·384 batches of 256 new sequences whose weight in each state's decaying sum and
+    count falls from 0.5 to 0.01 along a cosine. The samples come from torch's CPU generator in the reference's order,
+    the Viterbi runs on the GPU (lamq_viterbi, states identical to the reference's), and the per-state sums are kept in
+    fp64 on the host with the reference's ops, so the fitted values are the reference's."""
+    if fit not in ("lloyd", "ema"):
+        raise ValueError(fit)
+    dev = _dev(device)
+    g = torch.Generator().manual_seed(seed)
+    S = 1 << L
+    v = torch.special.ndtri((torch.randperm(S, generator=g).double() + 0.5) / S)
+    if fit == "lloyd":
+        X0 = torch.randn(4096, T, generator=g, dtype=torch.float64)
+        batches = ((X0, 1.0) for _ in range(6 if refine is None else refine))
+    else:
+        steps = 16 * (384 if refine is None else refine)
+        batches = ((torch.randn(256, T, generator=g, dtype=torch.float64),
+                    0.01 + 0.245 * (1 + math.cos(math.pi * j / max(steps - 1, 1)))) for j in range(steps))
+    sums, cnt = torch.zeros(S, dtype=torch.float64), torch.zeros(S, dtype=torch.float64)
+    for X, a in batches:
+        st = viterbi(X.to(dev), v, L, k).reshape(-1).cpu()
+        sums = (1 - a) * sums + a * torch.zeros(S, dtype=torch.float64).index_add_(0, st, X.reshape(-1))
+        cnt = (1 - a) * cnt + a * torch.bincount(st, minlength=S).double()
+        v = torch.where(cnt > 0, sums / cnt.clamp(min=1e-300), v)
+    return v
 
 
 def stacked_tables(L: int = 12, T: int = 256, device=None) -> torch.Tensor:

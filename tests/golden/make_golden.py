@@ -68,7 +68,7 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=["artifact"], help="write only this fixture (the others stay as committed)")
+    ap.add_argument("--only", choices=["artifact", "fit"], help="write only this fixture (the others stay as committed)")
     args = ap.parse_args()
     C = setup_reference(args.reference.resolve())
     import torch
@@ -78,6 +78,9 @@ def main():
 
     if args.only == "artifact":
         write_artifact_fixture(C, Q, CA, torch)
+        return
+    if args.only == "fit":
+        write_fit_fixture(C, torch)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -193,7 +196,18 @@ def main():
            "S": net.cores["W.S"].data.numpy()}
     np.savez_compressed(HERE / "column_trellis.npz", **col)
     write_artifact_fixture(C, Q, CA, torch)
+    write_fit_fixture(C, torch)
     print("golden vectors written to", HERE)
+
+
+def write_fit_fixture(C, torch):
+    """8. Table fits (codes.py:187-220) by the reference's own trellis_values, short enough for its CPU Viterbi: the
+    e-means fit with refine = 1 (16 batches) and two Lloyd steps, for k = 2 and 3 at T = 64."""
+    fit = {}
+    for k in (2, 3):
+        fit[f"ema_k{k}"] = C.trellis_values(12, k, 64, seed=5, refine=1, fit="ema").numpy()
+        fit[f"lloyd_k{k}"] = C.trellis_values(12, k, 64, seed=6, refine=2, fit="lloyd").numpy()
+    np.savez_compressed(HERE / "fit.npz", **fit)
 
 
 def write_artifact_fixture(C, Q, CA, torch):
