@@ -358,3 +358,37 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
                                in_seed, R_in, R_out, fixed, T))
         r0 = r1
     return out
+
+
+def main():
+    """`python -m lookatmyquant_b200.codes fit --k 2 3 4 --T 320 --out DIR`: fits tables on the GPU (fit_trellis_values)
+    and writes them as raw little-endian fp64 files named as the package's tables, with their SHA-256 sums."""
+    import argparse
+    import hashlib
+    import time
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("command", choices=["fit"])
+    ap.add_argument("--L", type=int, default=12)
+    ap.add_argument("--k", type=int, nargs="+", default=[2, 3, 4])
+    ap.add_argument("--T", type=int, default=320)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--fit", default="ema", choices=["ema", "lloyd"])
+    ap.add_argument("--out", type=Path, required=True)
+    a = ap.parse_args()
+    a.out.mkdir(parents=True, exist_ok=True)
+    for k in a.k:
+        t0 = time.time()
+        v = fit_trellis_values(a.L, k, a.T, a.seed, None, a.fit)
+        name = f"trellis_L{a.L}_k{k}_T{a.T}_s{a.seed}{'' if a.fit == 'lloyd' else '_' + a.fit}.f64"
+        raw = v.numpy().astype("<f8").tobytes()
+        (a.out / name).write_bytes(raw)
+        shipped = TABLES / name
+        note = ""
+        if shipped.exists():
+            ref = np.fromfile(shipped, dtype="<f8")
+            note = f" max |fit - shipped| {np.abs(ref - v.numpy()).max():.3e}"
+        print(f"{hashlib.sha256(raw).hexdigest()}  {name}  ({time.time() - t0:.1f} s){note}", flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+"""The `measure` sweep's KL probes on B200 (config 4): every linear piece of a model quantized at each trellis option,
+one at a time, and the KL of held-out windows to the unquantized model measured after each.
+
+Reference: compiler.py:134-291 (`measure`): held windows and their reference log-probabilities once (:176-187), input
+statistics H per group of four layers from a calibration pass that stops after the group (:220-265), then per piece
+and option `word(option, W, H, seed, trellis)` (quantize.py:332-347: the column TrellisCode with T = 320 for a
+960-wide model, two-sided rotation), the weight swapped in, `kl() − floor` recorded, the weight restored.
+
+Here: H from the tcgen05 statistics kernel (bf16 activations, as the reference's fp32 Xᵀ·X of the bf16 stream), the
+word from the column-trellis sweep kernel, the forward through the model's own bf16 layers, and the KL from the fused
+LM-head/log-softmax/KL kernel (kl.KLReference) on the final hidden states — no logits are formed. The model is a
+random-initialised SmolLM2-360M-architecture Llama (weights N(0, 0.02²), bf16) and the windows are seeded Zipf tokens.
+"""
+
+from __future__ import annotations
+
+import json
+import time
+
+import torch
+
+from . import codes
+from .hessian import Statistics
+from .kl import KLReference
+
+STAGES = [("self_attn", ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"]),
+          ("self_attn", ["self_attn.o_proj"]),
+          ("mlp", ["mlp.gate_proj", "mlp.up_proj"]),
+          ("mlp", ["mlp.down_proj"])]
+BLOCK_SEED = {"self_attn": 2, "mlp": 3}  # compiler_arch.block_seed for the Llama blocks
+
+
+def smollm2_config(layers: int = 32):
+    from transformers import LlamaConfig
+    cfg = LlamaConfig(hidden_size=960, intermediate_size=2560, num_hidden_layers=layers, num_attention_heads=15,
+                      num_key_value_heads=5, vocab_size=49152, rms_norm_eps=1e-5, rope_theta=1e5,
+                      tie_word_embeddings=True, max_position_embeddings=8192, initializer_range=0.02)
+    cfg._attn_implementation = "sdpa"
+    return cfg
+
+
+def build_model(layers: int = 32, seed: int = 0, device="cuda"):
+    """A SmolLM2-360M-architecture model with random N(0, 0.02²) weights, bf16, on the device."""
+    from transformers import LlamaForCausalLM
+    torch.manual_seed(seed)
+    model = LlamaForCausalLM(smollm2_config(layers))
+    return model.to(device=device, dtype=torch.bfloat16).eval()
+
+
+def zipf_tokens(windows: int, T: int, V: int, seed: int, s: float = 1.1) -> torch.Tensor:
+    """windows × T token ids, id r − 1 with probability ∝ r^−s (seeded, torch's CPU generator)."""
+    w = torch.arange(1, V + 1, dtype=torch.float64).pow(-s)
+    g = torch.Generator().manual_seed(seed)
+    return torch.multinomial(w, windows * T, replacement=True, generator=g).reshape(windows, T)
+
+
+class _Stop(Exception):
+    pass
+
+
+@torch.no_grad()
+def capture(model, layers, chunks) -> dict:
+    """{(layer, first name of the stage): H (fp64)} for the stages of `layers`, from one calibration pass over
+    `chunks` that stops after the group's last layer (compiler.py:220-265)."""
+    decoder = model.model.layers
+    stats, hooks = {}, []
+    for i in layers:
+        for _, names in STAGES:
+            key = (i, names[0])
+            mod = decoder[i].get_submodule(names[0])
+
+            def hook(m, a, key=key, d=mod.in_features):
+                if key not in stats:
+                    stats[key] = Statistics(d, device=a[0].device)
+                stats[key].add(a[0].reshape(-1, a[0].shape[-1]))
+            hooks.append(mod.register_forward_pre_hook(hook))
+    last = max(layers)
+    if last + 1 < len(decoder):
+        def stop(m, a, k):
+            raise _Stop()
+        hooks.append(decoder[last + 1].register_forward_pre_hook(stop, with_kwargs=True))
+    try:
+        for x in chunks:
+            try:
+                model.model(x, use_cache=False)
+            except _Stop:
+                pass
+    finally:
+        for h in hooks:
+            h.remove()
+    out = {}
+    for key, st in stats.items():
+        H, _ = st.finalize()
+        st.check_status()
+        out[key] = H
+    return out
+
+
+class Probe:
+    """Held windows, their reference distribution (once) and the KL of the current model to it."""
+
+    def __init__(self, model, held: torch.Tensor, batch: int = 2, weights: torch.Tensor | None = None):
+        self.model, self.held, self.batch = model, held, batch
+        self.w = weights
+        self.ref = KLReference(self.hidden(), model.lm_head.weight)
+
+    @torch.no_grad()
+    def hidden(self) -> torch.Tensor:
+        dev = self.model.lm_head.weight.device
+        hs = [self.model.model(self.held[b:b + self.batch].to(dev), use_cache=False).last_hidden_state
+              for b in range(0, len(self.held), self.batch)]
+        return torch.cat(hs).reshape(-1, hs[0].shape[-1])
+
+    def kl(self) -> float:
+        return self.ref.kl(self.hidden(), self.w)
+
+
+def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, windows: int = 8, T: int = 2048,
+        calib: int = 16, chunk: int = 4, kl_batch: int = 2, seed: int = 0, device="cuda", log=print) -> dict:
+    """The measure sweep over the linear pieces of `layers`: returns the records and the timing."""
+    dev = torch.device(device)
+    t_all = time.time()
+    model = build_model(n_layers, seed, dev)
+    V = model.config.vocab_size
+    held = zipf_tokens(windows, T, V, seed + 1)
+    cal = zipf_tokens(calib, T, V, seed + 2)
+    chunks = [cal[b:b + chunk].to(dev) for b in range(0, len(cal), chunk)]
+    t0 = time.time()
+    probe = Probe(model, held, kl_batch)
+    torch.cuda.synchronize()
+    t_ref = time.time() - t0
+    t0 = time.time()
+    floor = probe.kl()
+    t_kl = time.time() - t0
+    T_tr = 256 if model.config.hidden_size % 256 == 0 else 320
+    trellis = {}
+    recs, t_probe, n_probe = [], 0.0, 0
+    layers = list(layers)
+    groups = [layers[k:k + 4] for k in range(0, len(layers), 4)]
+    for group in groups:
+        H = capture(model, group, chunks)
+        for i in group:
+            L = model.model.layers[i]
+            for block, names in STAGES:
+                Hs = H[(i, names[0])]
+                for j, name in enumerate(names):
+                    mod = L.get_submodule(name)
+                    orig = mod.weight.data.clone()
+                    W = orig.double()
+                    m, n = W.shape
+                    Tm = T_tr if m % T_tr == 0 else next(t for t in (320, 256, 128, 64) if m % t == 0)
+                    seed_ = 1000 * i + 100 * BLOCK_SEED[block] + j
+                    for o in options:
+                        k = int(o[2:])
+                        if (k, Tm) not in trellis:
+                            trellis[(k, Tm)] = codes.TrellisCode(12, k, T=Tm)
+                        ts = time.time()
+                        word = codes.ldlq_words([W], Hs, trellis[(k, Tm)], [seed_])[0]
+                        mod.weight.data = word.matrix().to(torch.bfloat16)
+                        d = probe.kl() - floor
+                        mod.weight.data = orig
+                        dt = time.time() - ts
+                        t_probe += dt
+                        n_probe += 1
+                        recs.append({"item": f"{i}.{name}", "layer": i, "role": name, "shape": [m, n], "T": Tm,
+                                     "option": o, "bits": word.rate_bits(), "dkl": d, "seconds": round(dt, 4)})
+                    log(f"  layer {i} {name}: " + ", ".join(f"{r['option']} {r['dkl']:.3e}" for r in recs[-len(options):]))
+    return {"records": recs, "kl floor": floor, "probes": n_probe, "seconds in probes": t_probe,
+            "probes per hour": 3600.0 * n_probe / t_probe if t_probe else None, "seconds per kl": t_kl,
+            "seconds for the reference distribution": t_ref, "seconds": time.time() - t_all,
+            "held windows": [windows, T], "calibration": [calib, T]}
+
+
+def main():
+    """`python -m lookatmyquant_b200.measure [--layers A:B] [--windows 8] [--T 2048]`: the config-4 KL probes over the
+    linear pieces of the chosen layers of a random SmolLM2-360M-architecture model; prints one JSON summary."""
+    import argparse
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--layers", default="0:1")
+    ap.add_argument("--model-layers", type=int, default=32)
+    ap.add_argument("--windows", type=int, default=8)
+    ap.add_argument("--T", type=int, default=2048)
+    ap.add_argument("--calib", type=int, default=16)
+    ap.add_argument("--options", nargs="+", default=["tr2", "tr3", "tr4"])
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args()
+    lo, hi = (int(x) for x in a.layers.split(":"))
+    res = run(range(lo, hi), a.options, a.model_layers, a.windows, a.T, a.calib)
+    summary = {k: v for k, v in res.items() if k != "records"}
+    print(json.dumps(summary), flush=True)
+    if a.out:
+        with open(a.out, "w") as f:
+            json.dump(res, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

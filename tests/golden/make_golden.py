@@ -90,6 +90,10 @@ def main():
         path = TABLES / f"trellis_L12_k{k}_T256_s0_ema.f64"
         path.write_bytes(v.astype("<f8").tobytes())
         digests[path.name] = hashlib.sha256(path.read_bytes()).hexdigest()
+    # the sums cover every table in the folder (the T = 320 ones are fitted on the GPU by `python -m
+    # lookatmyquant_b200.codes fit`, which reproduces these T = 256 tables bit for bit)
+    for path in TABLES.glob("trellis_*.f64"):
+        digests.setdefault(path.name, hashlib.sha256(path.read_bytes()).hexdigest())
     (TABLES / "SHA256SUMS").write_text("".join(f"{h}  {n}\n" for n, h in sorted(digests.items())))
 
     # 1. Viterbi (codes.py:151-181): windows with a start state, free-start runs, small tables

@@ -1,0 +1,33 @@
+"""The measure sweep's pieces (compiler.py:134-291) on a two-layer model of the SmolLM2 architecture: H from the
+calibration pass against the reference's fp32 Xᵀ·X / n of the same activations, the KL floor, and one probe."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_capture_matches_fp32_statistics():
+    from lookatmyquant_b200 import measure
+    model = measure.build_model(layers=2)
+    chunks = [measure.zipf_tokens(2, 96, model.config.vocab_size, 3).cuda()]
+    H = measure.capture(model, [0], chunks)
+    xs = []
+    h = model.model.layers[0].mlp.down_proj.register_forward_pre_hook(lambda m, a: xs.append(a[0].reshape(-1, a[0].shape[-1])))
+    with torch.no_grad():
+        model.model(chunks[0], use_cache=False)
+    h.remove()
+    x = xs[0].float()
+    ref = (x.T @ x / len(x)).double()
+    got = H[(0, "mlp.down_proj")]
+    assert (got - ref).norm() <= 1e-5 * ref.norm()
+    assert set(H) == {(0, "self_attn.q_proj"), (0, "self_attn.o_proj"), (0, "mlp.gate_proj"), (0, "mlp.down_proj")}
+
+
+def test_probe_floor_and_one_option():
+    from lookatmyquant_b200 import measure
+    res = measure.run(layers=range(1), options=("tr2",), n_layers=2, windows=2, T=128, calib=2, chunk=2, log=lambda s: None)
+    assert res["kl floor"] == 0.0
+    assert res["probes"] == 7
+    dkl = [r["dkl"] for r in res["records"]]
+    assert all(d >= -1e-6 for d in dkl) and max(dkl) > 0

@@ -11,3 +11,29 @@ def test_missing_table_is_fitted_and_cached(tmp_path, monkeypatch):
     v = codes.trellis_values(12, 2, 48)
     assert (tmp_path / "trellis_L12_k2_T48_s0_ema.f64").exists()
     assert np.array_equal(codes.trellis_values(12, 2, 48).numpy(), v.numpy())
+
+
+def test_zipf_tokens_are_seeded_and_in_range():
+    from lookatmyquant_b200 import measure
+    a = measure.zipf_tokens(3, 50, 1000, 7)
+    b = measure.zipf_tokens(3, 50, 1000, 7)
+    assert torch.equal(a, b) and a.shape == (3, 50) and int(a.min()) >= 0 and int(a.max()) < 1000
+    assert (a == 0).float().mean() > (a == 10).float().mean()  # rank 1 is the most frequent
+
+
+def test_smollm2_shape():
+    from lookatmyquant_b200 import measure
+    c = measure.smollm2_config()
+    assert (c.hidden_size, c.intermediate_size, c.num_hidden_layers, c.num_attention_heads, c.num_key_value_heads,
+            c.vocab_size, c.tie_word_embeddings) == (960, 2560, 32, 15, 5, 49152, True)
+
+
+def test_shipped_tables_match_their_sums():
+    import hashlib
+    from lookatmyquant_b200 import codes
+    lines = (codes.TABLES / "SHA256SUMS").read_text().split("\n")
+    sums = dict(reversed(line.split("  ")) for line in lines if line)
+    assert len(sums) == 7
+    for name, h in sums.items():
+        assert hashlib.sha256((codes.TABLES / name).read_bytes()).hexdigest() == h
+        assert np.fromfile(codes.TABLES / name, dtype="<f8").shape == (4096,)
