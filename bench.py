@@ -220,23 +220,13 @@ class Config3:
             torch.distributed.all_gather_into_tensor(allb.view(torch.uint8), buf.view(torch.uint8), group=self.group)
 
     def e2e_step(self):
-        """The build from host memory: every stage's weights and activations copied from pinned host buffers inside the
-        timed region, the states and scales read back."""
-        from lookatmyquant_b200.layer import build_stage, stacked_tables
-        tables = stacked_tables(12, 256, self.device)
-        res = []
-        for s in self.stages:
-            x = self.host_acts[s.name][0].to(self.device, non_blocking=True)
-            xr = self.host_acts[s.name][1].to(self.device, non_blocking=True)
-            ws = {nm: self.host_weights[nm].to(self.device, non_blocking=True) for nm, _ in s.matrices}
-            w = self.host_w.to(self.device, non_blocking=True)
-            r = build_stage(s, ws, x, xr, w, self.bits, 0, self.group, False, tables, self.tokens)
-            del x, xr
-            for nm in r.states:
-                res.append(r.states[nm].to("cpu", non_blocking=True))
-                res.append(r.scales[nm].to("cpu", non_blocking=True))
-        torch.cuda.synchronize()
-        return res
+        """The build from host memory through the public API (layer.build_layer_from_host): every stage's weights and
+        activations copied from pinned host buffers inside the timed region (overlapped with the compute), the states
+        and scales read back."""
+        from lookatmyquant_b200.layer import build_layer_from_host
+        out = build_layer_from_host(self.stages, self.host_weights, self.host_acts, self.host_w, self.bits, 0,
+                                    self.group, self.tokens, device=self.device)
+        return [t for r in out.values() for nm in r.states for t in (r.states[nm], r.scales[nm])]
 
     def prepare_e2e(self):
         self.host_acts = {k: (a.cpu().pin_memory(), b.cpu().pin_memory()) for k, (a, b) in self.acts.items()}

@@ -51,9 +51,12 @@ class Statistics:
                                           1 if symmetric else 0, ptr(acc), acc.stride(0), self.chunk_tokens,
                                           ptr(self.status), stream_ptr(self.device)), "lamq_xtx_accumulate")
 
-    def add(self, x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor | None = None):
+    def add(self, x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor | None = None,
+            weighted: torch.Tensor | None = None):
         """One calibration chunk: x (tokens × d bf16, the stream the matrix will see), its token weights w (fp32, or
-        None for 1) and, for D, x_ref (the reference stream at the same tokens)."""
+        None for 1) and, for D, x_ref (the reference stream at the same tokens). `weighted` (int32, on the device)
+        may give the chunk's tokens whose weight is not 1, found by the caller; otherwise they are found here, which
+        reads their count back from the device."""
         x = _bf16(x)
         tokens = x.shape[0]
         if x.shape[1] != self.d:
@@ -68,7 +71,7 @@ class Statistics:
             w = w.reshape(-1).to(self.device, torch.float32).contiguous()
             if w.numel() != tokens:
                 raise ValueError("one weight per token")
-            idx = torch.nonzero(w != 1.0).flatten().to(torch.int32)
+            idx = torch.nonzero(w != 1.0).flatten().to(torch.int32) if weighted is None else weighted
             nw = int(idx.numel())
             if nw:
                 lib = _lib.load()

@@ -91,11 +91,17 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
     """One stage: statistics, QEP target, rotation, environment and the fused row-trellis sweep over every row of the
     stage's matrices. `weights[name]` is rows × d (any float dtype, on the device), `bits[name]` the per-row widths.
     With a process group, x/x_ref/w are this rank's token shard and each rank sweeps a contiguous share of rows."""
-    dev = x.device
+    st = Statistics(spec.d, cross=True, device=x.device)
+    st.add(x, w, x_ref)
+    return build_stage_from_statistics(spec, weights, st, bits, layer, group, dequantize, tables, n_tok_total)
+
+
+def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, bits: dict, layer: int = 0, group=None,
+                                dequantize: bool = True, tables=None, n_tok_total: int | None = None) -> StageResult:
+    """The stage after its statistics have been accumulated (all of this rank's tokens added to `st`)."""
+    dev = st.device
     world = group.size() if group is not None else 1
     rank = group.rank() if group is not None else 0
-    st = Statistics(spec.d, cross=True, device=dev)
-    st.add(x, w, x_ref)
     n_tok = st.n_tok
     if group is not None:
         torch.distributed.all_reduce(st.accH, group=group)
@@ -147,6 +153,66 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
     env.check()
     qep.check()
     return res
+
+
+_COPY = {}
+
+
+def _copy_stream(dev) -> torch.cuda.Stream:
+    if dev not in _COPY:
+        _COPY[dev] = torch.cuda.Stream(device=dev)
+    return _COPY[dev]
+
+
+def build_layer_from_host(stages, weights, acts, w, bits, layer: int = 0, group=None, n_tok_total: int | None = None,
+                          chunk_tokens: int = 65536, device=None):
+    """The layer build from host memory: `weights[name]` and `acts[stage] = (x, x_ref)` are pinned CPU tensors (this
+    rank's token shard), `w` the pinned per-token weights. Every copy is queued at once on a copy stream, chunk by
+    chunk and stage by stage, so the statistics kernel consumes each chunk as soon as it is resident and the later
+    stages' activations arrive while the earlier stages factor and sweep: the build takes about the longer of the
+    host→device transfer and the compute instead of their sum. The weighted tokens of each chunk are found on the
+    host. Returns {stage: StageResult} with states and scales in pinned host memory (the call synchronizes)."""
+    dev = torch.device(device or "cuda")
+    copy, main = _copy_stream(dev), torch.cuda.current_stream(dev)
+    tables = stacked_tables(12, 256, dev)
+    copy.wait_stream(main)
+    staged = []
+    with torch.cuda.stream(copy):
+        w_d = w.to(dev, non_blocking=True)
+        for s in stages:
+            x_h, xr_h = acts[s.name]
+            wts = {nm: weights[nm].to(dev, non_blocking=True) for nm, _ in s.matrices}
+            x_d = torch.empty(x_h.shape, dtype=x_h.dtype, device=dev)
+            xr_d = torch.empty(xr_h.shape, dtype=xr_h.dtype, device=dev)
+            chunks = []
+            for c0 in range(0, x_h.shape[0], chunk_tokens):
+                c1 = min(c0 + chunk_tokens, x_h.shape[0])
+                wc = w[c0:c1]
+                idx = torch.nonzero(wc != 1.0).flatten().to(torch.int32).pin_memory().to(dev, non_blocking=True)
+                x_d[c0:c1].copy_(x_h[c0:c1], non_blocking=True)
+                xr_d[c0:c1].copy_(xr_h[c0:c1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy)
+                chunks.append((c0, c1, idx, ev))
+            staged.append((x_d, xr_d, wts, chunks))
+    for t in [w_d] + [t for x_d, xr_d, wts, chunks in staged for t in [x_d, xr_d, *wts.values(), *(c[2] for c in chunks)]]:
+        t.record_stream(main)
+    out = {}
+    for i, s in enumerate(stages):
+        x_d, xr_d, wts, chunks = staged[i]
+        staged[i] = None  # the stage's activations are freed once its statistics are done
+        st = Statistics(s.d, cross=True, device=dev)
+        for c0, c1, idx, ev in chunks:
+            main.wait_event(ev)
+            st.add(x_d[c0:c1], w_d[c0:c1], xr_d[c0:c1], weighted=idx)
+        del x_d, xr_d, chunks
+        res = build_stage_from_statistics(s, wts, st, bits, layer, group, False, tables, n_tok_total)
+        for nm in list(res.states):
+            res.states[nm] = res.states[nm].to("cpu", non_blocking=True)
+            res.scales[nm] = res.scales[nm].to("cpu", non_blocking=True)
+        out[s.name] = res
+    torch.cuda.synchronize(dev)
+    return out
 
 
 def sweep_rows(X, S, env, row_bits, tables=None):

@@ -44,3 +44,25 @@ def test_small_layer_matches_oracle():
                 pg, po = np.sum((E @ Hr_) * E), np.sum((Eo @ Hr_) * Eo)
                 assert abs(pg - po) <= 0.005 * po, (s.name, nm, k, pg, po)
             assert sum(same) / rows >= 0.999, (s.name, nm, sum(same) / rows)
+
+
+def test_build_from_host_equals_the_device_build():
+    """build_layer_from_host (copies streamed chunk by chunk, weighted tokens found on the host) gives the states and
+    scales of the build from device-resident inputs."""
+    from lookatmyquant_b200.layer import StageSpec, build_layer, build_layer_from_host
+    from lookatmyquant_b200.workloads import config3
+    stages = [StageSpec("attn_in", 256, [("self_attn.q_proj", 256), ("self_attn.k_proj", 128)], "self_attn"),
+              StageSpec("down_in", 320, [("mlp.down_proj", 192)], "mlp")]
+    stages, weights, acts, w, bits = config3(20000, stages=stages)
+    ref = build_layer(stages, weights, acts, w, bits, dequantize=False)
+    host_acts = {k: (a.cpu().pin_memory(), b.cpu().pin_memory()) for k, (a, b) in acts.items()}
+    host_w = {k: v.cpu().pin_memory() for k, v in weights.items()}
+    out = build_layer_from_host(stages, host_w, host_acts, w.cpu().pin_memory(), bits, chunk_tokens=4096)
+    # the chunked statistics sum the tokens in another order (fp32 rounding), so H, D and the words may differ in
+    # the last bits: the north-star bars apply
+    for s in stages:
+        for nm, _ in s.matrices:
+            a, b = out[s.name].states[nm], ref[s.name].states[nm].cpu()
+            assert (a == b).double().mean() >= 0.999
+            sa, sb = out[s.name].scales[nm], ref[s.name].scales[nm].cpu()
+            assert ((sa - sb).abs() <= 1e-6 * sb.abs()).all()
