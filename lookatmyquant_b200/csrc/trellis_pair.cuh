@@ -4,9 +4,9 @@
 //   cost_t[s] = best_t[s >> k] + (x_t − C[s])²,   best_t[r] = min_{h < 2^k} cost_{t−1}[h·R + r]   (smallest h on ties)
 // Thread p (0..63) of the pair owns RT = R/64 consecutive r and keeps the 64 table values C[h·R + r] of its
 // predecessors in registers as fp32 pairs (half the registers of one warp per row, so twice the warps fit on an SM).
-// (x − C)² is computed two states at a time with sub/mul.rn.f32x2 and the add to the best predecessor cost with
-// add.rn.f32: every value is rounded exactly as the reference's scalar fp32 sub, mul and add (explicit rounding, never
-// fused). The minimum over the 2^k predecessors is a knock-out tournament whose decisions are the sign bits of fp32
+// (x − C)² and its add to the best predecessor cost are computed two states at a time with sub/mul/add.rn.f32x2
+// (states r and r + 1 share their predecessors): every value is rounded exactly as the reference's scalar fp32 sub, mul
+// and add (explicit rounding, never fused). The minimum over the 2^k predecessors is a knock-out tournament whose decisions are the sign bits of fp32
 // differences (the fp32 pipe, not the half-rate compare/select pipe) appended to the back-pointer words by funnel
 // shifts: 2^k − 1 bits per r, decoded on the traceback. The pair exchanges the R best values through shared memory
 // (double buffered, one named barrier per step), stored in 16-byte units swizzled by writer thread so that writes and
@@ -152,6 +152,12 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
                 bv[h][0] = bin[pslot<K>(base)];
             }
         }
+        // r = ii and ii + 1 share their predecessors' best values (ii >> K), so the add is paired too
+        u64 bb[T::NB][CH];
+#pragma unroll
+        for (int h = 0; h < T::NB; ++h)
+#pragma unroll
+            for (int j = 0; j < CH; ++j) bb[h][j] = pk2(bv[h][j], bv[h][j]);
         float nb4[4];
 #pragma unroll
         for (int i = 0; i < CI; i += 2) {
@@ -159,12 +165,8 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
             float clo[T::NB], chi[T::NB];
 #pragma unroll
             for (int h = 0; h < T::NB; ++h) {
-                const float b = bv[h][(CH == 4) ? (i >> K) : 0];
                 const u64 d = sub2(xx, cv[h][ii >> 1]);  // (x − C) for r = ii and ii + 1
-                float slo, shi;
-                upk2(mul2(d, d), slo, shi);
-                clo[h] = __fadd_rn(b, slo);
-                chi[h] = __fadd_rn(b, shi);
+                upk2(add2(bb[h][(CH == 4) ? (i >> K) : 0], mul2(d, d)), clo[h], chi[h]);  // best + (x − C)²
             }
             nb4[i & 3] = tournament<K>(clo, words, ii * (T::NB - 1));
             nb4[(i & 3) + 1] = tournament<K>(chi, words, (ii + 1) * (T::NB - 1));
