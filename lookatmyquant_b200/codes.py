@@ -367,14 +367,19 @@ def main():
     import hashlib
     import time
     ap = argparse.ArgumentParser(description=main.__doc__)
-    ap.add_argument("command", choices=["fit"])
+    ap.add_argument("command", choices=["fit", "sweep"])
+    ap.add_argument("--rows", type=int, default=1024)
+    ap.add_argument("--n", type=int, default=2560)
     ap.add_argument("--L", type=int, default=12)
     ap.add_argument("--k", type=int, nargs="+", default=[2, 3, 4])
     ap.add_argument("--T", type=int, default=320)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--fit", default="ema", choices=["ema", "lloyd"])
-    ap.add_argument("--out", type=Path, required=True)
+    ap.add_argument("--out", type=Path)
     a = ap.parse_args()
+    if a.command == "sweep":
+        _sweep_cli(a.rows, a.n, a.k[0])
+        return
     a.out.mkdir(parents=True, exist_ok=True)
     for k in a.k:
         t0 = time.time()
@@ -388,6 +393,25 @@ def main():
             ref = np.fromfile(shipped, dtype="<f8")
             note = f" max |fit - shipped| {np.abs(ref - v.numpy()).max():.3e}"
         print(f"{hashlib.sha256(raw).hexdigest()}  {name}  ({time.time() - t0:.1f} s){note}", flush=True)
+
+
+def _sweep_cli(rows: int, n: int, k: int):
+    """One row-trellis sweep of a random rows × n word at width k under a random H (two launches, the second timed)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randn(2 * n, n, device="cuda", dtype=torch.float64, generator=g)
+    A = A * torch.exp(torch.randn(n, device="cuda", dtype=torch.float64, generator=g))
+    env = Environment(A.T @ A / (2 * n))
+    X = 0.02 * torch.randn(rows, n, device="cuda", dtype=torch.float64, generator=g)
+    S = X.pow(2).mean(1).sqrt()
+    code = RowTrellisCode(12, k)
+    rb = torch.full((rows,), k, dtype=torch.uint8, device="cuda")
+    for rep in range(2):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        _row_trellis_sweep(X, S, env, code, row_bits=rb)
+        e_.record()
+        e_.synchronize()
+    print(f"sweep {rows} x {n}, k = {k}: {s_.elapsed_time(e_):.3f} ms")
 
 
 if __name__ == "__main__":

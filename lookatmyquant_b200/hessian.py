@@ -115,3 +115,33 @@ def hessian(x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor 
     st = Statistics(x.shape[-1], cross=x_ref is not None, device=x.device, chunk_tokens=chunk_tokens)
     st.add(x, w, x_ref)
     return st.finalize()
+
+
+def main():
+    """`python -m lookatmyquant_b200.hessian --tokens 65536 --d 9728`: H and D of random bf16 activations (two passes,
+    the second timed with CUDA events); prints the achieved TFLOP/s of each contraction."""
+    import argparse
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--d", type=int, default=9728)
+    a = ap.parse_args()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(a.tokens, a.d, device="cuda", generator=g).to(torch.bfloat16)
+    xr = torch.randn(a.tokens, a.d, device="cuda", generator=g).to(torch.bfloat16)
+    st = Statistics(a.d, cross=True)
+    for rep in range(2):
+        for sym, (A, B, acc) in ((True, (x, x, st.accH)), (False, (x, xr, st.accD))):
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            st._xtx(A, B, sym, acc, a.tokens)
+            e_.record()
+            e_.synchronize()
+            ms = s_.elapsed_time(e_)
+            fl = 2.0 * a.tokens * a.d * (a.d + 1) / 2 if sym else 2.0 * a.tokens * a.d * a.d
+            if rep:
+                print(f"d={a.d} tokens={a.tokens} {'H' if sym else 'D'}: {ms:.3f} ms, {fl / ms / 1e9:.1f} TFLOP/s")
+    st.check_status()
+
+
+if __name__ == "__main__":
+    main()
