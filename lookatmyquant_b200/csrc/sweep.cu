@@ -2,8 +2,9 @@
 //
 // Reference: opgraph/syntax.py:86-124 (`sweep`), with the projection of opgraph/codes.py:442-450 and
 // RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so rows are grouped by
-// their width k into tiles of 16 and each tile is swept start to finish by one CTA of 16 warps: 8 warp pairs, each
-// decoding 2 rows in turn (trellis_pair.cuh: 64 states per thread, fp32x2 arithmetic):
+// their width k into tiles of 16 rows (or 8, when 16-row tiles would leave the last wave of CTAs mostly empty) and
+// each tile is swept start to finish by one CTA of 16 warps: 8 warp pairs, each decoding its 2 rows (or 1) in turn
+// (trellis_pair.cuh: 64 states per thread, fp32x2 arithmetic):
 //
 //   per run of `lazy` columns [b0, b1):
 //     the run's targets plus the `look` columns after it are copied from T into shared memory (Trun);
@@ -15,7 +16,8 @@
 //     then the whole CTA applies the run to every later column, T[:, b1:] -= Z·U[b0:b1, b1:] (syntax.py:122-123), as
 //       an fp64 tensor-core GEMM (mma.sync m8n8k4 f64) over 16 rows, U staged through shared memory by cp.async so
 //       each U element crosses L2 once per 16 rows.
-// Tiles are taken from a work counter (persistent grid), so tiles of different widths and matrix sizes balance.
+// Tiles are taken from a work counter (persistent grid), the widest rows first, so tiles of different widths and
+// matrix sizes balance.
 #include <algorithm>
 
 #include "lamq_common.cuh"
@@ -28,8 +30,8 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kPairs = kWarps / 2;
-constexpr int kRowsPerPair = 2;
-constexpr int kTileRows = kPairs * kRowsPerPair;  // 16
+constexpr int kMaxRowsPerPair = 2;
+constexpr int kTileRows = kPairs * kMaxRowsPerPair;  // 16: the largest tile (8 when each pair takes one row)
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxWin = 24;  // RowTrellisCode windows: width 16 + look 8
 constexpr int kGemmCols = 64;                      // columns of U per GEMM stage (8 per warp)
@@ -40,7 +42,7 @@ struct SweepParams {
     double *T;
     int64_t ldT;
     int n;
-    const int32_t *rowlist;   // tiles of 16 row indices grouped by width, -1 = padding
+    const int32_t *rowlist;   // tiles of tile_rows row indices grouped by width (widest first), -1 = padding
     const int *ntiles;        // device: number of tiles
     int *counter;             // device: next tile to take
     const uint8_t *row_bits;  // per-row width or null
@@ -52,6 +54,7 @@ struct SweepParams {
     const double *tables;
     int width, look, lazy;
     int trun_stride;          // doubles per Trun row
+    int rows_per_pair;        // 1 or 2: tiles of 8 or 16 rows
     int16_t *states;
     double *settled;
 };
@@ -144,9 +147,10 @@ __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *
     uint32_t *args = reinterpret_cast<uint32_t *>(best1 + PairTrellis<K>::R);
     float *red = reinterpret_cast<float *>(wv + kPairMax);
     // each row's last state, shared by the pair; outside the Viterbi scratch, which the run's GEMM reuses
-    int *pstate = row_state + pair * kRowsPerPair;
+    const int rpp = p.rows_per_pair;
+    int *pstate = row_state + pair * rpp;
     const int n = p.n;
-    if (pt < kRowsPerPair) pstate[pt] = 0;  // every row's path starts at state 0 (codes.py:399-400)
+    if (pt < rpp) pstate[pt] = 0;  // every row's path starts at state 0 (codes.py:399-400)
     for (int b0 = 0; b0 < n; b0 += p.lazy) {
         const int b1 = min(b0 + p.lazy, n);
         const int ncol = b1 - b0 + min(p.look, n - b1);
@@ -159,8 +163,8 @@ __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *
             const int w = min(p.width, n - j);
             const int win = w + min(p.look, n - j - w);
 #pragma unroll 1
-            for (int rr = 0; rr < kRowsPerPair; ++rr) {
-                const int r = pair * kRowsPerPair + rr;
+            for (int rr = 0; rr < rpp; ++rr) {
+                const int r = pair * rpp + rr;
                 const int row = rows[r];
                 if (row < 0) continue;
                 double *tr = Trun + r * p.trun_stride;
@@ -230,7 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
         const int tile = tile_s;
         if (tile >= ntiles) break;
         if (threadIdx.x < kTileRows) {
-            const int row = p.rowlist[tile * kTileRows + threadIdx.x];
+            const int tr = kPairs * p.rows_per_pair;  // rows in a tile; the slots past them stay empty
+            const int row = threadIdx.x < tr ? p.rowlist[tile * tr + threadIdx.x] : -1;
             rows[threadIdx.x] = row;
             rs[threadIdx.x] = row >= 0 ? p.S[row] : 1.0;
             if (threadIdx.x == 0) k_s = p.row_bits ? (int)p.row_bits[row] : p.k_all;
@@ -253,14 +258,15 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
     }
 }
 
-// Groups rows by width into tiles of 16 (ascending row order inside each width, -1 padding) with one CTA.
-__global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_all, int32_t *rowlist, int *ntiles,
-                                  int *counter) {
+// Groups rows by width into tiles of tile_rows, the widest first (their tiles take longest, so the persistent grid
+// ends on the short ones), ascending row order inside each width, -1 padding; one CTA.
+__global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_all, int tile_rows, int32_t *rowlist,
+                                  int *ntiles, int *counter) {
     __shared__ int base[5];
     __shared__ int warp_sums[32];
     int cursor = 0;
     const int tid = threadIdx.x, nt = blockDim.x;
-    for (int k = 1; k <= 4; ++k) {
+    for (int k = 4; k >= 1; --k) {
         // ascending scan of rows with width k
         int offset = 0;
         for (int64_t a = 0; a < rows; a += nt) {
@@ -282,13 +288,13 @@ __global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_a
             offset += total;
             __syncthreads();
         }
-        const int padded = (offset + kTileRows - 1) / kTileRows * kTileRows;
+        const int padded = (offset + tile_rows - 1) / tile_rows * tile_rows;
         for (int i = offset + tid; i < padded; i += nt) rowlist[cursor + i] = -1;
         cursor += padded;
         __syncthreads();
     }
     if (tid == 0) {
-        *ntiles = cursor / kTileRows;
+        *ntiles = cursor / tile_rows;
         *counter = 0;
     }
     (void)base;
@@ -325,13 +331,21 @@ extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n,
     int32_t *rowlist = reinterpret_cast<int32_t *>(workspace);
     int *ntiles = reinterpret_cast<int *>(rowlist + rows + 4 * kTileRows);
     int *counter = ntiles + 1;
-    group_rows_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(rows, row_bits, k_all, rowlist, ntiles, counter);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // Tiles of 16 rows (two per warp pair) or of 8 (one per pair): 8-row tiles take ~0.54 of the time of 16-row ones
+    // (the run GEMM does not shrink), so they win when the 16-row tiles' last wave would be mostly empty.
+    const int64_t t16 = (rows + 15) / 16 + 4, t8 = (rows + 7) / 8 + 4;  // (+4: per-width padding, at most)
+    const int rpp = (double)((t8 + sms - 1) / sms) * 0.54 < (double)((t16 + sms - 1) / sms) ? 1 : 2;
+    group_rows_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(rows, row_bits, k_all, kPairs * rpp, rowlist, ntiles,
+                                                            counter);
     LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis (grouping)");
     // Trun rows of lazy + look doubles, padded so 2·stride ≡ 24 (mod 32) banks: conflict-free A fragments
     int ts = lazy + look;
     while ((2 * ts) % 32 != 24) ++ts;
     SweepParams p{T, ldT, n, rowlist, ntiles, counter, row_bits, k_all, U, ldU, dead, S, tables,
-                  width, look, lazy, ts, states, settled};
+                  width, look, lazy, ts, rpp, states, settled};
     const size_t smem = (size_t)kTileRows * ts * sizeof(double) + 16 + kUnionBytes;
     cudaError_t e = cudaFuncSetAttribute(sweep_rowtrellis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
@@ -339,10 +353,7 @@ extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n,
         set_error("lamq_ldlq_rowtrellis: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t max_tiles = (rows + kTileRows - 1) / kTileRows + 4;
+    const int64_t max_tiles = rpp == 1 ? t8 : t16;
     const int grid = (int)std::min<int64_t>(max_tiles, sms);
     sweep_rowtrellis_kernel<<<grid, kThreads, smem, (cudaStream_t)stream>>>(p);
     LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis");
