@@ -23,9 +23,9 @@ namespace lamq {
 
 namespace {
 
-constexpr int GM = 128, GN = 64, GK = 16;
+constexpr int GM = 128, GN = 128, GK = 16, GSTAGES = 4;
 constexpr int kGemmThreads = 256;
-constexpr int SA = GK + 4;   // A tile row stride (doubles): 2·SA ≡ 8 (mod 32) banks
+constexpr int SA = GK + 4;   // A tile row stride (doubles): fragment loads hit every bank pair once
 constexpr int SBN = GN + 4;  // B tile (k-major, NN) row stride
 constexpr int SBT = GK + 4;  // B tile (n-major, NT) row stride
 constexpr int NB = 128;      // Cholesky panel / diagonal block
@@ -43,10 +43,11 @@ struct GemmArgs {
     int lower_only;  // skip tiles entirely above the diagonal of C
     int a_lower;     // A is lower triangular (A[m][k] = 0 for k > m): the K loop stops at the tile's last row
     int b_lower;     // the stored B is lower triangular: NN skips k < n, NT skips k > n
+    int vec;         // A and B rows are 16-byte aligned: copy two doubles per cp.async
 };
 
 __device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b) {
-    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+    asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
                  : "+d"(c0), "+d"(c1)
                  : "d"(a), "d"(b));
 }
@@ -56,45 +57,75 @@ __device__ __forceinline__ void cp8(double *dst, const double *src, bool ok) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(ok ? 8 : 0) : "memory");
 }
 
-__device__ __forceinline__ void load_tiles(const GemmArgs &g, double *As, double *Bs, int m0, int n0, int k0) {
-    // A: GM x GK, row-major
-    for (int e = threadIdx.x; e < GM * GK; e += kGemmThreads) {
-        const int r = e / GK, c = e % GK;
-        const bool ok = (m0 + r < g.M) && (k0 + c < g.K);
-        cp8(As + r * SA + c, g.A + (ok ? (int64_t)(m0 + r) * g.lda + k0 + c : 0), ok);
+// Two doubles; `n` (0, 1 or 2) of them read, the rest zero-filled.
+__device__ __forceinline__ void cp16(double *dst, const double *src, int n) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(8 * n) : "memory");
+}
+
+// One thread's share of a tile copy, worked out once per CTA: slot q copies the element pair (r, c..c+1) of a
+// rows x cols tile (cols even, 16-byte copies) or the single element (r, c) (8-byte copies) of a row-major source,
+// zero-filling what lies outside Rmax x Cmax. Per K step only the K offset changes.
+struct TileCopy {
+    static constexpr int kSlots = 8;
+    int n;                    // slots in use
+    int soff[kSlots];         // destination offsets (doubles)
+    int64_t goff[kSlots];     // source offsets (doubles) at K offset 0
+    int rr[kSlots], cc[kSlots];
+};
+
+// `k_rows`: the tile's rows run along K (B without transposition), else its columns do.
+__device__ __forceinline__ void tile_copy_init(TileCopy &t, int ld, int64_t lds, int r0, int c0, int rows, int cols,
+                                               bool vec) {
+    const int per = vec ? cols / 2 : cols;
+    t.n = 0;
+#pragma unroll
+    for (int q = 0; q < TileCopy::kSlots; ++q) {
+        const int e = threadIdx.x + q * kGemmThreads;
+        const int r = e / per, c = vec ? 2 * (e % per) : e % per;
+        t.soff[q] = r * ld + c;
+        t.goff[q] = (int64_t)(r0 + r) * lds + c0 + c;
+        t.rr[q] = r0 + r;
+        t.cc[q] = c0 + c;
+        if (e < rows * per) t.n = q + 1;
     }
-    if (!g.transB) {  // B: GK x GN (k-major)
-        for (int e = threadIdx.x; e < GK * GN; e += kGemmThreads) {
-            const int r = e / GN, c = e % GN;
-            const bool ok = (k0 + r < g.K) && (n0 + c < g.N);
-            cp8(Bs + r * SBN + c, g.B + (ok ? (int64_t)(k0 + r) * g.ldb + n0 + c : 0), ok);
-        }
-    } else {  // B: GN x GK rows of B (n-major)
-        for (int e = threadIdx.x; e < GN * GK; e += kGemmThreads) {
-            const int r = e / GK, c = e % GK;
-            const bool ok = (n0 + r < g.N) && (k0 + c < g.K);
-            cp8(Bs + r * SBT + c, g.B + (ok ? (int64_t)(n0 + r) * g.ldb + k0 + c : 0), ok);
+}
+
+// Issues the copies for a tile whose rows (k_rows) or columns are shifted by k0 along K.
+__device__ __forceinline__ void tile_copy_issue(const TileCopy &t, double *dst, const double *src, int64_t lds, int k0,
+                                                bool k_rows, int Rmax, int Cmax, bool vec) {
+    const int64_t shift = k_rows ? (int64_t)k0 * lds : (int64_t)k0;
+#pragma unroll
+    for (int q = 0; q < TileCopy::kSlots; ++q) {
+        if (q >= t.n) break;
+        const int r = t.rr[q] + (k_rows ? k0 : 0), c = t.cc[q] + (k_rows ? 0 : k0);
+        if (vec) {
+            int nv = (r < Rmax) ? min(2, Cmax - c) : 0;
+            nv = nv < 0 ? 0 : nv;
+            cp16(dst + t.soff[q], src + (nv > 0 ? t.goff[q] + shift : 0), nv);
+        } else {
+            const bool ok = r < Rmax && c < Cmax;
+            cp8(dst + t.soff[q], src + (ok ? t.goff[q] + shift : 0), ok);
         }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 constexpr int kATile = GM * SA;
 constexpr int kBTile = GK * SBN > GN * SBT ? GK * SBN : GN * SBT;
-constexpr size_t kGemmSmem = 2 * (size_t)(kATile + kBTile) * sizeof(double);
+constexpr size_t kGemmSmem = GSTAGES * (size_t)(kATile + kBTile) * sizeof(double);
 
+// C = α·A·B(ᵀ) + β·C on the fp64 tensor cores: 128 x 128 CTA tiles, 8 warps of 64 x 32 (8 x 4 fragments of
+// mma.sync m8n8k4), K in steps of 16 through a 4-stage cp.async ring.
 __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
     extern __shared__ __align__(16) double gsm[];
-    double *As[2] = {gsm, gsm + kATile};
-    double *Bs[2] = {gsm + 2 * kATile, gsm + 2 * kATile + kBTile};
     const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
     if (g.lower_only && m0 + GM - 1 < n0) return;  // every row of the tile is above the diagonal
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;  // warp tile 32 x 32
+    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;  // warp tile 64 x 32
     const int fr = lane >> 2, fk = lane & 3;
-    double acc[4][4][2];
+    double acc[8][4][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
     // the K range that can hold non-zero products for this tile
@@ -105,35 +136,56 @@ __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
         else kb = max(kb, (n0 / GK) * GK);
     }
     const int ksteps = ke > kb ? (ke - kb + GK - 1) / GK : 0;
-    if (ksteps > 0) load_tiles(g, As[0], Bs[0], m0, n0, kb);
-    for (int ks = 0; ks < ksteps; ++ks) {
-        const int cur = ks & 1;
-        if (ks + 1 < ksteps) {
-            load_tiles(g, As[cur ^ 1], Bs[cur ^ 1], m0, n0, kb + (ks + 1) * GK);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
-        __syncthreads();
-        const double *A = As[cur], *B = Bs[cur];
+    auto As = [&](int s) { return gsm + (size_t)s * (kATile + kBTile); };
+    auto Bs = [&](int s) { return gsm + (size_t)s * (kATile + kBTile) + kATile; };
+    const bool vec = g.vec != 0;
+    TileCopy ca, cb;
+    tile_copy_init(ca, SA, g.lda, m0, 0, GM, GK, vec);  // A: GM x GK at (m0, k)
+    if (!g.transB) tile_copy_init(cb, SBN, g.ldb, 0, n0, GK, GN, vec);  // B: GK x GN at (k, n0)
+    else tile_copy_init(cb, SBT, g.ldb, n0, 0, GN, GK, vec);            // B: GN x GK at (n0, k)
+    auto load = [&](int s, int k0) {
+        tile_copy_issue(ca, As(s), g.A, g.lda, k0, false, g.M, g.K, vec);
+        if (!g.transB) tile_copy_issue(cb, Bs(s), g.B, g.ldb, k0, true, g.K, g.N, vec);
+        else tile_copy_issue(cb, Bs(s), g.B, g.ldb, k0, false, g.N, g.K, vec);
+    };
 #pragma unroll
-        for (int kk = 0; kk < GK; kk += 4) {
-            double a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = A[(wm + 8 * i + fr) * SA + kk + fk];
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                b[j] = g.transB ? B[(wn + 8 * j + fr) * SBT + kk + fk] : B[(kk + fk) * SBN + wn + 8 * j + fr];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) dmma(acc[i][j][0], acc[i][j][1], a[i], b[j]);
-        }
-        __syncthreads();
+    for (int s = 0; s < GSTAGES - 1; ++s) {
+        if (s < ksteps) load(s, kb + s * GK);
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
+    for (int ks = 0; ks < ksteps; ++ks) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(GSTAGES - 2) : "memory");
+        __syncthreads();  // stage ks is in, and stage ks − 1 is free for the next load
+        const int nxt = ks + GSTAGES - 1;
+        if (nxt < ksteps) load(nxt % GSTAGES, kb + nxt * GK);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const double *A = As(ks % GSTAGES), *B = Bs(ks % GSTAGES);
+        double a[2][8], b[2][4];  // fragments of this K slice and the next, loaded one slice ahead
+        auto frag = [&](int kk, double (&fa)[8], double (&fb)[4]) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) fa[i] = A[(wm + 8 * i + fr) * SA + kk + fk];
+            if (g.transB) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) fb[j] = B[(wn + 8 * j + fr) * SBT + kk + fk];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) fb[j] = B[(kk + fk) * SBN + wn + 8 * j + fr];
+            }
+        };
+        frag(0, a[0], b[0]);
+#pragma unroll
+        for (int q = 0; q < GK / 4; ++q) {
+            if (q + 1 < GK / 4) frag(4 * (q + 1), a[(q + 1) & 1], b[(q + 1) & 1]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma(acc[i][j][0], acc[i][j][1], a[q & 1][i], b[q & 1][j]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     // C fragment: row fr, columns 2·fk, 2·fk + 1 of each 8 x 8 block
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
         const int r = m0 + wm + 8 * i + fr;
         if (r >= g.M) continue;
 #pragma unroll
@@ -304,7 +356,8 @@ int dgemm(cudaStream_t s, int transB, int M, int N, int K, double alpha, const d
         cudaFuncSetAttribute(dgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
         attr = true;
     }
-    GemmArgs g{M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, transB, lower_only, a_lower, b_lower};
+    const bool vec = ((uintptr_t)A % 16 == 0) && (lda % 2 == 0) && ((uintptr_t)B % 16 == 0) && (ldb % 2 == 0);
+    GemmArgs g{M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, transB, lower_only, a_lower, b_lower, vec ? 1 : 0};
     dim3 grid((N + GN - 1) / GN, (M + GM - 1) / GM);
     dgemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(g);
     LAMQ_CHECK_LAUNCH("dgemm");
