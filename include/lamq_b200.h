@@ -98,11 +98,11 @@ int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *value
  *           width + look <= 24, lazy a multiple of width.
  * states:   rows x n int16 out (ldStates = n): the trellis states.
  * settled:  rows x n fp64 out or NULL: the settled table values, in units of the row scale.
- * workspace: lamq_ldlq_rowtrellis_workspace_size(rows) bytes of device memory (the rows grouped by width into tiles
- *           of 16, and a tile counter).
+ * workspace: lamq_ldlq_rowtrellis_workspace_size(rows, n) bytes of device memory (the rows grouped by width into
+ *           tiles, per-run tile counters, each row's last state, and the run's z per row: about rows x 1 KiB).
  * Supported: L = 12; width + look <= 24; lazy <= 128 and a multiple of 4.
  */
-size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows);
+size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows, int n);
 int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,
                          const uint8_t *dead, const double *S, const double *tables, const uint8_t *row_bits, int k_all,
                          int L, int width, int look, int lazy, int16_t *states, double *settled, void *workspace,

@@ -50,7 +50,7 @@ SIGNATURES = {
     "lamq_unpack_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _I64, _P]),
     "lamq_decode_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _P]),
     "lamq_trellis_product": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P]),
-    "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64]),
+    "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64, _I32]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),
 }

@@ -276,7 +276,7 @@ def _row_trellis_sweep(X, S, env, code, row_bits=None, settled_out=True):
     if row_bits is None:
         tables[code.k - 1] = code.values.to(dev)
     dead = env.dead.to(dev, torch.uint8) if bool(env.dead.any()) else None
-    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows), dtype=torch.uint8, device=dev)
+    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows, n), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         check(_lib.load().lamq_ldlq_rowtrellis(
             ptr(T), n, rows, n, ptr(env.U), env.U.stride(0), ptr(dead), ptr(S.contiguous()), ptr(tables),

@@ -17,6 +17,6 @@ void set_error(const char *fmt, ...) {
 
 }  // namespace lamq
 
-extern "C" int lamq_abi_version(void) { return 3; }
+extern "C" int lamq_abi_version(void) { return 4; }
 
 extern "C" const char *lamq_last_error(void) { return lamq::g_error; }

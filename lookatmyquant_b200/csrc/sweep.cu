@@ -1,23 +1,21 @@
-// The block-LDLQ sweep with a row trellis (the lm2 build's per-matrix loop), fused into one persistent kernel.
+// The block-LDLQ sweep with a row trellis (the lm2 build's per-matrix loop).
 //
 // Reference: opgraph/syntax.py:86-124 (`sweep`), with the projection of opgraph/codes.py:442-450 and
-// RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so rows are grouped by
-// their width k into tiles of 16 rows (or 8, when 16-row tiles would leave the last wave of CTAs mostly empty) and
-// each tile is swept start to finish by one CTA of 16 warps: 8 warp pairs, each decoding its 2 rows (or 1) in turn
-// (trellis_pair.cuh: 64 states per thread, fp32x2 arithmetic):
+// RowTrellisCode.step (codes.py:397-404). Rows never interact under Refit (codes.py:417-418), so inside a run of
+// `lazy` columns every row is independent; across runs, the run's errors reach all later columns of all rows through
+// one matrix product. The sweep is therefore a sequence of runs, each two launches:
 //
-//   per run of `lazy` columns [b0, b1):
-//     the run's targets plus the `look` columns after it are copied from T into shared memory (Trun);
-//     per block of `width` columns, each pair, for each of its rows: decodes the block plus `look` columns ahead (in
-//       units of the row scale, from the row's last state; the look-ahead past b1 is stale by design, as in the
-//       reference), settles the block with the fp64 table values, writes the columns as they stood to T (what sweep
-//       returns), solves z·U_BB = E by substitution, keeps z in the block's Trun slots, and updates the rest of the
-//       run in shared memory (syntax.py:117-120);
-//     then the whole CTA applies the run to every later column, T[:, b1:] -= Z·U[b0:b1, b1:] (syntax.py:122-123), as
-//       an fp64 tensor-core GEMM (mma.sync m8n8k4 f64) over 16 rows, U staged through shared memory by cp.async so
-//       each U element crosses L2 once per 16 rows.
-// Tiles are taken from a work counter (persistent grid), the widest rows first, so tiles of different widths and
-// matrix sizes balance.
+//   sweep_run_kernel — rows grouped by their width k into tiles of 16 rows (or 8, when 16-row tiles would leave the
+//     last wave of CTAs mostly empty), a persistent grid taking tiles from a counter, widest rows first; per tile the
+//     run's targets plus the `look` columns after it go to shared memory (Trun), and 8 warp pairs (trellis_pair.cuh:
+//     64 states per thread, fp32x2 arithmetic) take its rows in turn: per block of `width` columns each pair decodes
+//     the block plus `look` columns ahead (in units of the row scale, from the row's last state; the look-ahead past
+//     the run is stale by design, as in the reference), settles the block with the fp64 table values, writes the
+//     columns as they stood to T (what sweep returns), solves z·U_BB = E by substitution, keeps z in the block's Trun
+//     slots and updates the rest of the run in shared memory (syntax.py:117-120); at the end of the run the tile's z
+//     go to Z and each row's last state to a per-row array for the next run;
+//   lamq_dgemm — T[:, b1:] −= Z·U[b0:b1, b1:] for all rows at once (syntax.py:122-123), on the fp64 tensor cores,
+//     each U element read once per 128 rows instead of once per tile.
 #include <algorithm>
 
 #include "lamq_common.cuh"
@@ -34,8 +32,6 @@ constexpr int kMaxRowsPerPair = 2;
 constexpr int kTileRows = kPairs * kMaxRowsPerPair;  // 16: the largest tile (8 when each pair takes one row)
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxWin = 24;  // RowTrellisCode windows: width 16 + look 8
-constexpr int kGemmCols = 64;                      // columns of U per GEMM stage (8 per warp)
-constexpr int kUStride = kGemmCols + 4;            // padded row of a staged U tile (conflict-free B fragments)
 constexpr int kMaxLazy = 128;
 
 struct SweepParams {
@@ -44,7 +40,7 @@ struct SweepParams {
     int n;
     const int32_t *rowlist;   // tiles of tile_rows row indices grouped by width (widest first), -1 = padding
     const int *ntiles;        // device: number of tiles
-    int *counter;             // device: next tile to take
+    int *counters;            // device: per run, the next tile to take
     const uint8_t *row_bits;  // per-row width or null
     int k_all;
     const double *U;
@@ -55,86 +51,26 @@ struct SweepParams {
     int width, look, lazy;
     int trun_stride;          // doubles per Trun row
     int rows_per_pair;        // 1 or 2: tiles of 8 or 16 rows
+    double *Z;                // rows x kMaxLazy: each row's z over the run (the run product's left factor)
+    int *rstate;              // rows: each row's last state after the runs so far
+    int b0, b1, run;          // this launch's run [b0, b1)
     int16_t *states;
     double *settled;
 };
 
 // Per-pair Viterbi scratch, carved per width: two best buffers of R floats and kMaxWin steps of back-pointers (WORDS x
-// 64 words each) — at most 22 KiB (k = 1) — and 8 words for the final reduction. The GEMM at the end of each run
-// reuses this space.
+// 64 words each) — at most 22 KiB (k = 1) — and 8 words for the final reduction.
 template <int K>
 constexpr size_t pair_bytes() {
     return 2 * (size_t)PairTrellis<K>::R * sizeof(float) + (size_t)kMaxWin * 64 * PairTrellis<K>::WORDS * sizeof(uint32_t);
 }
 constexpr size_t kPairMax = pair_bytes<1>() > pair_bytes<2>() ? pair_bytes<1>() : pair_bytes<2>();
 constexpr size_t kPairViterbiBytes = kPairMax + 8 * sizeof(float);
-constexpr size_t kGemmBytes = 2 * (size_t)kMaxLazy * kUStride * sizeof(double);
-constexpr size_t kUnionBytes = (kPairs * kPairViterbiBytes > kGemmBytes) ? kPairs * kPairViterbiBytes : kGemmBytes;
-
-__device__ __forceinline__ void dmma_8x8x4(double &c0, double &c1, double a, double b) {
-    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
-                 : "+d"(c0), "+d"(c1)
-                 : "d"(a), "d"(b));
-}
-
-__device__ __forceinline__ void cp_async8(void *dst, const void *src, bool valid) {
-    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-
-// Stages U[b0 : b0+nr, c0 : c0+64] into Us (rows of kUStride doubles); columns at or past n read as zero.
-__device__ __forceinline__ void stage_u(double *Us, const SweepParams &p, int b0, int nr, int c0) {
-    for (int e = threadIdx.x; e < nr * kGemmCols; e += kThreads) {
-        const int i = e / kGemmCols, c = e % kGemmCols;
-        const bool ok = c0 + c < p.n;
-        cp_async8(Us + i * kUStride + c, p.U + (int64_t)(b0 + i) * p.ldU + (ok ? c0 + c : 0), ok);
-    }
-}
-
-// T[row][b1:] -= Z·U[b0:b1, b1:] for the tile's rows (Z in the Trun slots of the run's columns), fp64 tensor cores.
-__device__ void run_update(const SweepParams &p, double *Trun, const int *rows, double *gemm, int b0, int b1) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nr = b1 - b0;  // a multiple of 4 (lazy is a multiple of width, runs before the last are full)
-    double *Us[2] = {gemm, gemm + (size_t)kMaxLazy * kUStride};
-    const int nchunks = (p.n - b1 + kGemmCols - 1) / kGemmCols;
-    stage_u(Us[0], p, b0, nr, b1);
-    cp_async_commit();
-    const int ar = lane >> 2, ak = lane & 3;  // A fragment: row ar, k ak; B fragment: k ak, column ar
-    const int mt = warp >> 3, cg = warp & 7;   // this warp: rows 8·mt.., columns 8·cg.. of each 64-column chunk
-    const int r0 = rows[8 * mt + ar];
-    for (int ch = 0; ch < nchunks; ++ch) {
-        const int c0 = b1 + ch * kGemmCols;
-        if (ch + 1 < nchunks) {
-            stage_u(Us[(ch + 1) & 1], p, b0, nr, c0 + kGemmCols);
-            cp_async_commit();
-            cp_async_wait_one();
-        } else {
-            cp_async_wait_all();
-        }
-        __syncthreads();
-        const double *Ut = Us[ch & 1];
-        const int col = c0 + 8 * cg + 2 * ak;  // this thread's two output columns: col, col + 1
-        double c[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) c[e] = (r0 >= 0 && col + e < p.n) ? p.T[(int64_t)r0 * p.ldT + col + e] : 0.0;
-        const double *Ua = Ut + 8 * cg + ar;
-        const double *Za = Trun + (8 * mt + ar) * p.trun_stride + ak;
-#pragma unroll 8
-        for (int ks = 0; ks < nr; ks += 4) dmma_8x8x4(c[0], c[1], -Za[ks], Ua[(ks + ak) * kUStride]);
-        // D fragment: row ar, columns 2·ak, 2·ak + 1 of the warp's 8
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-            if (r0 >= 0 && col + e < p.n) p.T[(int64_t)r0 * p.ldT + col + e] = c[e];
-        __syncthreads();  // the stage buffer is refilled two chunks later
-    }
-}
+constexpr size_t kUnionBytes = kPairs * kPairViterbiBytes;
 
 template <int K>
 __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *rs, double *Trun, unsigned char *vregion,
-                           double *gemm, int *row_state) {
+                           int *row_state) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pair = warp >> 1, pt = (warp & 1) * 32 + lane, bar = 1 + pair;
     const bool lead = (warp & 1) == 0;  // the pair's first warp settles and refits its rows
@@ -146,13 +82,16 @@ __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *
     float *best1 = best0 + PairTrellis<K>::R;
     uint32_t *args = reinterpret_cast<uint32_t *>(best1 + PairTrellis<K>::R);
     float *red = reinterpret_cast<float *>(wv + kPairMax);
-    // each row's last state, shared by the pair; outside the Viterbi scratch, which the run's GEMM reuses
+    // each row's last state, shared by the pair
     const int rpp = p.rows_per_pair;
     int *pstate = row_state + pair * rpp;
     const int n = p.n;
-    if (pt < rpp) pstate[pt] = 0;  // every row's path starts at state 0 (codes.py:399-400)
-    for (int b0 = 0; b0 < n; b0 += p.lazy) {
-        const int b1 = min(b0 + p.lazy, n);
+    if (pt < rpp) {  // every row's path starts at state 0 (codes.py:399-400), later runs where the last one ended
+        const int row = rows[pair * rpp + pt];
+        pstate[pt] = (p.b0 > 0 && row >= 0) ? p.rstate[row] : 0;
+    }
+    {
+        const int b0 = p.b0, b1 = p.b1;
         const int ncol = b1 - b0 + min(p.look, n - b1);
         for (int e = threadIdx.x; e < kTileRows * ncol; e += kThreads) {
             const int r = e / ncol, c = e % ncol;
@@ -214,11 +153,20 @@ __device__ void sweep_tile(const SweepParams &p, const int *rows, const double *
             }
         }
         __syncthreads();
-        if (b1 < n) run_update(p, Trun, rows, gemm, b0, b1);
+        // the run's z (the Trun slots of its columns) and each row's last state, for the run product and the next run
+        const int nr = b1 - b0;
+        for (int e = threadIdx.x; e < kTileRows * nr; e += kThreads) {
+            const int r = e / nr, c = e % nr;
+            if (rows[r] >= 0) p.Z[(int64_t)rows[r] * kMaxLazy + c] = Trun[r * p.trun_stride + c];
+        }
+        if (pt < rpp) {
+            const int row = rows[pair * rpp + pt];
+            if (row >= 0) p.rstate[row] = pstate[pt];
+        }
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepParams p) {
+__global__ void __launch_bounds__(kThreads, 1) sweep_run_kernel(SweepParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     double *Trun = reinterpret_cast<double *>(smem);
     unsigned char *uni = smem + (size_t)kTileRows * p.trun_stride * sizeof(double);
@@ -229,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
     __shared__ int tile_s, k_s;
     const int ntiles = *p.ntiles;
     for (;;) {
-        if (threadIdx.x == 0) tile_s = atomicAdd(p.counter, 1);
+        if (threadIdx.x == 0) tile_s = atomicAdd(p.counters + p.run, 1);
         __syncthreads();
         const int tile = tile_s;
         if (tile >= ntiles) break;
@@ -242,17 +190,17 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
         }
         __syncthreads();
         // dead inputs: their targets start at zero (syntax.py:100-101)
-        if (p.dead != nullptr)
+        if (p.dead != nullptr && p.b0 == 0)
             for (int e = threadIdx.x; e < kTileRows * p.n; e += kThreads) {
                 const int r = e / p.n, c = e % p.n;
                 if (rows[r] >= 0 && p.dead[c]) p.T[(int64_t)rows[r] * p.ldT + c] = 0.0;
             }
         __syncthreads();
         switch (k_s) {
-            case 1: sweep_tile<1>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
-            case 2: sweep_tile<2>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
-            case 3: sweep_tile<3>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
-            default: sweep_tile<4>(p, rows, rs, Trun, uni, reinterpret_cast<double *>(uni), row_state); break;
+            case 1: sweep_tile<1>(p, rows, rs, Trun, uni, row_state); break;
+            case 2: sweep_tile<2>(p, rows, rs, Trun, uni, row_state); break;
+            case 3: sweep_tile<3>(p, rows, rs, Trun, uni, row_state); break;
+            default: sweep_tile<4>(p, rows, rs, Trun, uni, row_state); break;
         }
         __syncthreads();
     }
@@ -261,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_rowtrellis_kernel(SweepPara
 // Groups rows by width into tiles of tile_rows, the widest first (their tiles take longest, so the persistent grid
 // ends on the short ones), ascending row order inside each width, -1 padding; one CTA.
 __global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_all, int tile_rows, int32_t *rowlist,
-                                  int *ntiles, int *counter) {
+                                  int *ntiles, int *counters, int nruns) {
     __shared__ int base[5];
     __shared__ int warp_sums[32];
     int cursor = 0;
@@ -293,10 +241,8 @@ __global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_a
         cursor += padded;
         __syncthreads();
     }
-    if (tid == 0) {
-        *ntiles = cursor / tile_rows;
-        *counter = 0;
-    }
+    if (tid == 0) *ntiles = cursor / tile_rows;
+    for (int r = tid; r < nruns; r += nt) counters[r] = 0;
     (void)base;
 }
 
@@ -306,9 +252,25 @@ __global__ void group_rows_kernel(int64_t rows, const uint8_t *row_bits, int k_a
 
 using namespace lamq;
 
-extern "C" size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows) {
-    if (rows <= 0) return 0;
-    return (size_t)(rows + 4 * kTileRows) * sizeof(int32_t) + 64;
+// Workspace: the tile list, per-run tile counters, each row's last state and the run's z per row.
+struct SweepLayout {
+    size_t rowlist, counters, rstate, z, total;
+};
+
+static SweepLayout sweep_layout(int64_t rows, int n) {
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    SweepLayout l{};
+    l.rowlist = up((size_t)(rows + 4 * kTileRows + 2) * sizeof(int32_t));  // + the tile count
+    l.counters = up((size_t)((n + 3) / 4 + 1) * sizeof(int));             // runs are at least 4 columns
+    l.rstate = up((size_t)rows * sizeof(int));
+    l.z = up((size_t)rows * kMaxLazy * sizeof(double));
+    l.total = l.rowlist + l.counters + l.rstate + l.z;
+    return l;
+}
+
+extern "C" size_t lamq_ldlq_rowtrellis_workspace_size(int64_t rows, int n) {
+    if (rows <= 0 || n <= 0) return 0;
+    return sweep_layout(rows, n).total;
 }
 
 extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n, const double *U, int64_t ldU,
@@ -325,37 +287,51 @@ extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n,
     LAMQ_REQUIRE(lazy >= width && lazy % width == 0 && lazy <= kMaxLazy && lazy % 4 == 0,
                  "lamq_ldlq_rowtrellis: lazy must be a multiple of width and of 4, at most 128");
     LAMQ_REQUIRE(row_bits != nullptr || (k_all >= 1 && k_all <= 4), "lamq_ldlq_rowtrellis: k must be 1..4");
-    const size_t need = lamq_ldlq_rowtrellis_workspace_size(rows);
-    LAMQ_REQUIRE(workspace != nullptr && workspace_bytes >= need,
-                 "lamq_ldlq_rowtrellis: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    int32_t *rowlist = reinterpret_cast<int32_t *>(workspace);
+    LAMQ_REQUIRE(rows <= INT32_MAX, "lamq_ldlq_rowtrellis: too many rows");
+    const SweepLayout l = sweep_layout(rows, n);
+    LAMQ_REQUIRE(workspace != nullptr && workspace_bytes >= l.total,
+                 "lamq_ldlq_rowtrellis: workspace of %zu bytes needed, %zu given", l.total, workspace_bytes);
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t *base = reinterpret_cast<uint8_t *>(workspace);
+    int32_t *rowlist = reinterpret_cast<int32_t *>(base);
     int *ntiles = reinterpret_cast<int *>(rowlist + rows + 4 * kTileRows);
-    int *counter = ntiles + 1;
+    int *counters = reinterpret_cast<int *>(base + l.rowlist);
+    int *rstate = reinterpret_cast<int *>(base + l.rowlist + l.counters);
+    double *Z = reinterpret_cast<double *>(base + l.rowlist + l.counters + l.rstate);
+    const int nruns = (n + lazy - 1) / lazy;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // Tiles of 16 rows (two per warp pair) or of 8 (one per pair): 8-row tiles take ~0.54 of the time of 16-row ones
-    // (the run GEMM does not shrink), so they win when the 16-row tiles' last wave would be mostly empty.
+    // Tiles of 16 rows (two per warp pair) or of 8 (one per pair, about half the time): 8-row tiles win when the
+    // 16-row tiles' last wave would be mostly empty.
     const int64_t t16 = (rows + 15) / 16 + 4, t8 = (rows + 7) / 8 + 4;  // (+4: per-width padding, at most)
-    const int rpp = (double)((t8 + sms - 1) / sms) * 0.54 < (double)((t16 + sms - 1) / sms) ? 1 : 2;
-    group_rows_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(rows, row_bits, k_all, kPairs * rpp, rowlist, ntiles,
-                                                            counter);
+    const int rpp = (double)((t8 + sms - 1) / sms) * 0.5 < (double)((t16 + sms - 1) / sms) ? 1 : 2;
+    group_rows_kernel<<<1, 1024, 0, s>>>(rows, row_bits, k_all, kPairs * rpp, rowlist, ntiles, counters, nruns);
     LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis (grouping)");
-    // Trun rows of lazy + look doubles, padded so 2·stride ≡ 24 (mod 32) banks: conflict-free A fragments
+    // Trun rows of lazy + look doubles, padded to an odd number of 16-byte units (conflict-free row starts)
     int ts = lazy + look;
     while ((2 * ts) % 32 != 24) ++ts;
-    SweepParams p{T, ldT, n, rowlist, ntiles, counter, row_bits, k_all, U, ldU, dead, S, tables,
-                  width, look, lazy, ts, rpp, states, settled};
+    SweepParams p{T, ldT, n, rowlist, ntiles, counters, row_bits, k_all, U, ldU, dead, S, tables,
+                  width, look, lazy, ts, rpp, Z, rstate, 0, 0, 0, states, settled};
     const size_t smem = (size_t)kTileRows * ts * sizeof(double) + 16 + kUnionBytes;
-    cudaError_t e = cudaFuncSetAttribute(sweep_rowtrellis_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(sweep_run_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
         set_error("lamq_ldlq_rowtrellis: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
     }
     const int64_t max_tiles = rpp == 1 ? t8 : t16;
     const int grid = (int)std::min<int64_t>(max_tiles, sms);
-    sweep_rowtrellis_kernel<<<grid, kThreads, smem, (cudaStream_t)stream>>>(p);
-    LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis");
+    for (int run = 0; run < nruns; ++run) {
+        p.run = run;
+        p.b0 = run * lazy;
+        p.b1 = std::min(p.b0 + lazy, n);
+        sweep_run_kernel<<<grid, kThreads, smem, s>>>(p);
+        LAMQ_CHECK_LAUNCH("lamq_ldlq_rowtrellis");
+        if (p.b1 < n) {  // the run's errors reach every later column: T[:, b1:] −= Z·U[b0:b1, b1:]
+            const int st = lamq_dgemm(0, (int)rows, n - p.b1, p.b1 - p.b0, -1.0, Z, kMaxLazy,
+                                      U + (int64_t)p.b0 * ldU + p.b1, ldU, 1.0, T + p.b1, ldT, stream);
+            if (st != LAMQ_OK) return st;
+        }
+    }
     return LAMQ_OK;
 }

@@ -226,7 +226,7 @@ def sweep_rows(X, S, env, row_bits, tables=None):
     settled = torch.empty(rows, n, dtype=torch.float64, device=dev)
     tables = stacked_tables(12, 256, dev) if tables is None else tables
     dead = env.dead.to(dev, torch.uint8) if bool(env.dead.any()) else None
-    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows), dtype=torch.uint8, device=dev)
+    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows, n), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         check(_lib.load().lamq_ldlq_rowtrellis(
             ptr(T), n, rows, n, ptr(env.U), env.U.stride(0), ptr(dead), ptr(S.contiguous()), ptr(tables),

@@ -24,7 +24,7 @@ def kernel_sweep(X, S, U, dead, k, row_bits=None, width=16, look=8):
     tabs = stacked_tables(12, 256, dev)
     states = torch.empty(rows, n, dtype=torch.int16, device=dev)
     settled = torch.empty(rows, n, dtype=torch.float64, device=dev)
-    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows), dtype=torch.uint8, device=dev)
+    ws = torch.empty(_lib.load().lamq_ldlq_rowtrellis_workspace_size(rows, n), dtype=torch.uint8, device=dev)
     _lib.check(_lib.load().lamq_ldlq_rowtrellis(
         T.data_ptr(), n, rows, n, Ut.data_ptr(), n, None if dd is None else dd.data_ptr(), St.data_ptr(),
         tabs.data_ptr(), None if rb is None else rb.data_ptr(), k, 12, width, look, 128, states.data_ptr(),
