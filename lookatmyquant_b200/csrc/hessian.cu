@@ -13,14 +13,16 @@
 //              thread fills the other one; at the end of a unit they add the tile into the fp32 d × d accumulator in
 //              global memory (coalesced: written transposed).
 // The tensor core's own fp32 accumulation truncates (it loses about half an ulp per MMA on average, always towards
-// zero), so TMEM only ever accumulates kDrainBlocks × 4 = 32 MMAs (512 tokens) before it is drained into the
-// registers: the bias stays near 1e-6 relative, where a whole chunk in TMEM would bias H by more than the 1e-5 bar.
+// zero), so TMEM only ever accumulates kDrainBlocks × 4 = 64 MMAs (1024 tokens) before it is drained into the
+// registers: the bias stays near 2e-6 relative (measured: 2.2e-6 at d = 2560, 262,144 weighted tokens; 1.1e-6 with
+// 512-token drains, slower by 6 %), where a whole chunk in TMEM would bias H by more than the 1e-5 bar.
 // A work unit is one 128 × 256 output tile over one chunk of tokens. The tiles are listed band by band (bands of about
 // 16 row tiles, column by column inside a band) and cut into windows of exactly one tile per CTA; units run window by
 // window, chunk by chunk inside a window. So each wave of CTAs computes one window over one chunk: a compact block of
 // about 16 × 9 tiles whose CTAs read the same A and B tiles at about the same time and share them through L2. For H
-// only tiles that
-// hold a pair i <= j are computed (H is symmetric); the finalize kernel mirrors them.
+// only tiles that hold a pair i <= j are computed (H is symmetric); the finalize kernel mirrors them.
+// From d = 512 on, xtx_pair_kernel (below) computes 256 × 256 tiles on pairs of CTAs (cta_group::2 MMAs): half the
+// operand bytes per CTA per flop, a 6-stage ring.
 //
 // Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
 // (A = X, B = X: exact products), and the weighted tokens add Σ_t (w_t − 1)·x_t x_tᵀ in a second pass over only
@@ -48,7 +50,7 @@ constexpr int B_BYTES = BN * BK * 2;  // 32 KiB: four boxes
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int HALF_BYTES = 64 * BK * 2;  // one TMA box: 64 columns x 64 tokens = 8 KiB (LBO between MN blocks)
 constexpr int kBandTarget = 16;          // row tiles per band (bands are evened out to at most this many)
-constexpr int kDrainBlocks = 8;          // 64-token blocks accumulated in TMEM between drains (32 MMAs)
+constexpr int kDrainBlocks = 16;         // 64-token blocks accumulated in TMEM between drains (64 MMAs)
 constexpr int kEpiWarps = 8;             // two per TMEM lane quadrant, 128 columns each
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;      // two 128 x 256 fp32 accumulators
@@ -74,6 +76,7 @@ struct GemmParams {
     int kblocks;            // total 64-token blocks
     int kblocks_per_chunk;
     int symmetric;
+    int pair;               // tiles of 256 x 256 computed by a pair of CTAs (cta_group::2), else 128 x 256 per CTA
     int64_t units;
     int *status;
     unsigned int *gate;     // units whose loads have all been issued (the wave gate), zeroed before the launch
@@ -86,7 +89,8 @@ struct Unit {
 // Tiles of column tj inside the band of row tiles [b0, b1). Symmetric C: row tile ti (rows 128·ti..) and column tile
 // tj (columns 256·tj..) hold a pair i <= j iff tj >= ti / 2, that is ti < 2·tj + 2.
 __device__ __forceinline__ int band_column(int b0, int b1, int tj, const GemmParams &p) {
-    return p.symmetric ? max(0, min(b1, 2 * tj + 2) - b0) : b1 - b0;
+    // paired tiles are square: row tile ti holds a pair i <= j iff ti <= tj
+    return p.symmetric ? max(0, min(b1, p.pair ? tj + 1 : 2 * tj + 2) - b0) : b1 - b0;
 }
 
 // The idx-th tile of the band raster (bands top to bottom, columns left to right, rows top to bottom).
@@ -331,6 +335,199 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// The same contraction with 256 x 256 tiles computed by a pair of CTAs (a cluster of two) with cta_group::2 MMAs
+// (M = 256, N = 256, K = 16): each CTA loads its 128 rows of A and its 128 columns of B per 64-token slice (32 KiB
+// instead of 48 KiB for a 128 x 256 tile of its own), so a 6-stage ring fits and covers more of the load latency,
+// and each CTA's TMEM holds its 128 rows x 256 columns. The even CTA issues the MMAs; both CTAs' loads complete on
+// its full barriers; its commits release both CTAs' ring stages and accumulators (multicast commit); both CTAs'
+// drain warps release an accumulator on the even CTA's barrier. No TMA multicast: each CTA loads its own halves.
+constexpr int PSTAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2, P_B_BYTES = 128 * BK * 2, P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr size_t kPairSmemBytes = 1024 + PSTAGES * P_STAGE_BYTES + 256;
+constexpr int kPairBandTarget = 8;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    xtx_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + PSTAGES * P_STAGE_BYTES);
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * PSTAGES + 5);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int64_t cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + PSTAGES);
+    const uint32_t tfull0 = smem_u32(bars + 2 * PSTAGES), tempty0 = smem_u32(bars + 2 * PSTAGES + 2);
+    const uint32_t drain = smem_u32(bars + 2 * PSTAGES + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PSTAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);   // the even CTA's expect_tx (its full barriers count both CTAs' bytes)
+            mbar_init(empty0 + 8 * s, 1);  // the even CTA's multicast commit
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull0 + 8 * a, 1);
+            mbar_init(tempty0 + 8 * a, 2 * kEpiWarps * 32);  // both CTAs' drain threads (used on the even CTA)
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+        prefetch_tmap(&mapA);
+        prefetch_tmap(&mapB);
+    }
+    if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM
+        tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer (both CTAs: each loads its own halves)
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true, gate = leader && p.gate != nullptr;
+            int64_t wave = 0;
+            for (int64_t u = cluster; ok && u < p.units; u += nclusters, ++wave) {
+                Unit U;
+                if (!unit_at(u, p, U)) break;
+                if (gate && wave > 0) {
+                    const unsigned int target = (unsigned int)(wave * nclusters);
+                    const unsigned long long t0 = globaltimer();
+                    while (ld_relaxed_u32(p.gate) < target) {
+                        if (globaltimer() - t0 > kGateTimeoutNs) {
+                            gate = false;
+                            break;
+                        }
+                        __nanosleep(256);
+                    }
+                }
+                const int ra = U.ti * 256 + 128 * (int)rank, rb = U.tj * 256 + 128 * (int)rank;
+                for (int kb = 0; kb < U.nkb; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(full0 + 8 * stage, 2 * P_STAGE_BYTES);
+                    const uint32_t fb = map_to_rank(full0 + 8 * stage, 0);
+                    const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES), sb = sa + P_A_BYTES;
+                    const int t = (U.kb0 + kb) * BK;
+                    tma_load_2d_pair(sa, &mapA, ra, t, fb);
+                    tma_load_2d_pair(sa + HALF_BYTES, &mapA, ra + 64, t, fb);
+                    tma_load_2d_pair(sb, &mapB, rb, t, fb);
+                    tma_load_2d_pair(sb + HALF_BYTES, &mapB, rb + 64, t, fb);
+                    if (++stage == PSTAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (ok && gate) atomicAdd(p.gate, 1u);
+            }
+            if (!ok) __nanosleep(200000);  // error path: the copies in flight land (their barrier is the even CTA's)
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {  // ---- MMA issuer (the even CTA)
+            const uint32_t idesc = idesc_bf16_f32(256, 256, true, true);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t uses[2] = {0, 0};
+            int acc = 0;
+            bool ok = true;
+            for (int64_t u = cluster; ok && u < p.units; u += nclusters) {
+                Unit U;
+                if (!unit_at(u, p, U)) break;
+                for (int sub = 0; ok && sub < U.nkb; sub += kDrainBlocks) {
+                    if (!mbar_wait(tempty0 + 8 * acc, (uses[acc] & 1) ^ 1, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    ++uses[acc];
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * BN;
+                    const int kend = min(U.nkb, sub + kDrainBlocks);
+                    for (int kb = sub; kb < kend; ++kb) {
+                        if (!mbar_wait(full0 + 8 * stage, phase, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES), sb = sa + P_A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint64_t ad = smem_desc_sw128(sa + kk * 2048, HALF_BYTES, 1024);
+                            const uint64_t bd = smem_desc_sw128(sb + kk * 2048, HALF_BYTES, 1024);
+                            mma_f16_ss_pair(d, ad, bd, idesc, (kb > sub || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit_pair_multicast(empty0 + 8 * stage, 0x3);
+                        if (++stage == PSTAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit_pair_multicast(tfull0 + 8 * acc, 0x3);
+                    acc ^= 1;
+                }
+            }
+            // every MMA this thread issued completes before TMEM is released
+            mma_commit_pair(drain);
+            const unsigned long long t0 = globaltimer();
+            while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitTimeoutNs) {
+            }
+        }
+    } else {  // ---- drain warps (both CTAs): warp w reads TMEM lanes 32·(w % 4).., columns 128·((w − 2) / 4)..
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        const uint32_t release = leader ? 0u : 1u;  // the peer's threads arrive on the even CTA's barrier
+        uint32_t uses[2] = {0, 0};
+        int acc = 0;
+        for (int64_t u = cluster; u < p.units; u += nclusters) {
+            Unit U;
+            if (!unit_at(u, p, U)) break;
+            float tile[128];
+#pragma unroll
+            for (int c = 0; c < 128; ++c) tile[c] = 0.f;
+            bool ok = true;
+            for (int sub = 0; sub < U.nkb; sub += kDrainBlocks) {
+                if (!mbar_wait(tfull0 + 8 * acc, uses[acc] & 1, p.status)) {
+                    ok = false;
+                    break;
+                }
+                ++uses[acc];
+                tc_fence_after();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + acc * BN + 128 * half;
+#pragma unroll
+                for (int c = 0; c < 128 / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) tile[c * 32 + e] = __fadd_rn(tile[c * 32 + e], __uint_as_float(r[e]));
+                }
+                tc_fence_before();
+                if (release) mbar_arrive_cluster(map_to_rank(tempty0 + 8 * acc, 0));
+                else mbar_arrive(tempty0 + 8 * acc);
+                acc ^= 1;
+            }
+            if (!ok) break;
+            const int i = U.ti * 256 + 128 * (int)rank + 32 * q + lane;
+            if (i < p.d) {
+#pragma unroll
+                for (int c = 0; c < 128; ++c) {
+                    const int j = U.tj * BN + 128 * half + c;
+                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, tile[c]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // neither CTA leaves while the pair's MMAs or arrivals may still touch it
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
 // Weighted tokens: out_plain rows r and r + nw hold plain[idx[r]]; out_split row r holds hi and row r + nw holds lo
 // of y = (w[idx[r]] − 1)·scaled[idx[r]] (fp32), hi = bf16(y), lo = bf16(y − hi).
 __global__ void weighted_split_kernel(const __nv_bfloat16 *__restrict__ scaled, int64_t lds,
@@ -481,10 +678,14 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     p.acc = acc;
     p.ldc = ldacc;
     p.d = d;
-    p.nti = (d + BM - 1) / BM;
+    // contractions of d >= 512 run on CTA pairs (256 x 256 tiles), smaller ones on single CTAs (128 x 256)
+    p.pair = d >= 512 ? 1 : 0;
+    const int tm = p.pair ? 256 : BM;
+    p.nti = (d + tm - 1) / tm;
     p.ntj = (d + BN - 1) / BN;
     {
-        const int nb = (p.nti + kBandTarget - 1) / kBandTarget;
+        const int target = p.pair ? kPairBandTarget : kBandTarget;
+        const int nb = (p.nti + target - 1) / target;
         p.band = (p.nti + nb - 1) / nb;
     }
     p.kblocks = (int)((tokens + BK - 1) / BK);
@@ -493,19 +694,48 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     p.symmetric = symmetric ? 1 : 0;
     p.status = status;
     int64_t tiles = 0;
-    for (int ti = 0; ti < p.nti; ++ti) tiles += symmetric ? std::max(0, p.ntj - ti / 2) : p.ntj;
+    for (int ti = 0; ti < p.nti; ++ti)
+        tiles += symmetric ? std::max(0, p.ntj - (p.pair ? ti : ti / 2)) : p.ntj;
     p.units = tiles * p.nchunk;
     p.ntiles = tiles;
-    cudaError_t e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    if (e != cudaSuccess) {
-        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
-        return LAMQ_ERR_CUDA;
-    }
-    const int64_t grid = p.units < num_sms() ? p.units : num_sms();
-    p.win = (int)grid;
     st = gate_counter((cudaStream_t)stream, &p.gate);
     if (st != LAMQ_OK) return st;
-    xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
+    cudaError_t e;
+    if (p.pair) {
+        const int64_t clusters = std::min<int64_t>(p.units, num_sms() / 2);
+        p.win = (int)clusters;
+        e = cudaFuncSetAttribute(xtx_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes);
+        if (e != cudaSuccess) {
+            set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = kPairSmemBytes;
+        cfg.stream = (cudaStream_t)stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, xtx_pair_kernel, ma, mb, p);
+        if (e != cudaSuccess) {
+            set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+    } else {
+        e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        if (e != cudaSuccess) {
+            set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        const int64_t grid = p.units < num_sms() ? p.units : num_sms();
+        p.win = (int)grid;
+        xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
+    }
     LAMQ_CHECK_LAUNCH("lamq_xtx_accumulate");
     return LAMQ_OK;
 }
