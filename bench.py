@@ -454,7 +454,7 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
-    launches0 = _lib.LAUNCHES["count"]
+    launches0 = _lib.kernel_launches()
     with Clocks(local) as clk:
         for i in range(args.steps):
             flush.zero_()
@@ -463,7 +463,7 @@ def main():
             ends[i].record()
         barrier()
         ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
-    launches = (_lib.LAUNCHES["count"] - launches0) // args.steps
+    launches = (_lib.kernel_launches() - launches0) // args.steps
     # e2e: the same build through the public API from pinned host memory, result read back, every step
     wl.prepare_e2e()
     e2e_ms = []

@@ -54,6 +54,9 @@ int lamq_abi_version(void);
 /* Text of the last error raised on the calling host thread ("" if none). */
 const char *lamq_last_error(void);
 
+/* Kernels this library has launched in the process (all threads): what a benchmark counts as its own launches. */
+uint64_t lamq_kernel_launches(void);
+
 /*
  * Viterbi over a bitshift trellis (opgraph/codes.py:151-181).
  * X: rows x T fp32 (ldX = T); values: 2^L fp32 table; start: rows int64 states or NULL (free start);

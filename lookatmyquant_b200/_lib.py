@@ -23,6 +23,7 @@ _P, _I64, _I32, _SZ, _D = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_size_t, _c.c_d
 # name -> (restype, argtypes): every symbol include/lamq_b200.h declares
 SIGNATURES = {
     "lamq_abi_version": (_I32, []),
+    "lamq_kernel_launches": (_c.c_uint64, []),
     "lamq_last_error": (_c.c_char_p, []),
     "lamq_viterbi_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
@@ -76,13 +77,13 @@ def load():
     return _lib
 
 
-LAUNCHES = {"count": 0}  # kernels launched through this module (the benchmark's gpu_launches)
+def kernel_launches() -> int:
+    """Kernels liblamq_b200 has launched in this process (lamq_kernel_launches)."""
+    return int(load().lamq_kernel_launches())
 
 
-def check(status: int, what: str, kernels: int = 1):
-    """Raises on a non-zero status; on success counts the entry point's kernel launches."""
-    if status == LAMQ_OK:
-        LAUNCHES["count"] += kernels
+def check(status: int, what: str):
+    """Raises on a non-zero status."""
     if status != LAMQ_OK:
         msg = load().lamq_last_error().decode(errors="replace")
         if status == LAMQ_ERR_INVALID:

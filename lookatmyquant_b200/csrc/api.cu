@@ -2,11 +2,16 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "lamq_common.cuh"
 
 namespace lamq {
 
 static thread_local char g_error[512] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char *fmt, ...) {
     va_list ap;
@@ -20,3 +25,5 @@ void set_error(const char *fmt, ...) {
 extern "C" int lamq_abi_version(void) { return 4; }
 
 extern "C" const char *lamq_last_error(void) { return lamq::g_error; }
+
+extern "C" uint64_t lamq_kernel_launches(void) { return lamq::g_launches.load(std::memory_order_relaxed); }

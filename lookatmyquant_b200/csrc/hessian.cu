@@ -726,6 +726,7 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
             set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
             return LAMQ_ERR_CUDA;
         }
+        count_launch();
     } else {
         e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
         if (e != cudaSuccess) {

@@ -11,6 +11,9 @@ namespace lamq {
 // Records the first CUDA error of the calling thread's last API call, for lamq_last_error().
 void set_error(const char *fmt, ...);
 
+// Counts one kernel launch of this library (lamq_kernel_launches()).
+void count_launch();
+
 #define LAMQ_CHECK_LAUNCH(what)                                                         \
     do {                                                                                \
         cudaError_t _e = cudaGetLastError();                                            \
@@ -18,6 +21,7 @@ void set_error(const char *fmt, ...);
             ::lamq::set_error("%s: %s", what, cudaGetErrorString(_e));                  \
             return LAMQ_ERR_CUDA;                                                       \
         }                                                                               \
+        ::lamq::count_launch();                                                         \
     } while (0)
 
 #define LAMQ_REQUIRE(cond, ...)                                                         \
