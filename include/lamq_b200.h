@@ -144,6 +144,19 @@ int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_t *B, int64
                         lamq_stream_t stream);
 
 /*
+ * lamq_xtx_accumulate with the products scaled: acc[j][i] += scale·Σ_t A[t][i]·B[t][j] (each chunk's fp32 partial is
+ * multiplied by `scale` as it is added). With the tokens of one weight value w gathered, scale = w − 1 adds their
+ * weighted share exactly from bf16 products (quantize.py:1389-1391).
+ */
+int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb, int64_t tokens, int d,
+                               int symmetric, float scale, float *acc, int64_t ldacc, int64_t chunk_tokens, int *status,
+                               lamq_stream_t stream);
+
+/* dst row r = src row idx[r] for r < n: bf16 rows of d (a multiple of 8) values, 16-byte aligned. */
+int lamq_gather_rows(const uint16_t *src, int64_t lds, const int32_t *idx, int64_t n, int d, uint16_t *dst,
+                     lamq_stream_t stream);
+
+/*
  * Token weights (quantize.py:1389-1391, 593-629): the weighted tokens' share Σ_t (w_t − 1)·x_t ⊗ y_t as two extra
  * rows per token for lamq_xtx_accumulate. For each r < nw, t = idx[r]: out_split row r = hi, row r + nw = lo of
  * (w[t] − 1)·scaled[t] (fp32; hi = bf16(y), lo = bf16(y − hi)); out_plain rows r and r + nw = plain[t].

@@ -29,6 +29,8 @@ SIGNATURES = {
     "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "lamq_viterbi_noalloc": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P]),
     "lamq_xtx_accumulate": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _I64, _I64, _P, _P]),
+    "lamq_xtx_accumulate_scaled": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _c.c_float, _P, _I64, _I64, _P, _P]),
+    "lamq_gather_rows": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P]),
     "lamq_weighted_split": (_I32, [_P, _I64, _P, _I64, _P, _P, _I64, _I32, _P, _P, _P]),
     "lamq_hessian_finalize": (_I32, [_P, _P, _I32, _I64, _D, _P, _P, _P]),
     "lamq_rht_rows": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _P, _P, _P, _D, _P]),

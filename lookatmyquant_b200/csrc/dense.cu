@@ -24,7 +24,9 @@ namespace lamq {
 namespace {
 
 constexpr int GM = 128, GN = 128, GK = 16, GSTAGES = 4;
-constexpr int kGemmThreads = 256;
+constexpr int kGemmWarpsM = 2, kGemmWarpsN = 4;  // 8 warps of 64 x 32
+constexpr int kGemmThreads = 32 * kGemmWarpsM * kGemmWarpsN;
+constexpr int WTM = GM / kGemmWarpsM, WTN = GN / kGemmWarpsN, FI = WTM / 16, FJ = WTN / 8;  // m16n8 tiles
 constexpr int SA = GK + 4;   // A tile row stride (doubles): fragment loads hit every bank pair once
 constexpr int SBN = GN + 4;  // B tile (k-major, NN) row stride
 constexpr int SBT = GK + 4;  // B tile (n-major, NT) row stride
@@ -45,6 +47,16 @@ struct GemmArgs {
     int b_lower;     // the stored B is lower triangular: NN skips k < n, NT skips k > n
     int vec;         // A and B rows are 16-byte aligned: copy two doubles per cp.async
 };
+
+// D (16 x 8) += A (16 x 16) · B (16 x 8) in fp64: per thread a0..a7 = A[g + 8·(i&1)][t + 4·(i>>1)],
+// b0..b3 = B[t + 4·i][g], c0..c3 = D[g + 8·(i>>1)][2t + (i&1)] (g = lane / 4, t = lane % 4).
+__device__ __forceinline__ void dmma16816(double (&c)[4], const double (&a)[8], const double (&b)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f64.f64.f64.f64 {%0, %1, %2, %3}, {%4, %5, %6, %7, %8, %9, %10, %11}, "
+        "{%12, %13, %14, %15}, {%0, %1, %2, %3};"
+        : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+        : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]), "d"(b[0]), "d"(b[1]),
+          "d"(b[2]), "d"(b[3]));
+}
 
 __device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b) {
     asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
@@ -114,20 +126,23 @@ constexpr int kATile = GM * SA;
 constexpr int kBTile = GK * SBN > GN * SBT ? GK * SBN : GN * SBT;
 constexpr size_t kGemmSmem = GSTAGES * (size_t)(kATile + kBTile) * sizeof(double);
 
-// C = α·A·B(ᵀ) + β·C on the fp64 tensor cores: 128 x 128 CTA tiles, 8 warps of 64 x 32 (8 x 4 fragments of
-// mma.sync m8n8k4), K in steps of 16 through a 4-stage cp.async ring.
+// C = α·A·B(ᵀ) + β·C on the fp64 tensor cores: 128 x 128 CTA tiles, 8 warps of 64 x 32 (4 x 4 fragments of
+// mma.sync m16n8k16 f64 — on B200 the large fp64 shape sustains ~37 TFLOP/s where m8n8k4 with changing operands
+// stops near 32), K in steps of 16 through a 4-stage cp.async ring.
 __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
     extern __shared__ __align__(16) double gsm[];
     const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
     if (g.lower_only && m0 + GM - 1 < n0) return;  // every row of the tile is above the diagonal
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;  // warp tile 64 x 32
-    const int fr = lane >> 2, fk = lane & 3;
-    double acc[8][4][2];
+    const int wm = (warp / kGemmWarpsN) * WTM, wn = (warp % kGemmWarpsN) * WTN;  // warp tile WTM x WTN
+    const int fg = lane >> 2, ft = lane & 3;
+    double acc[FI][FJ][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < FI; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+        for (int j = 0; j < FJ; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
     // the K range that can hold non-zero products for this tile
     int kb = 0, ke = g.K;
     if (g.a_lower) ke = min(ke, m0 + GM);
@@ -160,43 +175,39 @@ __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
         if (nxt < ksteps) load(nxt % GSTAGES, kb + nxt * GK);
         asm volatile("cp.async.commit_group;" ::: "memory");
         const double *A = As(ks % GSTAGES), *B = Bs(ks % GSTAGES);
-        double a[2][8], b[2][4];  // fragments of this K slice and the next, loaded one slice ahead
-        auto frag = [&](int kk, double (&fa)[8], double (&fb)[4]) {
+        double bf[FJ][4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) fa[i] = A[(wm + 8 * i + fr) * SA + kk + fk];
-            if (g.transB) {
+        for (int j = 0; j < FJ; ++j)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) fb[j] = B[(wn + 8 * j + fr) * SBT + kk + fk];
-            } else {
+            for (int e = 0; e < 4; ++e)
+                bf[j][e] = g.transB ? B[(wn + 8 * j + fg) * SBT + ft + 4 * e] : B[(ft + 4 * e) * SBN + wn + 8 * j + fg];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) fb[j] = B[(kk + fk) * SBN + wn + 8 * j + fr];
-            }
-        };
-        frag(0, a[0], b[0]);
+        for (int i = 0; i < FI; ++i) {
+            double af[8];
 #pragma unroll
-        for (int q = 0; q < GK / 4; ++q) {
-            if (q + 1 < GK / 4) frag(4 * (q + 1), a[(q + 1) & 1], b[(q + 1) & 1]);
+            for (int e = 0; e < 8; ++e) af[e] = A[(wm + 16 * i + fg + 8 * (e & 1)) * SA + ft + 4 * (e >> 1)];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) dmma(acc[i][j][0], acc[i][j][1], a[q & 1][i], b[q & 1][j]);
+            for (int j = 0; j < FJ; ++j) dmma16816(acc[i][j], af, bf[j]);
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    // C fragment: row fr, columns 2·fk, 2·fk + 1 of each 8 x 8 block
+    // D fragment: rows g and g + 8 of each 16 x 8 block, columns 2t, 2t + 1
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int r = m0 + wm + 8 * i + fr;
-        if (r >= g.M) continue;
+    for (int i = 0; i < FI; ++i) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int h = 0; h < 2; ++h) {
+            const int r = m0 + wm + 16 * i + fg + 8 * h;
+            if (r >= g.M) continue;
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int c = n0 + wn + 8 * j + 2 * fk + e;
-                if (c >= g.N) continue;
-                double *p = g.C + (int64_t)r * g.ldc + c;
-                const double v = g.alpha * acc[i][j][e];
-                *p = (g.beta == 0.0) ? v : fma(g.beta, *p, v);
+            for (int j = 0; j < FJ; ++j) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = n0 + wn + 8 * j + 2 * ft + e;
+                    if (c >= g.N) continue;
+                    double *p = g.C + (int64_t)r * g.ldc + c;
+                    const double v = g.alpha * acc[i][j][2 * h + e];
+                    *p = (g.beta == 0.0) ? v : fma(g.beta, *p, v);
+                }
             }
         }
     }

@@ -77,6 +77,7 @@ struct GemmParams {
     int kblocks_per_chunk;
     int symmetric;
     int pair;               // tiles of 256 x 256 computed by a pair of CTAs (cta_group::2), else 128 x 256 per CTA
+    float scale;            // each unit's tile is added into acc times this
     int64_t units;
     int *status;
     unsigned int *gate;     // units whose loads have all been issued (the wave gate), zeroed before the launch
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 128; ++c) {
                     const int j = U.tj * BN + 128 * half + c;
-                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, tile[c]);
+                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
                 }
             }
         }
@@ -516,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 128; ++c) {
                     const int j = U.tj * BN + 128 * half + c;
-                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, tile[c]);
+                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
                 }
             }
         }
@@ -547,6 +548,16 @@ __global__ void weighted_split_kernel(const __nv_bfloat16 *__restrict__ scaled, 
         const __nv_bfloat16 pv = plain[t * ldp + c];
         out_plain[r * d + c] = pv;
         out_plain[(r + nw) * d + c] = pv;
+    }
+}
+
+// dst row r = src row idx[r] (bf16 rows as 16-byte units; d a multiple of 8).
+__global__ void gather_rows_kernel(const uint4 *__restrict__ src, int64_t lds16, const int32_t *__restrict__ idx,
+                                   int64_t n, int units, uint4 *__restrict__ dst) {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * units; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / units;
+        const int u = (int)(e % units);
+        dst[r * units + u] = src[(int64_t)idx[r] * lds16 + u];
     }
 }
 
@@ -658,9 +669,20 @@ int num_sms() {
 
 using namespace lamq;
 
+extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb,
+                                          int64_t tokens, int d, int symmetric, float scale, float *acc, int64_t ldacc,
+                                          int64_t chunk_tokens, int *status, lamq_stream_t stream);
+
 extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb, int64_t tokens,
                                    int d, int symmetric, float *acc, int64_t ldacc, int64_t chunk_tokens, int *status,
                                    lamq_stream_t stream) {
+    return lamq_xtx_accumulate_scaled(A, lda, B, ldb, tokens, d, symmetric, 1.0f, acc, ldacc, chunk_tokens, status,
+                                      stream);
+}
+
+extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const uint16_t *B, int64_t ldb,
+                                          int64_t tokens, int d, int symmetric, float scale, float *acc, int64_t ldacc,
+                                          int64_t chunk_tokens, int *status, lamq_stream_t stream) {
     LAMQ_REQUIRE(tokens >= 0 && d > 0, "lamq_xtx_accumulate: bad shape");
     if (tokens == 0) return LAMQ_OK;
     LAMQ_REQUIRE(A && B && acc && status, "lamq_xtx_accumulate: null pointer");
@@ -678,6 +700,7 @@ extern "C" int lamq_xtx_accumulate(const uint16_t *A, int64_t lda, const uint16_
     p.acc = acc;
     p.ldc = ldacc;
     p.d = d;
+    p.scale = scale;
     // contractions of d >= 512 run on CTA pairs (256 x 256 tiles), smaller ones on single CTAs (128 x 256)
     p.pair = d >= 512 ? 1 : 0;
     const int tm = p.pair ? 256 : BM;
@@ -751,6 +774,21 @@ extern "C" int lamq_weighted_split(const uint16_t *scaled, int64_t lds, const ui
         reinterpret_cast<const __nv_bfloat16 *>(scaled), lds, reinterpret_cast<const __nv_bfloat16 *>(plain), ldp, w,
         idx, nw, d, reinterpret_cast<__nv_bfloat16 *>(out_split), reinterpret_cast<__nv_bfloat16 *>(out_plain));
     LAMQ_CHECK_LAUNCH("lamq_weighted_split");
+    return LAMQ_OK;
+}
+
+extern "C" int lamq_gather_rows(const uint16_t *src, int64_t lds, const int32_t *idx, int64_t n, int d, uint16_t *dst,
+                                lamq_stream_t stream) {
+    LAMQ_REQUIRE(n >= 0 && d > 0 && d % 8 == 0 && lds % 8 == 0 && lds >= d, "lamq_gather_rows: bad shape");
+    if (n == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(src && idx && dst, "lamq_gather_rows: null pointer");
+    LAMQ_REQUIRE(((uintptr_t)src % 16) == 0 && ((uintptr_t)dst % 16) == 0, "lamq_gather_rows: rows not 16-byte aligned");
+    const int units = d / 8;
+    const int64_t work = n * units;
+    const int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 16);
+    gather_rows_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint4 *>(src), lds / 8, idx, n,
+                                                                 units, reinterpret_cast<uint4 *>(dst));
+    LAMQ_CHECK_LAUNCH("lamq_gather_rows");
     return LAMQ_OK;
 }
 

@@ -20,6 +20,7 @@ from . import _lib
 from ._lib import check, ptr, stream_ptr
 
 CHUNK_TOKENS = 32768  # tokens accumulated on chip before each flush into the fp32 accumulator
+MAX_WEIGHT_GROUPS = 4  # distinct token weights handled by gathering (more: the hi/lo split)
 
 
 def _bf16(x: torch.Tensor) -> torch.Tensor:
@@ -44,19 +45,32 @@ class Statistics:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.n_tok = 0
 
-    def _xtx(self, A, B, symmetric, acc, tokens):
+    def _xtx(self, A, B, symmetric, acc, tokens, scale: float = 1.0):
         lib = _lib.load()
         with torch.cuda.device(self.device):
-            check(lib.lamq_xtx_accumulate(ptr(A), A.stride(0), ptr(B), B.stride(0), tokens, self.d,
-                                          1 if symmetric else 0, ptr(acc), acc.stride(0), self.chunk_tokens,
-                                          ptr(self.status), stream_ptr(self.device)), "lamq_xtx_accumulate")
+            check(lib.lamq_xtx_accumulate_scaled(ptr(A), A.stride(0), ptr(B), B.stride(0), tokens, self.d,
+                                                 1 if symmetric else 0, float(scale), ptr(acc), acc.stride(0),
+                                                 self.chunk_tokens, ptr(self.status), stream_ptr(self.device)),
+                  "lamq_xtx_accumulate")
+
+    def _gather(self, x, idx):
+        out = torch.empty(idx.numel(), self.d, dtype=torch.bfloat16, device=self.device)
+        with torch.cuda.device(self.device):
+            check(_lib.load().lamq_gather_rows(ptr(x), x.stride(0), ptr(idx), idx.numel(), self.d, ptr(out),
+                                               stream_ptr(self.device)), "lamq_gather_rows")
+        return out
 
     def add(self, x: torch.Tensor, w: torch.Tensor | None = None, x_ref: torch.Tensor | None = None,
-            weighted: torch.Tensor | None = None):
+            weighted=None):
         """One calibration chunk: x (tokens × d bf16, the stream the matrix will see), its token weights w (fp32, or
-        None for 1) and, for D, x_ref (the reference stream at the same tokens). `weighted` (int32, on the device)
-        may give the chunk's tokens whose weight is not 1, found by the caller; otherwise they are found here, which
-        reads their count back from the device."""
+        None for 1) and, for D, x_ref (the reference stream at the same tokens).
+
+        The main pass takes every token with weight 1 (exact bf16 products); the weighted tokens then add
+        Σ (w − 1)·x xᵀ (and Σ (w − 1)·x_ref xᵀ). When they carry at most MAX_WEIGHT_GROUPS distinct weights, the
+        tokens of each weight are gathered and added once with scale w − 1 (products still exact); otherwise each
+        weighted token enters twice, (w − 1)·x split into a bf16 hi + lo pair. `weighted` may give the groups found
+        by the caller as [(device int32 token indices, w), ...]; otherwise they are found here, which reads the
+        weights' distinct values back from the device."""
         x = _bf16(x)
         tokens = x.shape[0]
         if x.shape[1] != self.d:
@@ -71,27 +85,50 @@ class Statistics:
             w = w.reshape(-1).to(self.device, torch.float32).contiguous()
             if w.numel() != tokens:
                 raise ValueError("one weight per token")
-            idx = torch.nonzero(w != 1.0).flatten().to(torch.int32) if weighted is None else weighted
-            nw = int(idx.numel())
-            if nw:
-                lib = _lib.load()
-                split = torch.empty(2 * nw, self.d, dtype=torch.bfloat16, device=self.device)
-                plain = torch.empty_like(split)
-                with torch.cuda.device(self.device):
-                    check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(x), x.stride(0), ptr(w), ptr(idx), nw,
-                                                  self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
-                          "lamq_weighted_split")
-                # Σ (w−1)·x xᵀ: A = x (plain), B = (w−1)·x (hi and lo rows)
-                self._xtx(plain, split, True, self.accH, 2 * nw)
-                if xr is not None:
-                    with torch.cuda.device(self.device):
-                        check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(xr), xr.stride(0), ptr(w), ptr(idx),
-                                                      nw, self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
-                              "lamq_weighted_split")
-                    # D[j][i] += Σ (w−1)·x[i]·x_ref[j]: A = (w−1)·x (hi and lo), B = x_ref
-                    self._xtx(split, plain, False, self.accD, 2 * nw)
+            groups = weighted
+            if groups is None:
+                idx = torch.nonzero(w != 1.0).flatten().to(torch.int32)
+                vals = torch.unique(w[idx]).tolist() if idx.numel() else []
+                if len(vals) <= MAX_WEIGHT_GROUPS:
+                    groups = [(idx[w[idx] == v].contiguous(), v) for v in vals] if len(vals) > 1 else \
+                        [(idx, vals[0])] if vals else []
+                else:
+                    groups = idx
+            if isinstance(groups, torch.Tensor):
+                self._add_split(x, xr, w, groups)
+            else:
+                for gidx, v in groups:
+                    n = int(gidx.numel())
+                    if n == 0:
+                        continue
+                    xg = self._gather(x, gidx)
+                    self._xtx(xg, xg, True, self.accH, n, v - 1.0)
+                    if xr is not None:
+                        self._xtx(xg, self._gather(xr, gidx), False, self.accD, n, v - 1.0)
         self.n_tok += tokens
         return self
+
+    def _add_split(self, x, xr, w, idx):
+        """Σ (w − 1)·x xᵀ for weighted tokens of many distinct weights: (w − 1)·x as a bf16 hi + lo pair."""
+        nw = int(idx.numel())
+        if nw == 0:
+            return
+        lib = _lib.load()
+        split = torch.empty(2 * nw, self.d, dtype=torch.bfloat16, device=self.device)
+        plain = torch.empty_like(split)
+        with torch.cuda.device(self.device):
+            check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(x), x.stride(0), ptr(w), ptr(idx), nw,
+                                          self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
+                  "lamq_weighted_split")
+        # Σ (w−1)·x xᵀ: A = x (plain), B = (w−1)·x (hi and lo rows)
+        self._xtx(plain, split, True, self.accH, 2 * nw)
+        if xr is not None:
+            with torch.cuda.device(self.device):
+                check(lib.lamq_weighted_split(ptr(x), x.stride(0), ptr(xr), xr.stride(0), ptr(w), ptr(idx),
+                                              nw, self.d, ptr(split), ptr(plain), stream_ptr(self.device)),
+                      "lamq_weighted_split")
+            # D[j][i] += Σ (w−1)·x[i]·x_ref[j]: A = (w−1)·x (hi and lo), B = x_ref
+            self._xtx(split, plain, False, self.accD, 2 * nw)
 
     def finalize(self, n_tok: int | None = None):
         """(H, D) in fp64: H = acc/n_tok (mirrored from the computed triangle), D = accD/n_tok − H (or None)."""

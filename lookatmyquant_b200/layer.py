@@ -158,6 +158,22 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
 _COPY = {}
 
 
+def _weight_groups(w_host: torch.Tensor, dev):
+    """The weighted tokens of a chunk, found on the host: [(device int32 indices, w), ...] per distinct weight when
+    there are few (Statistics gathers each group and adds it once, scaled by w − 1), else the indices of all of them
+    (the hi/lo split). The copies to the device are queued on the current stream."""
+    from .hessian import MAX_WEIGHT_GROUPS
+    idx = torch.nonzero(w_host != 1.0).flatten().to(torch.int32)
+    vals = torch.unique(w_host[idx.long()]).tolist() if idx.numel() else []
+    if len(vals) > MAX_WEIGHT_GROUPS:
+        return idx.pin_memory().to(dev, non_blocking=True)
+    out = []
+    for v in vals:
+        sel = idx if len(vals) == 1 else idx[w_host[idx.long()] == v]
+        out.append((sel.contiguous().pin_memory().to(dev, non_blocking=True), float(v)))
+    return out
+
+
 def _copy_stream(dev) -> torch.cuda.Stream:
     if dev not in _COPY:
         _COPY[dev] = torch.cuda.Stream(device=dev)
@@ -187,15 +203,17 @@ def build_layer_from_host(stages, weights, acts, w, bits, layer: int = 0, group=
             chunks = []
             for c0 in range(0, x_h.shape[0], chunk_tokens):
                 c1 = min(c0 + chunk_tokens, x_h.shape[0])
-                wc = w[c0:c1]
-                idx = torch.nonzero(wc != 1.0).flatten().to(torch.int32).pin_memory().to(dev, non_blocking=True)
+                idx = _weight_groups(w[c0:c1], dev)
                 x_d[c0:c1].copy_(x_h[c0:c1], non_blocking=True)
                 xr_d[c0:c1].copy_(xr_h[c0:c1], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(copy)
                 chunks.append((c0, c1, idx, ev))
             staged.append((x_d, xr_d, wts, chunks))
-    for t in [w_d] + [t for x_d, xr_d, wts, chunks in staged for t in [x_d, xr_d, *wts.values(), *(c[2] for c in chunks)]]:
+    def group_tensors(g):
+        return [g] if isinstance(g, torch.Tensor) else [t for t, _ in g]
+    for t in [w_d] + [t for x_d, xr_d, wts, chunks in staged
+                      for t in [x_d, xr_d, *wts.values(), *(u for c in chunks for u in group_tensors(c[2]))]]:
         t.record_stream(main)
     out = {}
     for i, s in enumerate(stages):

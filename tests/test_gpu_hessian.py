@@ -36,12 +36,19 @@ def test_unweighted_h(tokens, d):
     assert np.array_equal(Hc, Hc.T)
 
 
+@pytest.mark.parametrize("kind", ["two values", "three values", "many values"])
 @pytest.mark.parametrize("tokens,d", [(3000, 256), (20000, 512)])
-def test_weighted_h_and_qep_d(tokens, d):
+def test_weighted_h_and_qep_d(tokens, d, kind):
+    """Weighted tokens gathered per weight value (few distinct weights) or split into bf16 hi + lo (many)."""
     from lookatmyquant_b200.hessian import hessian
     X = acts(tokens, d, 1)
     Xr = (X.float() + 0.05 * acts(tokens, d, 2, torch.float32)).to(torch.bfloat16)
     w = weights(tokens, 3)
+    g = torch.Generator().manual_seed(4)
+    if kind == "three values":
+        w = torch.where(torch.rand(tokens, generator=g) < 0.3, 0.25, w)
+    elif kind == "many values":
+        w = torch.where(w != 1.0, 1.0 + 9.0 * torch.rand(tokens, generator=g), w)
     H, D = hessian(X.cuda(), w.cuda(), Xr.cuda(), chunk_tokens=4096)
     refH, refD = O.hessian_accumulate([X.float().numpy()], [w.numpy()], [Xr.float().numpy()])
     assert rel(H.cpu().numpy(), refH) < 1e-5
