@@ -60,8 +60,10 @@ _SIDE = {}
 
 
 def _side_stream(dev) -> torch.cuda.Stream:
+    """The stage's QEP stream, at high priority: its factorization and the targets it feeds run first, the
+    environment's factorization (whose leaf steps leave most SMs idle) fills in around them."""
     if dev not in _SIDE:
-        _SIDE[dev] = torch.cuda.Stream(device=dev)
+        _SIDE[dev] = torch.cuda.Stream(device=dev, priority=-1)
     return _SIDE[dev]
 
 
@@ -113,26 +115,28 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     names = [nm for nm, _ in spec.matrices]
     total = sum(r for _, r in spec.matrices)
     r0, r1 = row_shard(total, rank, world)
-    # the QEP map (a factorization of H + λμI) and the environment (a factorization of R·H·Rᵀ) are independent:
-    # the first runs on a side stream while the second runs on the main one
+    # the QEP map (a factorization of H + λμI) with the rotated targets it feeds, and the environment (a
+    # factorization of R·H·Rᵀ), are independent: the first runs on a side stream while the second runs on the main one
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev)
+    rot = Rotation(spec.d, in_seed, dev)
     side.wait_stream(main)
+    Xs, ks, spans, off = [], [], {}, 0
     with torch.cuda.stream(side):
         qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0)
-    rot = Rotation(spec.d, in_seed, dev)
+        for nm, rows in spec.matrices:
+            a, b = max(r0, off), min(r1, off + rows)
+            if a < b:
+                target = qep.apply(weights[nm][a - off:b - off].to(torch.float64))
+                Xs.append(rot.rows(target))
+                ks.append(bits[nm][a - off:b - off])
+                spans[nm] = (a - off, b - off)
+            off += rows
     env = Environment(rot.conj(H))
     main.wait_stream(side)
     qep.record_stream(main)
-    Xs, ks, spans, off = [], [], {}, 0
-    for nm, rows in spec.matrices:
-        a, b = max(r0, off), min(r1, off + rows)
-        if a < b:
-            target = qep.apply(weights[nm][a - off:b - off].to(torch.float64))
-            Xs.append(rot.rows(target))
-            ks.append(bits[nm][a - off:b - off])
-            spans[nm] = (a - off, b - off)
-        off += rows
+    for t in Xs:
+        t.record_stream(main)
     res = StageResult(row_range=spans)
     if not Xs:
         return res
