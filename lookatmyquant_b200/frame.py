@@ -15,13 +15,25 @@ class Environment:
     not positive definite; it synchronises, so callers run it once the factor is needed on the host.
     """
 
-    def __init__(self, H: torch.Tensor, damp: float = 0.01, G: torch.Tensor | None = None):
+    def __init__(self, H: torch.Tensor, damp: float = 0.01, G: torch.Tensor | None = None,
+                 status: torch.Tensor | None = None):
         from .linalg import env_factor
         if not H.is_cuda:
             raise RuntimeError("Environment expects H on a CUDA device")
         self.G = None if G is None else G.double()
         self._H0, self.damp = H.double(), damp
-        self.U, self.dead, self.check = env_factor(self._H0, damp)
+        self.U, self.dead, self.check = env_factor(self._H0, damp, status)
+
+    @classmethod
+    def from_factor(cls, H: torch.Tensor, U: torch.Tensor, dead: torch.Tensor, status: torch.Tensor,
+                    damp: float = 0.01) -> "Environment":
+        """An environment whose factor was computed elsewhere (another rank): U, the dead flags and the status word
+        of that factorization."""
+        from .linalg import status_check
+        env = cls.__new__(cls)
+        env.G, env._H0, env.damp = None, H.double(), damp
+        env.U, env.dead, env.check = U, dead.bool(), status_check(status)
+        return env
 
     @property
     def H(self) -> torch.Tensor:

@@ -24,7 +24,7 @@ from . import codes
 from .codes import LAZY, stacked_tables
 from .frame import Environment
 from .hessian import Statistics
-from .linalg import CrossTarget
+from .linalg import CrossTarget, cholesky_inverse_lower, ridge, status_check
 from .rotation import Rotation
 
 ALPHA, LAM = 0.5, 0.1  # QEP strength of the lm2 build (--cross-alpha 0.5) and the ridge (quantize.py:93)
@@ -120,10 +120,17 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev)
     rot = Rotation(spec.d, in_seed, dev)
-    side.wait_stream(main)
+    if world >= 2:
+        # two ranks factor at once, one matrix each, and broadcast the factors (NVLink): the QEP's inverse Cholesky
+        # factor from rank 1, the environment's U from rank 0
+        env, Linv, qst = _factors_on_two_ranks(rot, H, rank, group)
+        side.wait_stream(main)
+    else:
+        side.wait_stream(main)
     Xs, ks, spans, off = [], [], {}, 0
     with torch.cuda.stream(side):
-        qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0)
+        qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0) if world < 2 else \
+            CrossTarget(None, D, ALPHA, LAM, rows=r1 - r0, Linv=Linv, check=status_check(qst))
         for nm, rows in spec.matrices:
             a, b = max(r0, off), min(r1, off + rows)
             if a < b:
@@ -132,7 +139,8 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
                 ks.append(bits[nm][a - off:b - off])
                 spans[nm] = (a - off, b - off)
             off += rows
-    env = Environment(rot.conj(H))
+    if world < 2:
+        env = Environment(rot.conj(H))
     main.wait_stream(side)
     qep.record_stream(main)
     for t in Xs:
@@ -157,6 +165,33 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     env.check()
     qep.check()
     return res
+
+
+def _factors_on_two_ranks(rot, H, rank: int, group):
+    """The stage's two factorizations on two ranks at once — Environment(R·H·Rᵀ) on rank 0, the QEP's inverse
+    Cholesky factor of H + λ·mean(diag H)·I on rank 1 — each queued before any collective, then broadcast to the
+    group (NVLink) with their status words. Returns (env, Linv, qep_status) on every rank."""
+    n, dev = H.shape[0], H.device
+    qst = torch.zeros(1, dtype=torch.int32, device=dev)
+    est = torch.zeros(1, dtype=torch.int32, device=dev)
+    Hr = rot.conj(H)
+    if rank == 1:
+        Linv = cholesky_inverse_lower(ridge(H, LAM), deferred=True, status=qst)[0]
+    else:
+        Linv = torch.empty(n, n, dtype=torch.float64, device=dev)
+    if rank == 0:
+        env0 = Environment(Hr, status=est)
+        U, dead = env0.U, env0.dead.to(torch.uint8)
+    else:
+        U = torch.empty(n, n, dtype=torch.float64, device=dev)
+        dead = torch.empty(n, dtype=torch.uint8, device=dev)
+    r0, r1 = torch.distributed.get_global_rank(group, 0), torch.distributed.get_global_rank(group, 1)
+    torch.distributed.broadcast(Linv, src=r1, group=group)
+    torch.distributed.broadcast(qst, src=r1, group=group)
+    torch.distributed.broadcast(U, src=r0, group=group)
+    torch.distributed.broadcast(dead, src=r0, group=group)
+    torch.distributed.broadcast(est, src=r0, group=group)
+    return Environment.from_factor(Hr, U, dead, est), Linv, qst
 
 
 _COPY = {}

@@ -46,7 +46,7 @@ def gemm(A, B, C=None, transB=False, alpha=1.0, beta=0.0):
     return C
 
 
-def env_factor(H: torch.Tensor, damp: float = 0.01):
+def env_factor(H: torch.Tensor, damp: float = 0.01, status: torch.Tensor | None = None):
     """(U, dead, check): the environment factor of frame.py:515-522 on the GPU. `check()` raises the reference's
     error if H was not positive definite (it synchronises; call it when the result is needed)."""
     H = _f64(H)
@@ -56,21 +56,26 @@ def env_factor(H: torch.Tensor, damp: float = 0.01):
     U = torch.empty(n, n, dtype=torch.float64, device=dev)
     dead = torch.empty(n, dtype=torch.uint8, device=dev)
     ws = torch.empty(lib.lamq_factor_workspace_size(n), dtype=torch.uint8, device=dev)
-    st = _status(dev)
+    st = _status(dev) if status is None else status
     with torch.cuda.device(dev):
         check(lib.lamq_env_factor(ptr(H), H.stride(0), n, float(damp), ptr(U), n, ptr(dead), ptr(ws), ws.numel(),
                                   ptr(st), stream_ptr(dev)), "lamq_env_factor")
     return U, dead.bool(), lambda: _raise_if_not_pd(st)
 
 
-def cholesky_inverse_lower(A: torch.Tensor, deferred: bool = False):
+def status_check(st: torch.Tensor):
+    """The deferred check of a factorization's status word (as env_factor and cholesky_inverse_lower return)."""
+    return lambda: _raise_if_not_pd(st)
+
+
+def cholesky_inverse_lower(A: torch.Tensor, deferred: bool = False, status: torch.Tensor | None = None):
     """L⁻¹ for A = L·Lᵀ (lower triangular, fp64), on a copy of A. With `deferred`, returns (L⁻¹, check) and leaves the
     positive-definiteness check (a synchronisation) to the caller."""
     A = _f64(A).clone()
     n = A.shape[0]
     lib = _lib.load()
     ws = torch.empty(lib.lamq_factor_workspace_size(n), dtype=torch.uint8, device=A.device)
-    st = _status(A.device)
+    st = _status(A.device) if status is None else status
     with torch.cuda.device(A.device):
         check(lib.lamq_cholesky_inverse_lower(ptr(A), A.stride(0), n, ptr(ws), ws.numel(), ptr(st),
                                               stream_ptr(A.device)), "lamq_cholesky_inverse_lower")
@@ -96,10 +101,13 @@ class CrossTarget:
     Dᵀ))ᵀ = I + α·D·(H + λμI)⁻¹ (lamq_cross_apply). With `rows` (the rows the stage will map) above n, M is formed
     once; otherwise each W is mapped as W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹."""
 
-    def __init__(self, H, D, alpha: float, lam: float, rows: int | None = None):
-        n = H.shape[0]
+    def __init__(self, H, D, alpha: float, lam: float, rows: int | None = None, Linv=None, check=None):
+        n = H.shape[0] if H is not None else D.shape[0]
         self.alpha = alpha
-        self.Linv, self.check = cholesky_inverse_lower(ridge(H, lam), deferred=True)
+        if Linv is None:
+            self.Linv, self.check = cholesky_inverse_lower(ridge(H, lam), deferred=True)
+        else:  # the factor computed elsewhere (another rank)
+            self.Linv, self.check = _f64(Linv), (check or (lambda: None))
         self.D = _f64(D)
         self.M = None
         if rows is None or rows > n:
