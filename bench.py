@@ -459,7 +459,7 @@ def main():
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()
-            wl.step()
+            wl.step(timed=True) if hasattr(wl, "stage_ms") else wl.step()
             ends[i].record()
         barrier()
         ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
@@ -492,7 +492,9 @@ def main():
         "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
     }
     if getattr(wl, "stage_ms", None):
-        pass
+        # per-stage device time of the timed steps (this rank's; the step's all-gather of states is outside them)
+        line["stage_ms"] = {k: round(statistics.mean(a.elapsed_time(b) for a, b in v), 2)
+                            for k, v in wl.stage_ms.items()}
     if rank == 0 and not args.no_cpu_baseline:
         v, sample = wl.cpu_sample(os.cpu_count() or 1)
         line["cpu_baseline"] = {"value": v, "unit": "s", "cores": os.cpu_count() or 1, "kind": "port",

@@ -9,11 +9,13 @@
 //      (2n³/3 multiply-adds) instead of three factorizations; U is the same unique factor.
 //   target = W·M = W + α·((W·D)·Lc⁻ᵀ)·Lc⁻¹ with H + λ·mean(diag H)·I = Lc·Lcᵀ (or M formed once when the stage has
 //      more rows than inputs).
-// GEMM: 128 × 64 CTA tiles, 8 warps of 32 × 32, K in steps of 16 staged through shared memory by cp.async (double
-// buffered, rows padded so every fragment load is bank-conflict free); a triangular operand clips each tile's K range.
+// GEMM: mma.sync m16n8k16 f64 on three CTA tile shapes — 128 x 128 (8 warps of 64 x 32) for large products,
+// 64 x 64 and 32 x 32 (4 warps) for the small ones at the bottom of the recursion, so they still spread over the
+// SMs — K in steps of 16 through a 4-stage cp.async ring (rows padded so fragment loads are bank-conflict free); a
+// triangular operand clips each tile's K range.
 // Cholesky and inverse together, recursively: (L11, X11) = rec(A11), L21 = A21·X11ᵀ, A22 −= L21·L21ᵀ,
 // (L22, X22) = rec(A22), X21 = −X22·(L21·X11) — 0.58n³ multiply-adds in large GEMMs; 128 x 128 leaves are factored
-// and inverted in one CTA's shared memory.
+// and inverted by one CTA, the block held in registers (right-looking, one barrier per column).
 #include <algorithm>
 #include <vector>
 
@@ -23,14 +25,26 @@ namespace lamq {
 
 namespace {
 
-constexpr int GM = 128, GN = 128, GK = 16, GSTAGES = 4;
-constexpr int kGemmWarpsM = 2, kGemmWarpsN = 4;  // 8 warps of 64 x 32
-constexpr int kGemmThreads = 32 * kGemmWarpsM * kGemmWarpsN;
-constexpr int WTM = GM / kGemmWarpsM, WTN = GN / kGemmWarpsN, FI = WTM / 16, FJ = WTN / 8;  // m16n8 tiles
+constexpr int GK = 16, GSTAGES = 4;
 constexpr int SA = GK + 4;   // A tile row stride (doubles): fragment loads hit every bank pair once
-constexpr int SBN = GN + 4;  // B tile (k-major, NN) row stride
 constexpr int SBT = GK + 4;  // B tile (n-major, NT) row stride
 constexpr int NB = 128;      // Cholesky panel / diagonal block
+
+// One CTA tile shape of the GEMM: BM x BN, warps in a WM_ x WN_ grid, each warp FI x FJ m16n8 fragments.
+template <int BM_, int BN_, int WM_, int WN_>
+struct Tiling {
+    static constexpr int BM = BM_, BN = BN_, kThreads = 32 * WM_ * WN_, kWarpsN = WN_;
+    static constexpr int WTM = BM / WM_, WTN = BN / WN_, FI = WTM / 16, FJ = WTN / 8;
+    static constexpr int SBN = BN + 4;  // B tile (k-major, NN) row stride
+    static constexpr int kATile = BM * SA;
+    static constexpr int kBTile = GK * SBN > BN * SBT ? GK * SBN : BN * SBT;
+    static constexpr size_t kSmem = GSTAGES * (size_t)(kATile + kBTile) * sizeof(double);
+    static_assert(FI >= 1 && FJ >= 1 && WTM % 16 == 0 && WTN % 8 == 0, "warp tile");
+    static_assert(BM * GK <= 8 * kThreads && BN * GK <= 8 * kThreads, "eight copy slots per thread");
+};
+using TileL = Tiling<128, 128, 2, 4>;  // 8 warps of 64 x 32
+using TileM = Tiling<64, 64, 2, 2>;    // 4 warps of 32 x 32
+using TileS = Tiling<32, 32, 2, 2>;    // 4 warps of 16 x 16
 
 struct GemmArgs {
     int M, N, K;
@@ -87,13 +101,14 @@ struct TileCopy {
 };
 
 // `k_rows`: the tile's rows run along K (B without transposition), else its columns do.
+template <int kThreads>
 __device__ __forceinline__ void tile_copy_init(TileCopy &t, int ld, int64_t lds, int r0, int c0, int rows, int cols,
                                                bool vec) {
     const int per = vec ? cols / 2 : cols;
     t.n = 0;
 #pragma unroll
     for (int q = 0; q < TileCopy::kSlots; ++q) {
-        const int e = threadIdx.x + q * kGemmThreads;
+        const int e = threadIdx.x + q * kThreads;
         const int r = e / per, c = vec ? 2 * (e % per) : e % per;
         t.soff[q] = r * ld + c;
         t.goff[q] = (int64_t)(r0 + r) * lds + c0 + c;
@@ -122,19 +137,18 @@ __device__ __forceinline__ void tile_copy_issue(const TileCopy &t, double *dst, 
     }
 }
 
-constexpr int kATile = GM * SA;
-constexpr int kBTile = GK * SBN > GN * SBT ? GK * SBN : GN * SBT;
-constexpr size_t kGemmSmem = GSTAGES * (size_t)(kATile + kBTile) * sizeof(double);
-
-// C = α·A·B(ᵀ) + β·C on the fp64 tensor cores: 128 x 128 CTA tiles, 8 warps of 64 x 32 (4 x 4 fragments of
-// mma.sync m16n8k16 f64 — on B200 the large fp64 shape sustains ~37 TFLOP/s where m8n8k4 with changing operands
+// C = α·A·B(ᵀ) + β·C on the fp64 tensor cores: one T::BM x T::BN tile per CTA, each warp FI x FJ fragments of
+// mma.sync m16n8k16 f64 (on B200 the large fp64 shape sustains ~37 TFLOP/s where m8n8k4 with changing operands
 // stops near 32), K in steps of 16 through a 4-stage cp.async ring.
-__global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
+template <class T>
+__global__ void __launch_bounds__(T::kThreads) dgemm_kernel(GemmArgs g) {
+    constexpr int GM = T::BM, GN = T::BN, FI = T::FI, FJ = T::FJ, WTM = T::WTM, WTN = T::WTN, SBN = T::SBN;
+    constexpr int kATile = T::kATile, kBTile = T::kBTile;
     extern __shared__ __align__(16) double gsm[];
     const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
     if (g.lower_only && m0 + GM - 1 < n0) return;  // every row of the tile is above the diagonal
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int wm = (warp / kGemmWarpsN) * WTM, wn = (warp % kGemmWarpsN) * WTN;  // warp tile WTM x WTN
+    const int wm = (warp / T::kWarpsN) * WTM, wn = (warp % T::kWarpsN) * WTN;  // warp tile WTM x WTN
     const int fg = lane >> 2, ft = lane & 3;
     double acc[FI][FJ][4];
 #pragma unroll
@@ -155,9 +169,9 @@ __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
     auto Bs = [&](int s) { return gsm + (size_t)s * (kATile + kBTile) + kATile; };
     const bool vec = g.vec != 0;
     TileCopy ca, cb;
-    tile_copy_init(ca, SA, g.lda, m0, 0, GM, GK, vec);  // A: GM x GK at (m0, k)
-    if (!g.transB) tile_copy_init(cb, SBN, g.ldb, 0, n0, GK, GN, vec);  // B: GK x GN at (k, n0)
-    else tile_copy_init(cb, SBT, g.ldb, n0, 0, GN, GK, vec);            // B: GN x GK at (n0, k)
+    tile_copy_init<T::kThreads>(ca, SA, g.lda, m0, 0, GM, GK, vec);  // A: GM x GK at (m0, k)
+    if (!g.transB) tile_copy_init<T::kThreads>(cb, SBN, g.ldb, 0, n0, GK, GN, vec);  // B: GK x GN at (k, n0)
+    else tile_copy_init<T::kThreads>(cb, SBT, g.ldb, n0, 0, GN, GK, vec);            // B: GN x GK at (n0, k)
     auto load = [&](int s, int k0) {
         tile_copy_issue(ca, As(s), g.A, g.lda, k0, false, g.M, g.K, vec);
         if (!g.transB) tile_copy_issue(cb, Bs(s), g.B, g.ldb, k0, true, g.K, g.N, vec);
@@ -215,67 +229,142 @@ __global__ void __launch_bounds__(kGemmThreads) dgemm_kernel(GemmArgs g) {
 
 // Factors the nb x nb diagonal block at A[k0][k0] in place (lower Cholesky; the block's strict upper part set to zero)
 // and writes its inverse to X[k0][k0] (lower, strict upper zero). A non-positive pivot sets *status = LAMQ_ERR_NOT_PD.
-// 512 threads: thread t owns column t & 127 and every fourth row from t >> 7.
-__global__ void __launch_bounds__(512) diag_block_kernel(double *A, int64_t lda, int k0, int nb, double *X,
-                                                         int64_t ldx, int *status) {
-    extern __shared__ __align__(16) double Bk[];  // nb x nb, row stride nb + 1
-    const int ld = nb + 1;
-    const int t = threadIdx.x, tc = t & 127, tg = t >> 7;
-    for (int r = tg; r < nb; r += 4)
-        if (tc < nb) Bk[r * ld + tc] = (tc <= r) ? A[(int64_t)(k0 + r) * lda + k0 + tc] : 0.0;
+// 512 threads; thread (ty, tx) = (t / 32, t % 32) holds the 8 x 4 elements (ty + 16a, tx + 32b) of the block in
+// registers (cyclic, so the shrinking trailing matrix stays spread over every warp). Both phases are right-looking
+// with one barrier per column:
+//   Cholesky, column j: l = B[:, j] / √B[j][j]; B[i][c] −= l_i·l_c for j < c <= i. The owners of column j + 1 publish
+//     it (and its pivot's square root and reciprocal) to shared memory as soon as their update is done.
+//   Inverse, row j: X[j][:] = R[j][:] / L[j][j], then R[i][:] −= L[i][j]·X[j][:] for i > j, R starting at I; the warp
+//     holding row j + 1 publishes it the same way.
+// L is kept transposed in shared memory (Lt[j][i] = L[i][j]) for the inverse and the write-back.
+constexpr int kLeafThreads = 512;
+constexpr int kLeafLd = NB + 1;
+constexpr size_t kLeafSmem = (size_t)(NB * kLeafLd + 3 * NB + 4) * sizeof(double);
+
+__global__ void __launch_bounds__(kLeafThreads) diag_block_kernel(double *A, int64_t lda, int k0, int nb, double *X,
+                                                                  int64_t ldx, int *status) {
+    extern __shared__ __align__(16) double lsm[];
+    double *Lt = lsm;                       // NB x kLeafLd: Lt[j][i] = L[i][j] for i >= j
+    double *col = Lt + NB * kLeafLd;        // 2 x NB: the column (Cholesky) or row (inverse) of the current step
+    double *invd = col + 2 * NB;            // NB: 1 / L[j][j]
+    double *piv = invd + NB;                // 2 x 2: √B[j][j] and its reciprocal, double-buffered
     __shared__ int bad;
+    const int t = threadIdx.x, ty = t >> 5, tx = t & 31;
+    double B[8][4];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int i = ty + 16 * a, c = tx + 32 * b;
+            B[a][b] = (i < nb && c <= i) ? A[(int64_t)(k0 + i) * lda + k0 + c] : 0.0;
+        }
     if (t == 0) bad = 0;
+    __syncthreads();  // bad is initialized before any pivot owner may set it
+    // the owners of column jn publish it and its pivot into buffer p
+    auto publish_column = [&](int jn, int p) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            if (tx + 32 * b != jn) continue;
+#pragma unroll
+            for (int a = 0; a < 8; ++a) {
+                const int i = ty + 16 * a;
+                col[p * NB + i] = B[a][b];
+                if (i == jn) {
+                    const double d = B[a][b];
+                    if (!(d > 0.0)) bad = 1;
+                    const double r = sqrt(fmax(d, 0.0));
+                    piv[2 * p] = r;
+                    piv[2 * p + 1] = 1.0 / r;
+                    invd[jn] = 1.0 / r;
+                }
+            }
+        }
+    };
+    publish_column(0, 0);
     __syncthreads();
     for (int j = 0; j < nb; ++j) {
-        if (t == 0) {
-            const double d = Bk[j * ld + j];
-            if (!(d > 0.0)) bad = 1;
-            Bk[j * ld + j] = sqrt(fmax(d, 0.0));
-        }
-        __syncthreads();
-        const double dj = Bk[j * ld + j];
-        // scale column j below the pivot
-        for (int i = j + 1 + t; i < nb; i += 512) Bk[i * ld + j] = Bk[i * ld + j] / dj;
-        __syncthreads();
-        // trailing update of the lower part: B[i][c] -= B[i][j]·B[c][j] for j < c <= i
-        if (tc > j && tc < nb) {
-            const double bcj = Bk[tc * ld + j];
-            for (int i = tc + ((tg - tc) & 3); i < nb; i += 4) Bk[i * ld + tc] -= Bk[i * ld + j] * bcj;
-        }
-        __syncthreads();
-    }
-    for (int r = tg; r < nb; r += 4)
-        if (tc < nb) A[(int64_t)(k0 + r) * lda + k0 + tc] = (tc <= r) ? Bk[r * ld + tc] : 0.0;
-    // inverse of the lower triangle by forward substitution, every column at once:
-    //   X[i][c] = (δ_ic − Σ_{c<=k<i} L[i][k]·X[k][c]) / L[i][i]
-    // four threads per column (k interleaved, a shuffle reduction per row). X[k][c] for k > c is kept transposed in the
-    // strict upper triangle of the block (free after the factorization), X[c][c] in xd.
-    __shared__ double xd[NB];
-    {
-        const int c = t >> 2, part = t & 3;
-        const bool active = c < nb;
-        if (active && part == 0) xd[c] = 1.0 / Bk[c * ld + c];
-        __syncwarp();
-        for (int i = 1; i < nb; ++i) {
-            double a0 = 0.0, a1 = 0.0;
-            if (active && i > c) {
-                int k = c + part;
-                for (; k + 4 < i; k += 8) {
-                    a0 = fma(Bk[i * ld + k], (k == c) ? xd[c] : Bk[c * ld + k], a0);
-                    a1 = fma(Bk[i * ld + k + 4], Bk[c * ld + k + 4], a1);
-                }
-                if (k < i) a0 = fma(Bk[i * ld + k], (k == c) ? xd[c] : Bk[c * ld + k], a0);
+        const int p = j & 1;
+        const double r = piv[2 * p], rinv = piv[2 * p + 1];
+        double li[8], lc[4];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) li[a] = col[p * NB + ty + 16 * a] * rinv;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) lc[b] = col[p * NB + tx + 32 * b] * rinv;
+        if (tx == 0) {
+#pragma unroll
+            for (int a = 0; a < 8; ++a) {
+                const int i = ty + 16 * a;
+                if (i >= j && i < nb) Lt[j * kLeafLd + i] = (i == j) ? r : li[a];
             }
-            double acc = a0 + a1;
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            if (active && part == 0 && i > c) Bk[c * ld + i] = -acc / Bk[i * ld + i];
-            __syncwarp();
+        }
+        if (j + 1 == nb) break;
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            const int i = ty + 16 * a;
+            if (i <= j || i >= nb) continue;  // warp-uniform
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                if (32 * b + 31 <= j) continue;  // warp-uniform: the whole column group is finished
+                const int c = tx + 32 * b;
+                if (c > j && c <= i) B[a][b] = fma(-li[a], lc[b], B[a][b]);
+            }
+        }
+        publish_column(j + 1, p ^ 1);
+        __syncthreads();
+    }
+    __syncthreads();  // Lt and invd complete
+    for (int i = t >> 7; i < nb; i += kLeafThreads / 128) {
+        const int c = t & 127;
+        if (c < nb) A[(int64_t)(k0 + i) * lda + k0 + c] = (c <= i) ? Lt[c * kLeafLd + i] : 0.0;
+    }
+    // inverse: B now holds R, starting at the identity
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) B[a][b] = (ty + 16 * a == tx + 32 * b && ty + 16 * a < nb) ? 1.0 : 0.0;
+    auto publish_row = [&](int jn, int p) {
+        if (ty != (jn & 15)) return;  // one warp holds row jn
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            if (ty + 16 * a != jn) continue;
+            const double s = invd[jn];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) col[p * NB + tx + 32 * b] = B[a][b] * s;
+        }
+    };
+    publish_row(0, 0);
+    __syncthreads();
+    for (int j = 0; j + 1 < nb; ++j) {
+        const int p = j & 1;
+        double xc[4], lij[8];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) xc[b] = col[p * NB + tx + 32 * b];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) lij[a] = Lt[j * kLeafLd + ty + 16 * a];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+            const int i = ty + 16 * a;
+            if (i <= j || i >= nb) continue;  // warp-uniform
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                if (32 * b > j) continue;  // warp-uniform: X[j][c] = 0 for c > j
+                B[a][b] = fma(-lij[a], xc[b], B[a][b]);
+            }
+        }
+        publish_row(j + 1, p ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        const int i = ty + 16 * a;
+        if (i >= nb) continue;
+        const double s = invd[i];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int c = tx + 32 * b;
+            if (c < nb) X[(int64_t)(k0 + i) * ldx + k0 + c] = (c <= i) ? B[a][b] * s : 0.0;
         }
     }
-    __syncthreads();
-    for (int r = tg; r < nb; r += 4)
-        if (tc < nb) X[(int64_t)(k0 + r) * ldx + k0 + tc] = (tc < r) ? Bk[tc * ld + r] : (tc == r ? xd[r] : 0.0);
     if (t == 0 && bad) atomicCAS(status, 0, LAMQ_ERR_NOT_PD);
 }
 
@@ -358,21 +447,37 @@ __global__ void ridge_diag_kernel(double *A, int64_t lda, int n, double lam) {
 
 int grid_for(int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, 148 * 16); }
 
+template <class T>
+int launch_dgemm(cudaStream_t s, const GemmArgs &g) {
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(dgemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T::kSmem);
+        attr = true;
+    }
+    dim3 grid((g.N + T::BN - 1) / T::BN, (g.M + T::BM - 1) / T::BM);
+    dgemm_kernel<T><<<grid, T::kThreads, T::kSmem, s>>>(g);
+    LAMQ_CHECK_LAUNCH("dgemm");
+    return LAMQ_OK;
+}
+
+// CTA tiles of a b x b tiling of an M x N product (half of them when only the lower triangle is computed).
+int64_t tile_count(int M, int N, int b, int lower_only) {
+    const int64_t t = (int64_t)((M + b - 1) / b) * ((N + b - 1) / b);
+    return lower_only ? (t + (M + b - 1) / b) / 2 : t;
+}
+
+// The tile shape: the largest whose grid still fills most of the 148 SMs (smaller tiles re-read more of A and B
+// from L2, which only matters for products large enough to use the 128 x 128 tiles anyway).
 int dgemm(cudaStream_t s, int transB, int M, int N, int K, double alpha, const double *A, int64_t lda,
           const double *B, int64_t ldb, double beta, double *C, int64_t ldc, int lower_only = 0, int a_lower = 0,
           int b_lower = 0) {
     if (M <= 0 || N <= 0) return LAMQ_OK;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(dgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
-        attr = true;
-    }
     const bool vec = ((uintptr_t)A % 16 == 0) && (lda % 2 == 0) && ((uintptr_t)B % 16 == 0) && (ldb % 2 == 0);
     GemmArgs g{M, N, K, alpha, beta, A, lda, B, ldb, C, ldc, transB, lower_only, a_lower, b_lower, vec ? 1 : 0};
-    dim3 grid((N + GN - 1) / GN, (M + GM - 1) / GM);
-    dgemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(g);
-    LAMQ_CHECK_LAUNCH("dgemm");
-    return LAMQ_OK;
+    constexpr int64_t kFill = 120;
+    if (tile_count(M, N, 128, lower_only) >= kFill) return launch_dgemm<TileL>(s, g);
+    if (tile_count(M, N, 64, lower_only) >= kFill) return launch_dgemm<TileM>(s, g);
+    return launch_dgemm<TileS>(s, g);
 }
 
 // Recursive Cholesky with inverse of the block [o, o+m) of A (lower part read): L overwrites A's lower part, L⁻¹ goes
@@ -380,7 +485,7 @@ int dgemm(cudaStream_t s, int transB, int M, int N, int K, double alpha, const d
 // (L22, X22) = rec(A22); X21 = −X22·(L21·X11). W has room for (m/2 + NB) x m/2 doubles.
 int chol_inv_rec(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx, int o, int m, double *W, int *status) {
     if (m <= NB) {
-        diag_block_kernel<<<1, 512, m * (m + 1) * sizeof(double), s>>>(A, lda, o, m, X, ldx, status);
+        diag_block_kernel<<<1, kLeafThreads, kLeafSmem, s>>>(A, lda, o, m, X, ldx, status);
         LAMQ_CHECK_LAUNCH("diagonal block");
         return LAMQ_OK;
     }
@@ -412,8 +517,7 @@ int chol_inv_rec(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx,
 int chol_inv(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx, int n, double *W, int *status) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(diag_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(NB * (NB + 1) * sizeof(double)));
+        cudaFuncSetAttribute(diag_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLeafSmem);
         attr = true;
     }
     int st = chol_inv_rec(s, A, lda, X, ldx, 0, n, W, status);

@@ -17,7 +17,8 @@ def spd(n, seed, tokens=None):
     return A.T @ A / len(A)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (130, 70, 17), (257, 300, 129), (1024, 512, 640)])
+# the shapes reach every CTA tile: 32 x 32 (the first three), 64 x 64 (1024 x 512) and 128 x 128 (2048 x 1100)
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (130, 70, 17), (257, 300, 129), (1024, 512, 640), (2048, 1100, 300)])
 @pytest.mark.parametrize("transB", [False, True])
 def test_gemm(M, N, K, transB):
     from lookatmyquant_b200.linalg import gemm
@@ -28,6 +29,18 @@ def test_gemm(M, N, K, transB):
     got = gemm(torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda(), C=torch.as_tensor(C).cuda(), transB=transB,
                alpha=-0.5, beta=2.0).cpu().numpy()
     ref = -0.5 * (A @ (B.T if transB else B)) + 2.0 * C
+    assert np.abs(got - ref).max() < 1e-12 * np.abs(ref).max() * np.sqrt(K)
+
+
+@pytest.mark.parametrize("M,N,K", [(100, 90, 33), (1500, 1400, 77)])
+def test_gemm_unaligned_rows(M, N, K):
+    """Operands whose rows start off a 16-byte boundary (odd leading dimension): the 8-byte copy path."""
+    from lookatmyquant_b200.linalg import gemm
+    rng = np.random.default_rng(M)
+    A = torch.as_tensor(rng.standard_normal((M, K + 1))).cuda()[:, 1:]
+    B = torch.as_tensor(rng.standard_normal((K, N + 1))).cuda()[:, 1:]
+    got = gemm(A, B).cpu().numpy()
+    ref = A.cpu().numpy() @ B.cpu().numpy()
     assert np.abs(got - ref).max() < 1e-12 * np.abs(ref).max() * np.sqrt(K)
 
 
