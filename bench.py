@@ -35,6 +35,15 @@ SMS = 148
 FP32_LANES = 128
 
 
+# DRAM bytes (read + write) of the statistics kernel per calibration token, summed over the 16 launches of one
+# config-3 layer (H and D of every stage, and of its weighted tokens): ncu dram__bytes_read.sum + dram__bytes_write.sum
+# of every xtx launch of `python -m lookatmyquant_b200.layer --tokens 65536` (31.40 GB / 65,536 tokens). The kernel's
+# traffic per token does not depend on the token count (each launch streams its tokens once through the same tile
+# order), so a launch at any token count moves this many bytes per token.
+XTX_DRAM_BYTES_PER_TOKEN = 479_169
+XTX_LAUNCHES_PER_LAYER = 16
+
+
 def peaks():
     if PEAKS.exists():
         d = json.loads(PEAKS.read_text())
@@ -290,8 +299,11 @@ class Config3:
             edges += wins * 4096 * rows
             sweep_bytes += rows * s.d * (8 + 8 + 2 + 8) + 8 * s.d * (s.d + 1) // 2
         h_tflops = h_flop / (h_ms * 1e-3) / 1e12
-        hess = {"kernel": "xtx_kernel (tcgen05 H/D accumulation)", "bound": "tensor", "achieved": h_tflops,
-                "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": h_tflops / pk["bf16_tflops"], "traffic": None,
+        ntok = self.acts[self.stages[0].name][0].shape[0]
+        traffic = XTX_DRAM_BYTES_PER_TOKEN * ntok / XTX_LAUNCHES_PER_LAYER  # per launch, like `achieved`
+        hess = {"kernel": "xtx_pair_kernel (tcgen05 H/D accumulation)", "bound": "tensor", "achieved": h_tflops,
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": h_tflops / pk["bf16_tflops"],
+                "traffic": traffic, "traffic_unit": "bytes per launch (ncu, scaled by tokens)",
                 "kernel_ms": h_ms, "peak_source": pk["source"],
                 "note": "flops counted on the executed work: H's upper triangle, D in full, weighted tokens in their own pass"}
         sw = sweep_roofline(sw_ms, sweep_bytes, edges, pk)
