@@ -25,26 +25,27 @@ namespace lamq {
 
 namespace {
 
-constexpr int GK = 16, GSTAGES = 4;
-constexpr int SA = GK + 4;   // A tile row stride (doubles): fragment loads hit every bank pair once
-constexpr int SBT = GK + 4;  // B tile (n-major, NT) row stride
-constexpr int NB = 128;      // Cholesky panel / diagonal block
+constexpr int NB = 128;  // Cholesky panel / diagonal block
 
-// One CTA tile shape of the GEMM: BM x BN, warps in a WM_ x WN_ grid, each warp FI x FJ m16n8 fragments.
-template <int BM_, int BN_, int WM_, int WN_>
+// One CTA tile shape of the GEMM: BM x BN, warps in a WM_ x WN_ grid, each warp FI x FJ m16n8 fragments; K in stages
+// of BK (a multiple of 16) through an ST-stage cp.async ring. Row strides are ≡ 4 (mod 16) doubles, so fragment loads
+// hit every bank pair the minimum number of times.
+template <int BM_, int BN_, int WM_, int WN_, int BK_, int ST_>
 struct Tiling {
-    static constexpr int BM = BM_, BN = BN_, kThreads = 32 * WM_ * WN_, kWarpsN = WN_;
+    static constexpr int BM = BM_, BN = BN_, BK = BK_, ST = ST_, kThreads = 32 * WM_ * WN_, kWarpsN = WN_;
     static constexpr int WTM = BM / WM_, WTN = BN / WN_, FI = WTM / 16, FJ = WTN / 8;
+    static constexpr int SA = BK + 4;   // A tile row stride
     static constexpr int SBN = BN + 4;  // B tile (k-major, NN) row stride
+    static constexpr int SBT = BK + 4;  // B tile (n-major, NT) row stride
     static constexpr int kATile = BM * SA;
-    static constexpr int kBTile = GK * SBN > BN * SBT ? GK * SBN : BN * SBT;
-    static constexpr size_t kSmem = GSTAGES * (size_t)(kATile + kBTile) * sizeof(double);
-    static_assert(FI >= 1 && FJ >= 1 && WTM % 16 == 0 && WTN % 8 == 0, "warp tile");
-    static_assert(BM * GK <= 8 * kThreads && BN * GK <= 8 * kThreads, "eight copy slots per thread");
+    static constexpr int kBTile = BK * SBN > BN * SBT ? BK * SBN : BN * SBT;
+    static constexpr size_t kSmem = ST * (size_t)(kATile + kBTile) * sizeof(double);
+    static_assert(FI >= 1 && FJ >= 1 && WTM % 16 == 0 && WTN % 8 == 0 && BK % 16 == 0, "tile shape");
+    static_assert(kSmem <= 232448, "shared memory");
 };
-using TileL = Tiling<128, 128, 2, 4>;  // 8 warps of 64 x 32
-using TileM = Tiling<64, 64, 2, 2>;    // 4 warps of 32 x 32
-using TileS = Tiling<32, 32, 2, 2>;    // 4 warps of 16 x 16
+using TileL = Tiling<128, 128, 2, 4, 32, 3>;  // 8 warps of 64 x 32, K stages of 32
+using TileM = Tiling<64, 64, 2, 2, 16, 4>;    // 4 warps of 32 x 32
+using TileS = Tiling<32, 32, 2, 2, 16, 4>;    // 4 warps of 16 x 16
 
 struct GemmArgs {
     int M, N, K;
@@ -89,50 +90,30 @@ __device__ __forceinline__ void cp16(double *dst, const double *src, int n) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(8 * n) : "memory");
 }
 
-// One thread's share of a tile copy, worked out once per CTA: slot q copies the element pair (r, c..c+1) of a
-// rows x cols tile (cols even, 16-byte copies) or the single element (r, c) (8-byte copies) of a row-major source,
-// zero-filling what lies outside Rmax x Cmax. Per K step only the K offset changes.
-struct TileCopy {
-    static constexpr int kSlots = 8;
-    int n;                    // slots in use
-    int soff[kSlots];         // destination offsets (doubles)
-    int64_t goff[kSlots];     // source offsets (doubles) at K offset 0
-    int rr[kSlots], cc[kSlots];
-};
-
-// `k_rows`: the tile's rows run along K (B without transposition), else its columns do.
-template <int kThreads>
-__device__ __forceinline__ void tile_copy_init(TileCopy &t, int ld, int64_t lds, int r0, int c0, int rows, int cols,
-                                               bool vec) {
-    const int per = vec ? cols / 2 : cols;
-    t.n = 0;
+// A thread's share of the copy of a ROWS x COLS tile (row stride ld in shared memory) whose top-left element is
+// (r0, c0) of a row-major source with row stride lds, shifted by k0 along K (rows when k_rows, else columns): element
+// pairs by 16-byte cp.async when VEC (both rows 16-byte aligned), single elements otherwise; what lies outside
+// Rmax x Cmax is zero-filled. The slot arithmetic uses compile-time tile widths (shifts), so nothing is precomputed.
+template <int kThreads, int ROWS, int COLS, bool VEC>
+__device__ __forceinline__ void tile_copy(double *dst, int ld, const double *src, int64_t lds, int r0, int c0, int k0,
+                                          bool k_rows, int Rmax, int Cmax) {
+    constexpr int PER = VEC ? COLS / 2 : COLS;  // copies per row
+    constexpr int SLOTS = (ROWS * PER + kThreads - 1) / kThreads;
+    if (k_rows) r0 += k0;
+    else c0 += k0;
 #pragma unroll
-    for (int q = 0; q < TileCopy::kSlots; ++q) {
+    for (int q = 0; q < SLOTS; ++q) {
         const int e = threadIdx.x + q * kThreads;
-        const int r = e / per, c = vec ? 2 * (e % per) : e % per;
-        t.soff[q] = r * ld + c;
-        t.goff[q] = (int64_t)(r0 + r) * lds + c0 + c;
-        t.rr[q] = r0 + r;
-        t.cc[q] = c0 + c;
-        if (e < rows * per) t.n = q + 1;
-    }
-}
-
-// Issues the copies for a tile whose rows (k_rows) or columns are shifted by k0 along K.
-__device__ __forceinline__ void tile_copy_issue(const TileCopy &t, double *dst, const double *src, int64_t lds, int k0,
-                                                bool k_rows, int Rmax, int Cmax, bool vec) {
-    const int64_t shift = k_rows ? (int64_t)k0 * lds : (int64_t)k0;
-#pragma unroll
-    for (int q = 0; q < TileCopy::kSlots; ++q) {
-        if (q >= t.n) break;
-        const int r = t.rr[q] + (k_rows ? k0 : 0), c = t.cc[q] + (k_rows ? 0 : k0);
-        if (vec) {
-            int nv = (r < Rmax) ? min(2, Cmax - c) : 0;
+        if (ROWS * PER % kThreads != 0 && e >= ROWS * PER) break;
+        const int r = e / PER, c = (VEC ? 2 : 1) * (e % PER);
+        const int gr = r0 + r, gc = c0 + c;
+        if (VEC) {
+            int nv = (gr < Rmax) ? min(2, Cmax - gc) : 0;
             nv = nv < 0 ? 0 : nv;
-            cp16(dst + t.soff[q], src + (nv > 0 ? t.goff[q] + shift : 0), nv);
+            cp16(dst + r * ld + c, src + (nv > 0 ? (int64_t)gr * lds + gc : 0), nv);
         } else {
-            const bool ok = r < Rmax && c < Cmax;
-            cp8(dst + t.soff[q], src + (ok ? t.goff[q] + shift : 0), ok);
+            const bool ok = gr < Rmax && gc < Cmax;
+            cp8(dst + r * ld + c, src + (ok ? (int64_t)gr * lds + gc : 0), ok);
         }
     }
 }
@@ -142,7 +123,8 @@ __device__ __forceinline__ void tile_copy_issue(const TileCopy &t, double *dst, 
 // stops near 32), K in steps of 16 through a 4-stage cp.async ring.
 template <class T>
 __global__ void __launch_bounds__(T::kThreads) dgemm_kernel(GemmArgs g) {
-    constexpr int GM = T::BM, GN = T::BN, FI = T::FI, FJ = T::FJ, WTM = T::WTM, WTN = T::WTN, SBN = T::SBN;
+    constexpr int GM = T::BM, GN = T::BN, GK = T::BK, FI = T::FI, FJ = T::FJ, WTM = T::WTM, WTN = T::WTN;
+    constexpr int SA = T::SA, SBN = T::SBN, SBT = T::SBT, ST = T::ST;
     constexpr int kATile = T::kATile, kBTile = T::kBTile;
     extern __shared__ __align__(16) double gsm[];
     const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
@@ -168,40 +150,47 @@ __global__ void __launch_bounds__(T::kThreads) dgemm_kernel(GemmArgs g) {
     auto As = [&](int s) { return gsm + (size_t)s * (kATile + kBTile); };
     auto Bs = [&](int s) { return gsm + (size_t)s * (kATile + kBTile) + kATile; };
     const bool vec = g.vec != 0;
-    TileCopy ca, cb;
-    tile_copy_init<T::kThreads>(ca, SA, g.lda, m0, 0, GM, GK, vec);  // A: GM x GK at (m0, k)
-    if (!g.transB) tile_copy_init<T::kThreads>(cb, SBN, g.ldb, 0, n0, GK, GN, vec);  // B: GK x GN at (k, n0)
-    else tile_copy_init<T::kThreads>(cb, SBT, g.ldb, n0, 0, GN, GK, vec);            // B: GN x GK at (n0, k)
+    constexpr int TH = T::kThreads;
     auto load = [&](int s, int k0) {
-        tile_copy_issue(ca, As(s), g.A, g.lda, k0, false, g.M, g.K, vec);
-        if (!g.transB) tile_copy_issue(cb, Bs(s), g.B, g.ldb, k0, true, g.K, g.N, vec);
-        else tile_copy_issue(cb, Bs(s), g.B, g.ldb, k0, false, g.N, g.K, vec);
+        if (vec) {
+            tile_copy<TH, GM, GK, true>(As(s), SA, g.A, g.lda, m0, 0, k0, false, g.M, g.K);  // A: GM x GK at (m0, k)
+            if (!g.transB) tile_copy<TH, GK, GN, true>(Bs(s), SBN, g.B, g.ldb, 0, n0, k0, true, g.K, g.N);
+            else tile_copy<TH, GN, GK, true>(Bs(s), SBT, g.B, g.ldb, n0, 0, k0, false, g.N, g.K);
+        } else {
+            tile_copy<TH, GM, GK, false>(As(s), SA, g.A, g.lda, m0, 0, k0, false, g.M, g.K);
+            if (!g.transB) tile_copy<TH, GK, GN, false>(Bs(s), SBN, g.B, g.ldb, 0, n0, k0, true, g.K, g.N);
+            else tile_copy<TH, GN, GK, false>(Bs(s), SBT, g.B, g.ldb, n0, 0, k0, false, g.N, g.K);
+        }
     };
 #pragma unroll
-    for (int s = 0; s < GSTAGES - 1; ++s) {
+    for (int s = 0; s < ST - 1; ++s) {
         if (s < ksteps) load(s, kb + s * GK);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
     for (int ks = 0; ks < ksteps; ++ks) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(GSTAGES - 2) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(ST - 2) : "memory");
         __syncthreads();  // stage ks is in, and stage ks − 1 is free for the next load
-        const int nxt = ks + GSTAGES - 1;
-        if (nxt < ksteps) load(nxt % GSTAGES, kb + nxt * GK);
+        const int nxt = ks + ST - 1;
+        if (nxt < ksteps) load(nxt % ST, kb + nxt * GK);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const double *A = As(ks % GSTAGES), *B = Bs(ks % GSTAGES);
-        double bf[FJ][4];
+        const double *A = As(ks % ST), *B = Bs(ks % ST);
 #pragma unroll
-        for (int j = 0; j < FJ; ++j)
+        for (int kk = 0; kk < GK; kk += 16) {
+            double bf[FJ][4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                bf[j][e] = g.transB ? B[(wn + 8 * j + fg) * SBT + ft + 4 * e] : B[(ft + 4 * e) * SBN + wn + 8 * j + fg];
+            for (int j = 0; j < FJ; ++j)
 #pragma unroll
-        for (int i = 0; i < FI; ++i) {
-            double af[8];
+                for (int e = 0; e < 4; ++e)
+                    bf[j][e] = g.transB ? B[(wn + 8 * j + fg) * SBT + kk + ft + 4 * e]
+                                        : B[(kk + ft + 4 * e) * SBN + wn + 8 * j + fg];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) af[e] = A[(wm + 16 * i + fg + 8 * (e & 1)) * SA + ft + 4 * (e >> 1)];
+            for (int i = 0; i < FI; ++i) {
+                double af[8];
 #pragma unroll
-            for (int j = 0; j < FJ; ++j) dmma16816(acc[i][j], af, bf[j]);
+                for (int e = 0; e < 8; ++e) af[e] = A[(wm + 16 * i + fg + 8 * (e & 1)) * SA + kk + ft + 4 * (e >> 1)];
+#pragma unroll
+                for (int j = 0; j < FJ; ++j) dmma16816(acc[i][j], af, bf[j]);
+            }
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -227,143 +216,210 @@ __global__ void __launch_bounds__(T::kThreads) dgemm_kernel(GemmArgs g) {
     }
 }
 
+// Cholesky and inverse of a 16 x 16 block by one warp: S (row stride ld) holds the block's lower part on entry and L
+// (strict upper zero) on return; Xd (row stride kLeafLdd) receives L⁻¹ (strict upper zero). Lane r (and r + 16, which
+// repeats it) holds row r; column k: r_k = rsqrt(a_kk) from lane k, l = a[k]·r_k, a[c] −= l·l_c (l_c shuffled from
+// lane c). Entries above the diagonal take updates that are never read and are stored as zero. Column r of the inverse
+// is then formed by lane r, right-looking: x_m = acc_m·r_m, acc_q −= L[q][m]·x_m (q > m), acc starting at e_r.
+constexpr int kLeafLdd = 20;  // ≡ 4 (mod 16) doubles: fragment loads hit each bank pair twice, the minimum
+
+__device__ __forceinline__ void chol_inv16(double *S, int ld, double *Xd, int *bad) {
+    const int lane = threadIdx.x & 31, r = lane & 15;
+    double a[16], rinv[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) a[c] = S[r * ld + c];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const double d = __shfl_sync(0xffffffffu, a[k], k);
+        if (lane == 0 && !(d > 0.0)) *bad = 1;
+        rinv[k] = rsqrt(d);
+        const double l = a[k] * rinv[k];
+        a[k] = l;
+#pragma unroll
+        for (int c = k + 1; c < 16; ++c) a[c] = fma(-l, __shfl_sync(0xffffffffu, l, c), a[c]);
+    }
+    if (lane < 16) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) S[r * ld + c] = (c <= r) ? a[c] : 0.0;
+    }
+    __syncwarp();
+    double acc[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) acc[m] = (m == r) ? 1.0 : 0.0;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+        const double x = acc[m] * rinv[m];
+        acc[m] = x;
+#pragma unroll
+        for (int q = m + 1; q < 16; ++q) acc[q] = fma(-S[q * ld + m], x, acc[q]);
+    }
+    if (lane < 16) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m) Xd[m * kLeafLdd + r] = acc[m];  // X[m][r]: zero for m < r
+    }
+    __syncwarp();
+}
+
 // Factors the nb x nb diagonal block at A[k0][k0] in place (lower Cholesky; the block's strict upper part set to zero)
 // and writes its inverse to X[k0][k0] (lower, strict upper zero). A non-positive pivot sets *status = LAMQ_ERR_NOT_PD.
-// 512 threads; thread (ty, tx) = (t / 32, t % 32) holds the 8 x 4 elements (ty + 16a, tx + 32b) of the block in
-// registers (cyclic, so the shrinking trailing matrix stays spread over every warp). Both phases are right-looking
-// with one barrier per column:
-//   Cholesky, column j: l = B[:, j] / √B[j][j]; B[i][c] −= l_i·l_c for j < c <= i. The owners of column j + 1 publish
-//     it (and its pivot's square root and reciprocal) to shared memory as soon as their update is done.
-//   Inverse, row j: X[j][:] = R[j][:] / L[j][j], then R[i][:] −= L[i][j]·X[j][:] for i > j, R starting at I; the warp
-//     holding row j + 1 publishes it the same way.
-// L is kept transposed in shared memory (Lt[j][i] = L[i][j]) for the inverse and the write-back.
-constexpr int kLeafThreads = 512;
-constexpr int kLeafLd = NB + 1;
-constexpr size_t kLeafSmem = (size_t)(NB * kLeafLd + 3 * NB + 4) * sizeof(double);
+// Blocked by 16-column panels on the fp64 tensor cores, 8 warps, warp w owning rows [16w, 16w + 16); the block is
+// padded to a multiple of 16 with the identity and kept in shared memory (row stride ≡ 4 mod 16 doubles).
+//   Cholesky, panel p: warp p factors and inverts its diagonal 16 x 16 block (L_pp, X_pp = L_pp⁻¹); | barrier |
+//     every later warp forms its rows of the panel, L21 = A21·X_ppᵀ, with two m16n8k16 MMAs; | barrier | and updates
+//     its trailing tiles up to its own diagonal block, A22 −= L21·L21ᵀ. The next panel's diagonal block belongs to the
+//     warp that just updated it, so no barrier is needed before it is factored.
+//   Inverse, by row panels with R = I in registers (warp w: its rows, 16 column tiles of 16 x 8): panel q forms
+//     X[q] = X_qq·R[q] (its rows of L⁻¹) in shared memory; | barrier | later warps update R[w] −= L[w][q]·X[q]; | barrier |.
+constexpr int kLeafThreads = 256;
+constexpr int kLeafLd = NB + 4;
+constexpr size_t kLeafSmem = (size_t)(NB * kLeafLd + 8 * 16 * kLeafLdd + 16 * kLeafLd) * sizeof(double);
 
-__global__ void __launch_bounds__(kLeafThreads) diag_block_kernel(double *A, int64_t lda, int k0, int nb, double *X,
-                                                                  int64_t ldx, int *status) {
+__global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, int64_t lda, int k0, int nb,
+                                                                     double *X, int64_t ldx, int *status) {
     extern __shared__ __align__(16) double lsm[];
-    double *Lt = lsm;                       // NB x kLeafLd: Lt[j][i] = L[i][j] for i >= j
-    double *col = Lt + NB * kLeafLd;        // 2 x NB: the column (Cholesky) or row (inverse) of the current step
-    double *invd = col + 2 * NB;            // NB: 1 / L[j][j]
-    double *piv = invd + NB;                // 2 x 2: √B[j][j] and its reciprocal, double-buffered
+    double *Ls = lsm;                         // the padded block, row-major; L on the way out
+    double *Xd = Ls + NB * kLeafLd;           // the diagonal blocks' inverses, 16 x kLeafLdd each
+    double *Xp = Xd + 8 * 16 * kLeafLdd;      // one row panel of L⁻¹ (inverse phase)
     __shared__ int bad;
-    const int t = threadIdx.x, ty = t >> 5, tx = t & 31;
-    double B[8][4];
-#pragma unroll
-    for (int a = 0; a < 8; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int i = ty + 16 * a, c = tx + 32 * b;
-            B[a][b] = (i < nb && c <= i) ? A[(int64_t)(k0 + i) * lda + k0 + c] : 0.0;
+    const int t = threadIdx.x, w = t >> 5, lane = t & 31, g = lane >> 2, tq = lane & 3;
+    const int P = (nb + 15) >> 4, nbp = 16 * P;
+    // staging: thread t covers column t % 128 of rows t / 128, t / 128 + 2, ... (16 independent loads in flight)
+    {
+        const int c = t & (NB - 1);
+        const double *src = A + (int64_t)k0 * lda + k0 + c;
+#pragma unroll 16
+        for (int i = t >> 7; i < nbp; i += kLeafThreads / NB) {
+            double v = (i == c) ? 1.0 : 0.0;
+            if (i < nb && c < nb) v = (c <= i) ? __ldg(src + (int64_t)i * lda) : 0.0;
+            if (c < nbp) Ls[i * kLeafLd + c] = v;
         }
+    }
     if (t == 0) bad = 0;
-    __syncthreads();  // bad is initialized before any pivot owner may set it
-    // the owners of column jn publish it and its pivot into buffer p
-    auto publish_column = [&](int jn, int p) {
+    __syncthreads();
+    for (int p = 0; p < P; ++p) {
+        const int j0 = 16 * p;
+        if (w == p) chol_inv16(Ls + j0 * kLeafLd + j0, kLeafLd, Xd + p * 16 * kLeafLdd, &bad);
+        __syncthreads();
+        const bool mine = w > p && w < P;
+        double *band = Ls + (16 * w) * kLeafLd;
+        if (mine) {  // L21 = A21 · X_ppᵀ for rows [16w, 16w + 16)
+            double af[8], b0[4], b1[4], d0[4] = {0.0, 0.0, 0.0, 0.0}, d1[4] = {0.0, 0.0, 0.0, 0.0};
+            const double *xp = Xd + p * 16 * kLeafLdd;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            if (tx + 32 * b != jn) continue;
+            for (int e = 0; e < 8; ++e) af[e] = band[(g + 8 * (e & 1)) * kLeafLd + j0 + tq + 4 * (e >> 1)];
 #pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const int i = ty + 16 * a;
-                col[p * NB + i] = B[a][b];
-                if (i == jn) {
-                    const double d = B[a][b];
-                    if (!(d > 0.0)) bad = 1;
-                    const double r = sqrt(fmax(d, 0.0));
-                    piv[2 * p] = r;
-                    piv[2 * p + 1] = 1.0 / r;
-                    invd[jn] = 1.0 / r;
+            for (int e = 0; e < 4; ++e) {
+                b0[e] = xp[g * kLeafLdd + tq + 4 * e];
+                b1[e] = xp[(8 + g) * kLeafLdd + tq + 4 * e];
+            }
+            dmma16816(d0, af, b0);
+            dmma16816(d1, af, b1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                double *row = band + (g + 8 * h) * kLeafLd + j0 + 2 * tq;
+                *reinterpret_cast<double2 *>(row) = make_double2(d0[2 * h], d0[2 * h + 1]);
+                *reinterpret_cast<double2 *>(row + 8) = make_double2(d1[2 * h], d1[2 * h + 1]);
+            }
+        }
+        __syncthreads();
+        if (mine) {  // A22 −= L21 · L21ᵀ over this band's column tiles 2p + 2 .. 2w + 1
+            double af[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) af[e] = -band[(g + 8 * (e & 1)) * kLeafLd + j0 + tq + 4 * (e >> 1)];
+#pragma unroll
+            for (int ct = 2; ct < 16; ++ct) {  // unrolled so the independent tiles' MMAs overlap
+                if (ct < 2 * p + 2 || ct > 2 * w + 1) continue;  // warp-uniform
+                double bf[4], cf[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) bf[e] = Ls[(8 * ct + g) * kLeafLd + j0 + tq + 4 * e];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const double2 v = *reinterpret_cast<const double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq);
+                    cf[2 * h] = v.x;
+                    cf[2 * h + 1] = v.y;
+                }
+                dmma16816(cf, af, bf);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    *reinterpret_cast<double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq) =
+                        make_double2(cf[2 * h], cf[2 * h + 1]);
+            }
+        }
+    }
+    __syncthreads();
+    {
+        const int c = t & (NB - 1);
+        double *dst = A + (int64_t)k0 * lda + k0 + c;
+        if (c < nb) {
+#pragma unroll 8
+            for (int i = t >> 7; i < nb; i += kLeafThreads / NB) dst[(int64_t)i * lda] = Ls[i * kLeafLd + c];
+        }
+    }
+    // inverse: R[ct][e] = element (16w + g + 8(e >> 1), 8ct + 2tq + (e & 1)) of this warp's band, starting at I
+    double R[16][4];
+#pragma unroll
+    for (int ct = 0; ct < 16; ++ct)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) R[ct][e] = (16 * w + g + 8 * (e >> 1) == 8 * ct + 2 * tq + (e & 1)) ? 1.0 : 0.0;
+    for (int q = 0; q < P; ++q) {
+        if (w == q) {  // X[q] = X_qq · R[q]: only the column tiles ct < 2q + 2 are non-zero
+#pragma unroll
+            for (int ct = 0; ct < 16; ++ct) {
+                if (ct >= 2 * q + 2) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    *reinterpret_cast<double2 *>(Xp + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq) =
+                        make_double2(R[ct][2 * h], R[ct][2 * h + 1]);
+            }
+            __syncwarp();
+            double af[8];
+            const double *xq = Xd + q * 16 * kLeafLdd;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) af[e] = xq[(g + 8 * (e & 1)) * kLeafLdd + tq + 4 * (e >> 1)];
+#pragma unroll
+            for (int ct = 0; ct < 16; ++ct) {
+                if (ct >= 2 * q + 2) continue;
+                double bf[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) bf[e] = Xp[(tq + 4 * e) * kLeafLd + 8 * ct + g];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) R[ct][e] = 0.0;
+                dmma16816(R[ct], af, bf);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int ct = 0; ct < 16; ++ct) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = 16 * q + g + 8 * h, c = 8 * ct + 2 * tq;
+                    const double v0 = (ct < 2 * q + 2) ? R[ct][2 * h] : 0.0;
+                    const double v1 = (ct < 2 * q + 2) ? R[ct][2 * h + 1] : 0.0;
+                    if (ct < 2 * q + 2)
+                        *reinterpret_cast<double2 *>(Xp + (g + 8 * h) * kLeafLd + c) = make_double2(v0, v1);
+                    if (i < nb) {
+                        double *xr = X + (int64_t)(k0 + i) * ldx + k0;
+                        if (c < nb) xr[c] = v0;
+                        if (c + 1 < nb) xr[c + 1] = v1;
+                    }
                 }
             }
         }
-    };
-    publish_column(0, 0);
-    __syncthreads();
-    for (int j = 0; j < nb; ++j) {
-        const int p = j & 1;
-        const double r = piv[2 * p], rinv = piv[2 * p + 1];
-        double li[8], lc[4];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) li[a] = col[p * NB + ty + 16 * a] * rinv;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) lc[b] = col[p * NB + tx + 32 * b] * rinv;
-        if (tx == 0) {
-#pragma unroll
-            for (int a = 0; a < 8; ++a) {
-                const int i = ty + 16 * a;
-                if (i >= j && i < nb) Lt[j * kLeafLd + i] = (i == j) ? r : li[a];
-            }
-        }
-        if (j + 1 == nb) break;
-#pragma unroll
-        for (int a = 0; a < 8; ++a) {
-            const int i = ty + 16 * a;
-            if (i <= j || i >= nb) continue;  // warp-uniform
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                if (32 * b + 31 <= j) continue;  // warp-uniform: the whole column group is finished
-                const int c = tx + 32 * b;
-                if (c > j && c <= i) B[a][b] = fma(-li[a], lc[b], B[a][b]);
-            }
-        }
-        publish_column(j + 1, p ^ 1);
         __syncthreads();
-    }
-    __syncthreads();  // Lt and invd complete
-    for (int i = t >> 7; i < nb; i += kLeafThreads / 128) {
-        const int c = t & 127;
-        if (c < nb) A[(int64_t)(k0 + i) * lda + k0 + c] = (c <= i) ? Lt[c * kLeafLd + i] : 0.0;
-    }
-    // inverse: B now holds R, starting at the identity
+        if (w > q && w < P) {  // R[w] −= L[w][q] · X[q]
+            double af[8];
+            const double *band = Ls + (16 * w) * kLeafLd + 16 * q;
 #pragma unroll
-    for (int a = 0; a < 8; ++a)
+            for (int e = 0; e < 8; ++e) af[e] = -band[(g + 8 * (e & 1)) * kLeafLd + tq + 4 * (e >> 1)];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) B[a][b] = (ty + 16 * a == tx + 32 * b && ty + 16 * a < nb) ? 1.0 : 0.0;
-    auto publish_row = [&](int jn, int p) {
-        if (ty != (jn & 15)) return;  // one warp holds row jn
+            for (int ct = 0; ct < 16; ++ct) {
+                if (ct >= 2 * q + 2) continue;
+                double bf[4];
 #pragma unroll
-        for (int a = 0; a < 8; ++a) {
-            if (ty + 16 * a != jn) continue;
-            const double s = invd[jn];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) col[p * NB + tx + 32 * b] = B[a][b] * s;
-        }
-    };
-    publish_row(0, 0);
-    __syncthreads();
-    for (int j = 0; j + 1 < nb; ++j) {
-        const int p = j & 1;
-        double xc[4], lij[8];
-#pragma unroll
-        for (int b = 0; b < 4; ++b) xc[b] = col[p * NB + tx + 32 * b];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) lij[a] = Lt[j * kLeafLd + ty + 16 * a];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) {
-            const int i = ty + 16 * a;
-            if (i <= j || i >= nb) continue;  // warp-uniform
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                if (32 * b > j) continue;  // warp-uniform: X[j][c] = 0 for c > j
-                B[a][b] = fma(-lij[a], xc[b], B[a][b]);
+                for (int e = 0; e < 4; ++e) bf[e] = Xp[(tq + 4 * e) * kLeafLd + 8 * ct + g];
+                dmma16816(R[ct], af, bf);
             }
         }
-        publish_row(j + 1, p ^ 1);
         __syncthreads();
-    }
-#pragma unroll
-    for (int a = 0; a < 8; ++a) {
-        const int i = ty + 16 * a;
-        if (i >= nb) continue;
-        const double s = invd[i];
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int c = tx + 32 * b;
-            if (c < nb) X[(int64_t)(k0 + i) * ldx + k0 + c] = (c <= i) ? B[a][b] * s : 0.0;
-        }
     }
     if (t == 0 && bad) atomicCAS(status, 0, LAMQ_ERR_NOT_PD);
 }

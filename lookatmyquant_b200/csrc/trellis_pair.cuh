@@ -6,9 +6,10 @@
 // predecessors in registers as fp32 pairs (half the registers of one warp per row, so twice the warps fit on an SM).
 // (x − C)² and its add to the best predecessor cost are computed two states at a time with sub/mul/add.rn.f32x2
 // (states r and r + 1 share their predecessors): every value is rounded exactly as the reference's scalar fp32 sub, mul
-// and add (explicit rounding, never fused). The minimum over the 2^k predecessors is a knock-out tournament whose decisions are the sign bits of fp32
-// differences (the fp32 pipe, not the half-rate compare/select pipe) appended to the back-pointer words by funnel
-// shifts: 2^k − 1 bits per r, decoded on the traceback. The pair exchanges the R best values through shared memory
+// and add (explicit rounding, never fused). The minimum over the 2^k predecessors is a knock-out tournament (for
+// k >= 3 two states at a time on packed differences) whose decisions are the sign bits of fp32 differences (the fp32
+// pipe, not the half-rate compare/select pipe) appended to the back-pointer words by funnel shifts: 2^k − 1 bits per
+// r, decoded on the traceback. The pair exchanges the R best values through shared memory
 // (double buffered, one named barrier per step), stored in 16-byte units swizzled by writer thread so that writes and
 // reads are free of bank conflicts for every k.
 #pragma once
@@ -128,6 +129,38 @@ __device__ __forceinline__ float tournament(float (&m)[PairTrellis<K>::NB], uint
     return m[0];
 }
 
+// Whether the two states r, r + 1 of a pair run their tournaments together (tournament2, interleaved decision bits):
+// faster for 8 and 16 predecessors, slower for 2 and 4 (measured on B200).
+template <int K>
+constexpr bool kPairedTournament = K >= 3;
+
+// Knock-out minimum of NB costs for the two states r and r + 1 at once (m[h] holds their costs as an fp32 pair): pairs,
+// then pairs of winners, …, the left (smaller h) winning ties — the first minimum, as torch.min picks it. One packed
+// subtraction gives both states' differences (each rounded as the scalar fp32 subtraction). The decision bits are
+// appended interleaved, state r then r + 1 for each comparison in order (level 1 left to right, then level 2, …), so the
+// pair (r, r + 1) owns 2·(NB − 1) consecutive bits and comparison c of state r + e is bit 2c + e of them.
+template <int K>
+__device__ __forceinline__ u64 tournament2(u64 (&m)[PairTrellis<K>::NB], uint32_t (&words)[PairTrellis<K>::WORDS],
+                                           int seq) {
+    constexpr int NB = PairTrellis<K>::NB;
+    int q = 0;
+#pragma unroll
+    for (int n = NB; n > 1; n >>= 1) {
+#pragma unroll
+        for (int g = 0; g < n / 2; ++g) {
+            float dlo, dhi, alo, ahi, blo, bhi;
+            upk2(sub2(m[2 * g + 1], m[2 * g]), dlo, dhi);
+            push_bit<K>(words, seq + 2 * q, dlo);
+            push_bit<K>(words, seq + 2 * q + 1, dhi);
+            ++q;
+            upk2(m[2 * g], alo, ahi);
+            upk2(m[2 * g + 1], blo, bhi);
+            m[g] = pk2(fminf(alo, blo), fminf(ahi, bhi));
+        }
+    }
+    return m[0];
+}
+
 // One add-compare-select step for the thread's RT values of r: best_t into bout, the decision bits into words.
 template <int K>
 __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *__restrict__ bout, float xp, int p,
@@ -162,14 +195,21 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
 #pragma unroll
         for (int i = 0; i < CI; i += 2) {
             const int ii = c0 + i;
-            float clo[T::NB], chi[T::NB];
+            u64 c2[T::NB];
 #pragma unroll
             for (int h = 0; h < T::NB; ++h) {
                 const u64 d = sub2(xx, cv[h][ii >> 1]);  // (x − C) for r = ii and ii + 1
-                upk2(add2(bb[h][(CH == 4) ? (i >> K) : 0], mul2(d, d)), clo[h], chi[h]);  // best + (x − C)²
+                c2[h] = add2(bb[h][(CH == 4) ? (i >> K) : 0], mul2(d, d));  // best + (x − C)²
             }
-            nb4[i & 3] = tournament<K>(clo, words, ii * (T::NB - 1));
-            nb4[(i & 3) + 1] = tournament<K>(chi, words, (ii + 1) * (T::NB - 1));
+            if constexpr (kPairedTournament<K>) {
+                upk2(tournament2<K>(c2, words, ii * (T::NB - 1)), nb4[i & 3], nb4[(i & 3) + 1]);
+            } else {
+                float clo[T::NB], chi[T::NB];
+#pragma unroll
+                for (int h = 0; h < T::NB; ++h) upk2(c2[h], clo[h], chi[h]);
+                nb4[i & 3] = tournament<K>(clo, words, ii * (T::NB - 1));
+                nb4[(i & 3) + 1] = tournament<K>(chi, words, (ii + 1) * (T::NB - 1));
+            }
             if ((i & 3) == 2)
                 *reinterpret_cast<float4 *>(bout + pslot<K>(p * T::RT + ii - 2)) =
                     make_float4(nb4[0], nb4[1], nb4[2], nb4[3]);
@@ -187,7 +227,8 @@ __device__ __forceinline__ int decode_choice(const uint32_t *__restrict__ args, 
     for (int l = 1; l < K; ++l) before += T::NB >> l;  // comparisons below the top level
 #pragma unroll
     for (int lvl = K; lvl >= 1; --lvl) {
-        const int seq = i * (T::NB - 1) + before + g;
+        const int seq = kPairedTournament<K> ? (i & ~1) * (T::NB - 1) + 2 * (before + g) + (i & 1)  // interleaved
+                                             : i * (T::NB - 1) + before + g;
         const int w = seq >> 5;
         const int nbw = (T::NBITS - 32 * w) < 32 ? (T::NBITS - 32 * w) : 32;
         const uint32_t word = args[w * 64 + owner];
