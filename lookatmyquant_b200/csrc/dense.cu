@@ -127,7 +127,21 @@ __global__ void __launch_bounds__(T::kThreads) dgemm_kernel(GemmArgs g) {
     constexpr int SA = T::SA, SBN = T::SBN, SBT = T::SBT, ST = T::ST;
     constexpr int kATile = T::kATile, kBTile = T::kBTile;
     extern __shared__ __align__(16) double gsm[];
-    const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
+    // Tiles in launch order, the longest K ranges first when an operand is triangular (CTAs start in block order, so
+    // the short tiles fill the last wave): A lower — K grows with the row tile; B lower — with the column tile (NT) or
+    // shrinks with it (NN).
+    int mt = blockIdx.y, nt = blockIdx.x;
+    {
+        const int lin = blockIdx.x + gridDim.x * blockIdx.y;
+        if (g.a_lower) {
+            mt = gridDim.y - 1 - lin / gridDim.x;
+            nt = lin % gridDim.x;
+        } else if (g.b_lower) {
+            nt = g.transB ? gridDim.x - 1 - lin / gridDim.y : lin / gridDim.y;
+            mt = lin % gridDim.y;
+        }
+    }
+    const int m0 = mt * GM, n0 = nt * GN;
     if (g.lower_only && m0 + GM - 1 < n0) return;  // every row of the tile is above the diagonal
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int wm = (warp / T::kWarpsN) * WTM, wn = (warp % T::kWarpsN) * WTN;  // warp tile WTM x WTN
