@@ -8,8 +8,8 @@
 // (states r and r + 1 share their predecessors): every value is rounded exactly as the reference's scalar fp32 sub, mul
 // and add (explicit rounding, never fused). The minimum over the 2^k predecessors is a knock-out tournament (for
 // k >= 3 two states at a time on packed differences) whose decisions are the sign bits of fp32 differences (the fp32
-// pipe, not the half-rate compare/select pipe) appended to the back-pointer words by funnel shifts: 2^k − 1 bits per
-// r, decoded on the traceback. The pair exchanges the R best values through shared memory
+// pipe, not the half-rate compare/select pipe); the winner's k index bits are assembled from them by bit selects and
+// appended to one back-pointer word per thread per step, so the traceback reads each step's choice with one shift. The pair exchanges the R best values through shared memory
 // (double buffered, one named barrier per step), stored in 16-byte units swizzled by writer thread so that writes and
 // reads are free of bank conflicts for every k.
 #pragma once
@@ -26,10 +26,10 @@ struct PairTrellis {
     static constexpr int DIST = (RT >> K) > 0 ? (RT >> K) : 1;  // distinct best values a thread reads per h
     static constexpr int UNITS = RT / 4;                        // 16-byte units a thread writes
     static constexpr int SH = (UNITS >= 8) ? 3 : (UNITS == 4) ? 2 : (UNITS == 2) ? 1 : 0;
-    static constexpr int NBITS = RT * (NB - 1);                 // tournament bits per thread per step
-    static constexpr int WORDS = (NBITS + 31) / 32;
+    static constexpr int NBITS = RT * K;                        // back-pointer bits per thread per step (64K/NB <= 32)
+    static constexpr int WORDS = 1;
     static_assert(NB * RT == 64, "each thread covers 64 predecessor states");
-    static_assert(WORDS <= 2, "at most two back-pointer words per thread per step");
+    static_assert(NBITS <= 32, "one back-pointer word per thread per step");
 };
 
 template <int K>
@@ -102,62 +102,75 @@ __device__ __forceinline__ void init_best_pair(float *best, int p, bool has_star
     }
 }
 
-// Appends the decision bit of one comparison — the sign of c_b − c_a, set exactly when c_b < c_a (for these
-// non-negative costs the rounded difference has the sign of the exact one; ties and inf − inf give 0, keeping a) —
-// to the back-pointer word of sequence index `seq` (compile-time), by a funnel shift.
-template <int K>
-__device__ __forceinline__ void push_bit(uint32_t (&words)[PairTrellis<K>::WORDS], int seq, float d) {
-    words[seq >> 5] = __funnelshift_l(__float_as_uint(d), words[seq >> 5], 1);
+// Decision words: the sign bit of c_b − c_a is set exactly when c_b < c_a (for these non-negative costs the rounded
+// difference has the sign of the exact one; ties and inf − inf give 0, keeping a). The tournament carries, for each
+// surviving slot, the sign-bit words of its winner's index bits: a later level's decision selects between the two
+// halves' words bit by bit (one LOP3 each), so at the end the K bits of the winning predecessor h are known and are
+// appended (most significant first) to the thread's back-pointer word by funnel shifts — K bits per r, one word per
+// step, decoded on the traceback with a single shift.
+__device__ __forceinline__ uint32_t sel_bits(uint32_t e, uint32_t right, uint32_t left) {
+    return (e & right) | (~e & left);  // bit 31: right's when the right side won
 }
 
 // Knock-out minimum of NB costs (pairs, then pairs of winners, …), the left (smaller h) winning ties: the first
-// minimum, as torch.min picks it. Appends the NB − 1 decision bits in order (level 1 left to right, then level 2, …).
+// minimum, as torch.min picks it. Appends the winner's K index bits to `word`.
 template <int K>
-__device__ __forceinline__ float tournament(float (&m)[PairTrellis<K>::NB], uint32_t (&words)[PairTrellis<K>::WORDS],
-                                            int seq) {
+__device__ __forceinline__ float tournament(float (&m)[PairTrellis<K>::NB], uint32_t &word) {
     constexpr int NB = PairTrellis<K>::NB;
-    int q = 0;
+    uint32_t idx[NB / 2][K];
+    int lvl = 0;
 #pragma unroll
-    for (int n = NB; n > 1; n >>= 1) {
+    for (int n = NB; n > 1; n >>= 1, ++lvl) {
 #pragma unroll
         for (int g = 0; g < n / 2; ++g) {
-            push_bit<K>(words, seq + q, __fsub_rn(m[2 * g + 1], m[2 * g]));
-            ++q;
+            const uint32_t e = __float_as_uint(__fsub_rn(m[2 * g + 1], m[2 * g]));
+#pragma unroll
+            for (int b = 0; b < lvl; ++b) idx[g][b] = sel_bits(e, idx[2 * g + 1][b], idx[2 * g][b]);
+            idx[g][lvl] = e;
             m[g] = fminf(m[2 * g], m[2 * g + 1]);
         }
     }
+#pragma unroll
+    for (int b = K - 1; b >= 0; --b) word = __funnelshift_l(idx[0][b], word, 1);
     return m[0];
 }
 
-// Whether the two states r, r + 1 of a pair run their tournaments together (tournament2, interleaved decision bits):
-// faster for 8 and 16 predecessors, slower for 2 and 4 (measured on B200).
+// Whether the two states r, r + 1 of a pair run their tournaments together (tournament2): faster for 8 and 16
+// predecessors, slower for 2 and 4 (measured on B200).
 template <int K>
 constexpr bool kPairedTournament = K >= 3;
 
-// Knock-out minimum of NB costs for the two states r and r + 1 at once (m[h] holds their costs as an fp32 pair): pairs,
-// then pairs of winners, …, the left (smaller h) winning ties — the first minimum, as torch.min picks it. One packed
-// subtraction gives both states' differences (each rounded as the scalar fp32 subtraction). The decision bits are
-// appended interleaved, state r then r + 1 for each comparison in order (level 1 left to right, then level 2, …), so the
-// pair (r, r + 1) owns 2·(NB − 1) consecutive bits and comparison c of state r + e is bit 2c + e of them.
+// The tournament for the two states r and r + 1 at once (m[h] holds their costs as an fp32 pair): one packed
+// subtraction gives both states' differences (each rounded as the scalar fp32 subtraction). Appends r's K index bits,
+// then r + 1's.
 template <int K>
-__device__ __forceinline__ u64 tournament2(u64 (&m)[PairTrellis<K>::NB], uint32_t (&words)[PairTrellis<K>::WORDS],
-                                           int seq) {
+__device__ __forceinline__ u64 tournament2(u64 (&m)[PairTrellis<K>::NB], uint32_t &word) {
     constexpr int NB = PairTrellis<K>::NB;
-    int q = 0;
+    uint32_t ilo[NB / 2][K], ihi[NB / 2][K];
+    int lvl = 0;
 #pragma unroll
-    for (int n = NB; n > 1; n >>= 1) {
+    for (int n = NB; n > 1; n >>= 1, ++lvl) {
 #pragma unroll
         for (int g = 0; g < n / 2; ++g) {
             float dlo, dhi, alo, ahi, blo, bhi;
             upk2(sub2(m[2 * g + 1], m[2 * g]), dlo, dhi);
-            push_bit<K>(words, seq + 2 * q, dlo);
-            push_bit<K>(words, seq + 2 * q + 1, dhi);
-            ++q;
+            const uint32_t elo = __float_as_uint(dlo), ehi = __float_as_uint(dhi);
+#pragma unroll
+            for (int b = 0; b < lvl; ++b) {
+                ilo[g][b] = sel_bits(elo, ilo[2 * g + 1][b], ilo[2 * g][b]);
+                ihi[g][b] = sel_bits(ehi, ihi[2 * g + 1][b], ihi[2 * g][b]);
+            }
+            ilo[g][lvl] = elo;
+            ihi[g][lvl] = ehi;
             upk2(m[2 * g], alo, ahi);
             upk2(m[2 * g + 1], blo, bhi);
             m[g] = pk2(fminf(alo, blo), fminf(ahi, bhi));
         }
     }
+#pragma unroll
+    for (int b = K - 1; b >= 0; --b) word = __funnelshift_l(ilo[0][b], word, 1);
+#pragma unroll
+    for (int b = K - 1; b >= 0; --b) word = __funnelshift_l(ihi[0][b], word, 1);
     return m[0];
 }
 
@@ -202,13 +215,13 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
                 c2[h] = add2(bb[h][(CH == 4) ? (i >> K) : 0], mul2(d, d));  // best + (x − C)²
             }
             if constexpr (kPairedTournament<K>) {
-                upk2(tournament2<K>(c2, words, ii * (T::NB - 1)), nb4[i & 3], nb4[(i & 3) + 1]);
+                upk2(tournament2<K>(c2, words[0]), nb4[i & 3], nb4[(i & 3) + 1]);
             } else {
                 float clo[T::NB], chi[T::NB];
 #pragma unroll
                 for (int h = 0; h < T::NB; ++h) upk2(c2[h], clo[h], chi[h]);
-                nb4[i & 3] = tournament<K>(clo, words, ii * (T::NB - 1));
-                nb4[(i & 3) + 1] = tournament<K>(chi, words, (ii + 1) * (T::NB - 1));
+                nb4[i & 3] = tournament<K>(clo, words[0]);
+                nb4[(i & 3) + 1] = tournament<K>(chi, words[0]);
             }
             if ((i & 3) == 2)
                 *reinterpret_cast<float4 *>(bout + pslot<K>(p * T::RT + ii - 2)) =
@@ -217,25 +230,12 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
     }
 }
 
-// The chosen predecessor h of r at a step, decoded from the owner thread's tournament bits (args: WORDS x 64 words).
+// The chosen predecessor h of r at a step: the owner thread's K bits for its i-th r (args: 64 words, one per thread).
 template <int K>
 __device__ __forceinline__ int decode_choice(const uint32_t *__restrict__ args, int r) {
     using T = PairTrellis<K>;
     const int owner = r / T::RT, i = r % T::RT;
-    int g = 0, before = 0;
-#pragma unroll
-    for (int l = 1; l < K; ++l) before += T::NB >> l;  // comparisons below the top level
-#pragma unroll
-    for (int lvl = K; lvl >= 1; --lvl) {
-        const int seq = kPairedTournament<K> ? (i & ~1) * (T::NB - 1) + 2 * (before + g) + (i & 1)  // interleaved
-                                             : i * (T::NB - 1) + before + g;
-        const int w = seq >> 5;
-        const int nbw = (T::NBITS - 32 * w) < 32 ? (T::NBITS - 32 * w) : 32;
-        const uint32_t word = args[w * 64 + owner];
-        g = 2 * g + (int)((word >> (nbw - 1 - (seq & 31))) & 1u);
-        if (lvl > 1) before -= T::NB >> (lvl - 1);
-    }
-    return g;
+    return (int)((args[owner] >> (T::NBITS - K - i * K)) & (uint32_t)(T::NB - 1));
 }
 
 // First state of minimum final cost over the pair (smallest state on ties); red holds 4 words of pair scratch.
