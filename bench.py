@@ -198,9 +198,21 @@ class Config3:
         self.stage_ms = {}
 
     def step(self, timed=False):
-        from lookatmyquant_b200.layer import build_stage, stacked_tables
+        from lookatmyquant_b200.hessian import Statistics
+        from lookatmyquant_b200.layer import build_stage, build_stages_sharded, stacked_tables
         tables = stacked_tables(12, 256, self.device)
         out = {}
+        if self.world >= 4:  # every stage's statistics first, the stages' factorizations on separate rank pairs
+            stats = []
+            for s in self.stages:
+                x, xr = self.acts[s.name]
+                st = Statistics(s.d, cross=True, device=self.device)
+                st.add(x, self.w, xr)
+                stats.append(st)
+            out = build_stages_sharded(self.stages, self.weights, stats, self.bits, 0, self.group, True, tables,
+                                       self.tokens)
+            self.gather(out)
+            return out
         for s in self.stages:
             if timed:
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -256,7 +268,9 @@ class Config3:
                 "row_plan": "per 64-row group widths {1,2,3,4} w.p. {.15,.45,.30,.10}",
                 "trellis": "L=12 reference e-means tables (4096 states) for every width",
                 "qep_alpha": 0.5, "width": 16, "look": 8, "lazy": 128,
-                "parallelism": f"tokens x{self.world} (H/D all-reduce), rows x{self.world}",
+                "parallelism": f"tokens x{self.world} (H/D all-reduce), rows x{self.world}, " +
+                               ("each stage's two factorizations on ranks 0/1, broadcast" if self.world < 4 else
+                                "the stages' factorizations on separate rank pairs, broadcast"),
                 "l2": "inputs (60 GB of activations) far larger than L2"}
 
     def roofline(self, pk):

@@ -25,19 +25,22 @@ class Environment:
         self.U, self.dead, self.check = env_factor(self._H0, damp, status)
 
     @classmethod
-    def from_factor(cls, H: torch.Tensor, U: torch.Tensor, dead: torch.Tensor, status: torch.Tensor,
+    def from_factor(cls, H, U: torch.Tensor, dead: torch.Tensor, status: torch.Tensor,
                     damp: float = 0.01) -> "Environment":
         """An environment whose factor was computed elsewhere (another rank): U, the dead flags and the status word
-        of that factorization."""
+        of that factorization. `H` is the matrix or a zero-argument callable that forms it (only `H`/`error` use it,
+        so a rank that only sweeps never forms it)."""
         from .linalg import status_check
         env = cls.__new__(cls)
-        env.G, env._H0, env.damp = None, H.double(), damp
+        env.G, env._H0, env.damp = None, H if callable(H) else H.double(), damp
         env.U, env.dead, env.check = U, dead.bool(), status_check(status)
         return env
 
     @property
     def H(self) -> torch.Tensor:
         """The damped H (frame.py:517-521)."""
+        if callable(self._H0):
+            self._H0 = self._H0().double()
         H = self._H0.clone()
         idx = torch.nonzero(self.dead).flatten()
         H[idx, idx] = 1

@@ -98,19 +98,32 @@ def build_stage(spec: StageSpec, weights: dict, x: torch.Tensor, x_ref: torch.Te
     return build_stage_from_statistics(spec, weights, st, bits, layer, group, dequantize, tables, n_tok_total)
 
 
-def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, bits: dict, layer: int = 0, group=None,
-                                dequantize: bool = True, tables=None, n_tok_total: int | None = None) -> StageResult:
-    """The stage after its statistics have been accumulated (all of this rank's tokens added to `st`)."""
-    dev = st.device
-    world = group.size() if group is not None else 1
-    rank = group.rank() if group is not None else 0
+def _in_seed(spec: StageSpec, layer: int) -> int:
+    """The stage's input-rotation seed (quantize.py:1531: 1000·layer + 100·block_seed + 1)."""
+    return 1000 * layer + 100 * {"self_attn": 2, "mlp": 3}[spec.block] + 1
+
+
+def _reduce_finalize(st: Statistics, group, n_tok_total):
+    """H and D of a stage: the ranks' fp32 accumulators summed (one all-reduce each), then finalized."""
     n_tok = st.n_tok
     if group is not None:
         torch.distributed.all_reduce(st.accH, group=group)
         torch.distributed.all_reduce(st.accD, group=group)
-        n_tok = n_tok_total if n_tok_total is not None else n_tok * world
-    H, D = st.finalize(n_tok)
-    in_seed = 1000 * layer + 100 * {"self_attn": 2, "mlp": 3}[spec.block] + 1
+        n_tok = n_tok_total if n_tok_total is not None else n_tok * group.size()
+    return st.finalize(n_tok)
+
+
+def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, bits: dict, layer: int = 0, group=None,
+                                dequantize: bool = True, tables=None, n_tok_total: int | None = None, HD=None,
+                                factors=None) -> StageResult:
+    """The stage after its statistics have been accumulated (all of this rank's tokens added to `st`). `HD` (H, D)
+    and `factors` (env, Linv, qep_status) skip the reduction and the factorizations when they were done already
+    (build_stages_sharded)."""
+    dev = st.device if st is not None else HD[0].device
+    world = group.size() if group is not None else 1
+    rank = group.rank() if group is not None else 0
+    H, D = _reduce_finalize(st, group, n_tok_total) if HD is None else HD
+    in_seed = _in_seed(spec, layer)
     # all rows of the stage, this rank's contiguous share (whole 64-row groups)
     names = [nm for nm, _ in spec.matrices]
     total = sum(r for _, r in spec.matrices)
@@ -120,17 +133,17 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev)
     rot = Rotation(spec.d, in_seed, dev)
-    if world >= 2:
+    if factors is None and world >= 2:
         # two ranks factor at once, one matrix each, and broadcast the factors (NVLink): the QEP's inverse Cholesky
         # factor from rank 1, the environment's U from rank 0
-        env, Linv, qst = _factors_on_two_ranks(rot, H, rank, group)
-        side.wait_stream(main)
-    else:
-        side.wait_stream(main)
+        factors = _factors_on_two_ranks(rot, H, rank, group)
+    side.wait_stream(main)
     Xs, ks, spans, off = [], [], {}, 0
     with torch.cuda.stream(side):
-        qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0) if world < 2 else \
-            CrossTarget(None, D, ALPHA, LAM, rows=r1 - r0, Linv=Linv, check=status_check(qst))
+        if factors is None:
+            qep = CrossTarget(H, D, ALPHA, LAM, rows=r1 - r0)
+        else:
+            qep = CrossTarget(None, D, ALPHA, LAM, rows=r1 - r0, Linv=factors[1], check=status_check(factors[2]))
         for nm, rows in spec.matrices:
             a, b = max(r0, off), min(r1, off + rows)
             if a < b:
@@ -139,8 +152,7 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
                 ks.append(bits[nm][a - off:b - off])
                 spans[nm] = (a - off, b - off)
             off += rows
-    if world < 2:
-        env = Environment(rot.conj(H))
+    env = Environment(rot.conj(H)) if factors is None else factors[0]
     main.wait_stream(side)
     qep.record_stream(main)
     for t in Xs:
@@ -167,31 +179,78 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     return res
 
 
-def _factors_on_two_ranks(rot, H, rank: int, group):
-    """The stage's two factorizations on two ranks at once — Environment(R·H·Rᵀ) on rank 0, the QEP's inverse
-    Cholesky factor of H + λ·mean(diag H)·I on rank 1 — each queued before any collective, then broadcast to the
-    group (NVLink) with their status words. Returns (env, Linv, qep_status) on every rank."""
+def build_stages_sharded(stages, weights: dict, stats: list, bits: dict, layer: int = 0, group=None,
+                         dequantize: bool = True, tables=None, n_tok_total: int | None = None) -> dict:
+    """All stages of a layer over a group of 4 or more ranks, from their accumulated statistics: every stage's H and D
+    reduced first, then every stage's two factorizations queued at once on the rank pairs `factor_owners` assigns
+    (with 8 ranks each stage has its own pair), then stage by stage the factors are broadcast and each rank maps and
+    sweeps its rows. The factorizations of different stages overlap instead of adding up; the results equal
+    build_stage's. Returns {stage: StageResult} (this rank's rows)."""
+    world, rank = group.size(), group.rank()
+    HD = [_reduce_finalize(st, group, n_tok_total) for st in stats]
+    owners = factor_owners([s.d for s in stages], world)
+    dev = HD[0][0].device
+    rots = [Rotation(s.d, _in_seed(s, layer), dev) for s in stages]
+    bufs = [_own_factors(rots[i], HD[i][0], rank, *owners[i]) for i in range(len(stages))]
+    out = {}
+    for i, s in enumerate(stages):
+        factors = _share_factors(rots[i], HD[i][0], bufs[i], *owners[i], group)
+        out[s.name] = build_stage_from_statistics(s, weights, None, bits, layer, group, dequantize, tables,
+                                                  n_tok_total, HD=HD[i], factors=factors)
+    return out
+
+
+def _own_factors(rot, H, rank: int, env_rank: int, qep_rank: int):
+    """Queues this rank's share of a stage's two factorizations — Environment(R·H·Rᵀ) on `env_rank`, the QEP's inverse
+    Cholesky factor of H + λ·mean(diag H)·I on `qep_rank` — and returns the buffers the owners broadcast (empty ones to
+    receive into elsewhere): (Linv, qep_status, U, dead, env_status)."""
     n, dev = H.shape[0], H.device
     qst = torch.zeros(1, dtype=torch.int32, device=dev)
     est = torch.zeros(1, dtype=torch.int32, device=dev)
-    Hr = rot.conj(H)
-    if rank == 1:
+    if rank == qep_rank:
         Linv = cholesky_inverse_lower(ridge(H, LAM), deferred=True, status=qst)[0]
     else:
         Linv = torch.empty(n, n, dtype=torch.float64, device=dev)
-    if rank == 0:
-        env0 = Environment(Hr, status=est)
+    if rank == env_rank:
+        env0 = Environment(rot.conj(H), status=est)
         U, dead = env0.U, env0.dead.to(torch.uint8)
     else:
         U = torch.empty(n, n, dtype=torch.float64, device=dev)
         dead = torch.empty(n, dtype=torch.uint8, device=dev)
-    r0, r1 = torch.distributed.get_global_rank(group, 0), torch.distributed.get_global_rank(group, 1)
-    torch.distributed.broadcast(Linv, src=r1, group=group)
-    torch.distributed.broadcast(qst, src=r1, group=group)
-    torch.distributed.broadcast(U, src=r0, group=group)
-    torch.distributed.broadcast(dead, src=r0, group=group)
-    torch.distributed.broadcast(est, src=r0, group=group)
-    return Environment.from_factor(Hr, U, dead, est), Linv, qst
+    return Linv, qst, U, dead, est
+
+
+def _share_factors(rot, H, bufs, env_rank: int, qep_rank: int, group):
+    """Broadcasts a stage's factors from their owners (NVLink) and returns (env, Linv, qep_status) on every rank."""
+    Linv, qst, U, dead, est = bufs
+    src_q = torch.distributed.get_global_rank(group, qep_rank)
+    src_e = torch.distributed.get_global_rank(group, env_rank)
+    torch.distributed.broadcast(Linv, src=src_q, group=group)
+    torch.distributed.broadcast(qst, src=src_q, group=group)
+    torch.distributed.broadcast(U, src=src_e, group=group)
+    torch.distributed.broadcast(dead, src=src_e, group=group)
+    torch.distributed.broadcast(est, src=src_e, group=group)
+    return Environment.from_factor(lambda: rot.conj(H), U, dead, est), Linv, qst
+
+
+def _factors_on_two_ranks(rot, H, rank: int, group):
+    """The stage's two factorizations on two ranks at once — Environment(R·H·Rᵀ) on rank 0, the QEP's inverse
+    Cholesky factor of H + λ·mean(diag H)·I on rank 1 — each queued before any collective, then broadcast to the
+    group (NVLink) with their status words. Returns (env, Linv, qep_status) on every rank."""
+    return _share_factors(rot, H, _own_factors(rot, H, rank, 0, 1), 0, 1, group)
+
+
+def factor_owners(dims, world: int) -> list:
+    """(env_rank, qep_rank) per stage: the stages' factorizations spread over the group's rank pairs, the largest
+    first onto the least loaded pair (cost ∝ d³), so with 8 ranks each stage of a layer has its own pair."""
+    pairs = max(1, world // 2)
+    load = [0.0] * pairs
+    owners = [None] * len(dims)
+    for i in sorted(range(len(dims)), key=lambda i: -dims[i]):
+        p = min(range(pairs), key=lambda q: load[q])
+        load[p] += float(dims[i]) ** 3
+        owners[i] = (2 * p, 2 * p + 1) if world >= 2 else (0, 0)
+    return owners
 
 
 _COPY = {}

@@ -1,6 +1,7 @@
 """Worker of test_gpu_multi.py, launched by torch.distributed.run with one process per GPU: a small two-stage layer
-built with its tokens and rows sharded over the ranks (H and D all-reduced, the stage's two factorizations on two
-ranks and broadcast), every rank's states gathered to rank 0 and compared with the same layer built on one GPU."""
+built with its tokens and rows sharded over the ranks (H and D all-reduced; a stage's two factorizations on two ranks
+and broadcast — with 4 or more ranks, each stage on its own rank pair after every stage's statistics), every rank's
+states gathered to rank 0 and compared with the same layer built on one GPU."""
 
 import datetime
 import os
@@ -26,8 +27,19 @@ def main():
     tokens = 65536
     lo, hi = token_shard(tokens, rank, world)
     stages, weights, acts, w, bits = config3(tokens, device=dev, lo=lo, hi=hi, stages=spec)
-    out = build_layer(stages, weights, acts, w, bits, group=torch.distributed.group.WORLD, dequantize=False,
-                      n_tok_total=tokens)
+    group = torch.distributed.group.WORLD
+    if world >= 4:  # every stage's statistics first, the stages' factorizations on separate rank pairs
+        from lookatmyquant_b200.hessian import Statistics
+        from lookatmyquant_b200.layer import build_stages_sharded
+        stats = []
+        for s in stages:
+            x, xr = acts[s.name]
+            st = Statistics(s.d, cross=True, device=dev)
+            st.add(x, w, xr)
+            stats.append(st)
+        out = build_stages_sharded(stages, weights, stats, bits, group=group, dequantize=False, n_tok_total=tokens)
+    else:
+        out = build_layer(stages, weights, acts, w, bits, group=group, dequantize=False, n_tok_total=tokens)
     torch.cuda.synchronize()
     parts = [None] * world
     mine = {s.name: {nm: (out[s.name].row_range[nm], out[s.name].states[nm].cpu()) for nm in out[s.name].states}

@@ -1,6 +1,7 @@
-"""Multi-rank host logic on CPU (gloo, world size 2): token shards of the statistics sum to the whole (the fp32
+"""Multi-rank host logic on CPU (gloo, world sizes 2 and 4): token shards of the statistics sum to the whole (the fp32
 accumulators are what the layer build all-reduces), row shards cover every row once, and the padded all-gather of
-row shards reassembles the states."""
+row shards reassembles the states; the stages' factorizations are spread over rank pairs and every rank receives
+each stage's factors from its owners."""
 
 import os
 import socket
@@ -84,3 +85,54 @@ def test_two_gloo_ranks_reduce_and_gather():
     for rank, err, ok in out:
         assert err < 1e-5, (rank, err)
         assert ok, rank
+
+
+def test_factor_owners_spread_stages_over_pairs():
+    from lookatmyquant_b200.layer import factor_owners
+    dims = [2560, 4096, 2560, 9728]  # a Qwen3-4B-class layer's stages
+    assert factor_owners(dims, 2) == [(0, 1)] * 4
+    eight = factor_owners(dims, 8)
+    assert sorted(eight) == [(0, 1), (2, 3), (4, 5), (6, 7)]  # one pair per stage
+    assert eight[3] == (0, 1)  # the largest stage first
+    four = factor_owners(dims, 4)
+    assert four[3] == (0, 1) and all(o == (2, 3) for o in four[:3])  # 9728³ outweighs the other three together
+    for world in (2, 3, 4, 5, 8, 16):
+        assert all(0 <= e < world and 0 <= q < world and e != q for e, q in factor_owners(dims, world))
+
+
+def _share_worker(rank, world, port, q):
+    """Every stage's owners fill their factor buffers with marks; after _share_factors every rank holds them."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from lookatmyquant_b200.layer import _share_factors, factor_owners
+        dims = [8, 12, 8, 20]
+        owners = factor_owners(dims, world)
+        ok = True
+        for i, n in enumerate(dims):
+            e, qr = owners[i]
+            Linv = torch.full((n, n), 100.0 * i + qr if rank == qr else -1.0, dtype=torch.float64)
+            qst = torch.tensor([i if rank == qr else -1], dtype=torch.int32)
+            U = torch.full((n, n), 100.0 * i + e if rank == e else -1.0, dtype=torch.float64)
+            dead = torch.full((n,), 1 if rank == e else 7, dtype=torch.uint8)
+            est = torch.tensor([i + 50 if rank == e else -1], dtype=torch.int32)
+            env, L, qs = _share_factors(None, None, (Linv, qst, U, dead, est), e, qr, dist.group.WORLD)
+            ok &= bool((L == 100.0 * i + qr).all()) and int(qs[0]) == i
+            ok &= bool((env.U == 100.0 * i + e).all()) and bool(env.dead.all()) and int(est[0]) == i + 50
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_four_gloo_ranks_share_factors_from_their_owners():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_share_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok in out), out
