@@ -401,7 +401,7 @@ def sweep_roofline(kms, algo_bytes, edges, pk):
     sm_mhz = pk.get("sm_max_mhz", 1965.0)
     fp32_peak = SMS * FP32_LANES * sm_mhz * 1e6 / 1e12
     fp32_achieved = 3 * edges / (kms * 1e-3) / 1e12
-    return {"kernel": "sweep_rowtrellis_kernel", "bound": "hbm", "achieved": achieved_gbs, "peak": pk["hbm_gbs"],
+    return {"kernel": "sweep_run_kernel (fused row-trellis LDLQ sweep)", "bound": "hbm", "achieved": achieved_gbs, "peak": pk["hbm_gbs"],
             "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"], "traffic": None, "kernel_ms": kms,
             "peak_source": pk["source"],
             "alu": {"achieved": fp32_achieved, "peak": fp32_peak, "unit": "T fp32 lane-ops/s",
