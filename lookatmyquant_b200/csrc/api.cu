@@ -3,6 +3,9 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "lamq_common.cuh"
 
@@ -18,6 +21,19 @@ void set_error(const char *fmt, ...) {
     va_start(ap, fmt);
     vsnprintf(g_error, sizeof(g_error), fmt, ap);
     va_end(ap);
+}
+
+cudaError_t smem_limit_once(const void *kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;  // (kernel, device) pairs already raised
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kernel, dev})) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({kernel, dev});
+    return e;
 }
 
 }  // namespace lamq

@@ -519,10 +519,10 @@ int grid_for(int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, 148 * 1
 
 template <class T>
 int launch_dgemm(cudaStream_t s, const GemmArgs &g) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(dgemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T::kSmem);
-        attr = true;
+    const cudaError_t e = smem_limit_once((const void *)dgemm_kernel<T>, (int)T::kSmem);
+    if (e != cudaSuccess) {
+        set_error("dgemm: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
     }
     dim3 grid((g.N + T::BN - 1) / T::BN, (g.M + T::BM - 1) / T::BM);
     dgemm_kernel<T><<<grid, T::kThreads, T::kSmem, s>>>(g);
@@ -585,10 +585,10 @@ int chol_inv_rec(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx,
 }
 
 int chol_inv(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx, int n, double *W, int *status) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(diag_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLeafSmem);
-        attr = true;
+    const cudaError_t e = smem_limit_once((const void *)diag_block_kernel, (int)kLeafSmem);
+    if (e != cudaSuccess) {
+        set_error("cholesky leaf: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
     }
     int st = chol_inv_rec(s, A, lda, X, ldx, 0, n, W, status);
     if (st) return st;

@@ -11,6 +11,9 @@ namespace lamq {
 // Records the first CUDA error of the calling thread's last API call, for lamq_last_error().
 void set_error(const char *fmt, ...);
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device (thread-safe; defined in api.cu).
+cudaError_t smem_limit_once(const void *kernel, int bytes);
+
 // Counts one kernel launch of this library (lamq_kernel_launches()).
 void count_launch();
 
