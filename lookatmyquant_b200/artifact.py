@@ -200,12 +200,16 @@ class TrellisProduct:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         squeeze = x.ndim == 1
-        x = x.reshape(-1, self.n)
-        xr = self.rotate(x)
+        y = self.rotated(self.rotate(x.reshape(-1, self.n)))
+        return y[0] if squeeze else y
+
+    def rotated(self, xr: torch.Tensor) -> torch.Tensor:
+        """y = V[state]·S · xr for an input already rotated (R_in x, fp32, nvec × n): matrices that read the same
+        input through the same signs (a stage's q/k/v, gate/up) share one rotation."""
+        xr = xr.to(self.device, torch.float32).contiguous()
         nvec = xr.shape[0]
         if nvec >= DENSE_PRODUCT_VECTORS:
-            y = (xr.to(torch.bfloat16) @ self.dense_rotated().T).float()
-            return y[0] if squeeze else y
+            return (xr.to(torch.bfloat16) @ self.dense_rotated().T).float()
         y = torch.empty(nvec, self.m, dtype=torch.float32, device=self.device)
         lib = _lib.load()
         for g, codes, rows, scales, table in self.groups:
@@ -213,4 +217,4 @@ class TrellisProduct:
                 check(lib.lamq_trellis_product(ptr(codes), rows.numel(), self.n, g["bits"], g["state_bits"],
                                                ptr(scales), ptr(table), ptr(rows), ptr(xr), xr.stride(0), nvec,
                                                ptr(y), y.stride(0), stream_ptr(self.device)), "lamq_trellis_product")
-        return y[0] if squeeze else y
+        return y

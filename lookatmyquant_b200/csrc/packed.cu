@@ -84,67 +84,199 @@ __global__ void unpack_trellis_kernel(const uint32_t *__restrict__ codes, int64_
     }
 }
 
-// y[v][map[r]] = scale[r] · Σ_j table[state_rj] · x[v][j] for NV input vectors. A warp takes kRowsPerWarp rows at a
-// time and walks their columns 32 at a time (lane = column): each lane reads the one or two stream words that hold its
-// column's state (the warp's 32 columns share k + 1 words, which L1 serves), looks the value up in the table (shared
-// memory), and multiplies it into the NV vectors' sums; x values are reused across the rows.
-constexpr int kRowsPerWarp = 4;
+// y[v][map[r]] = scale[r] · Σ_j table[state_rj] · x[v][j] for NV input vectors. A CTA of 8 warps takes
+// kRowsPerCta rows at a time; warp w walks its share of the columns 32 at a time (lane = column): each lane reads the
+// one or two stream words that hold its column's state (the warp's 32 columns share k + 1 words, which L1 serves),
+// looks the value up in the table (shared memory) and multiplies it into the NV vectors' sums, each x value reused
+// across the rows. The warps' partial sums are added in a fixed order through shared memory, so the result is
+// deterministic. A persistent grid loads the table once per CTA.
+constexpr int kRowsPerCta = 4;
 constexpr int kProductWarps = 8;
+constexpr int kColumnBlocks = 4;
 
 template <int NV>
 __global__ void __launch_bounds__(kProductWarps * 32) trellis_product_kernel(
     const uint32_t *__restrict__ codes, int64_t rows, int n, int k, int L, const float *__restrict__ scales,
     const float *__restrict__ table, const uint32_t *__restrict__ map, const float *__restrict__ x, int64_t ldx,
     float *__restrict__ y, int64_t ldy) {
-    __shared__ float tab[4096];
+    __shared__ __align__(16) float tab[4096];
+    __shared__ float part[kProductWarps][kRowsPerCta][NV];
     const int nt = 1 << L;
-    for (int i = threadIdx.x; i < nt; i += blockDim.x) tab[i] = table[i];
+    if ((reinterpret_cast<uintptr_t>(table) & 15) == 0 && nt >= 4) {  // 16-byte loads, all in flight together
+#pragma unroll 4
+        for (int i = threadIdx.x; i < nt / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(tab)[i] = __ldg(reinterpret_cast<const float4 *>(table) + i);
+    } else {
+#pragma unroll 16
+        for (int i = threadIdx.x; i < nt; i += blockDim.x) tab[i] = __ldg(table + i);
+    }
     __syncthreads();
     const int N = (n + 31) / 32 * 32;
     const int wpr = N / 32 * k;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t groups = (rows + kRowsPerWarp - 1) / kRowsPerWarp;
-    for (int64_t g = (int64_t)blockIdx.x * kProductWarps + warp; g < groups; g += (int64_t)gridDim.x * kProductWarps) {
-        const int64_t r0 = g * kRowsPerWarp;
-        float acc[kRowsPerWarp][NV];
+    const int chunk = (N / 32 + kProductWarps - 1) / kProductWarps * 32;  // columns per warp, a multiple of 32
+    const int c0 = warp * chunk, c1 = min(n, c0 + chunk);
+    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
+        const int64_t r0 = g * kRowsPerCta;
+        float acc[kRowsPerCta][NV];
 #pragma unroll
-        for (int a = 0; a < kRowsPerWarp; ++a)
+        for (int a = 0; a < kRowsPerCta; ++a)
 #pragma unroll
             for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
-        for (int j0 = 0; j0 < n; j0 += 32) {
-            const int j = j0 + lane;
-            if (j < n) {
-                float val[kRowsPerWarp];
+        // kColumnBlocks blocks of 32 columns per step: their stream words are loaded together, so a warp waits on
+        // memory once per step rather than once per block
+        for (int j0 = c0; j0 < c1; j0 += 32 * kColumnBlocks) {
+            uint32_t st[kColumnBlocks][kRowsPerCta];
 #pragma unroll
-                for (int a = 0; a < kRowsPerWarp; ++a) {
+            for (int u = 0; u < kColumnBlocks; ++u) {
+                const int j = j0 + 32 * u + lane;
+#pragma unroll
+                for (int a = 0; a < kRowsPerCta; ++a) {
                     const int64_t r = min(r0 + a, rows - 1);
-                    val[a] = tab[stream_bits(codes + r * wpr, wpr, (int64_t)(N - 1 - j) * k, L)];
+                    st[u][a] = (j < c1) ? stream_bits(codes + r * wpr, wpr, (int64_t)(N - 1 - j) * k, L) : 0u;
                 }
+            }
 #pragma unroll
-                for (int v = 0; v < NV; ++v) {
-                    const float xv = __ldg(x + (int64_t)v * ldx + j);
+            for (int u = 0; u < kColumnBlocks; ++u) {
+                const int j = j0 + 32 * u + lane;
+                if (j < c1) {
+                    float val[kRowsPerCta];
 #pragma unroll
-                    for (int a = 0; a < kRowsPerWarp; ++a) acc[a][v] = fmaf(val[a], xv, acc[a][v]);
+                    for (int a = 0; a < kRowsPerCta; ++a) val[a] = tab[st[u][a]];
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        const float xv = __ldg(x + (int64_t)v * ldx + j);
+#pragma unroll
+                        for (int a = 0; a < kRowsPerCta; ++a) acc[a][v] = fmaf(val[a], xv, acc[a][v]);
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int a = 0; a < kRowsPerWarp; ++a) {
+        for (int a = 0; a < kRowsPerCta; ++a)
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
                 float s = acc[a][v];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                acc[a][v] = s;
+                if (lane == 0) part[warp][a][v] = s;
             }
+        __syncthreads();
+        for (int e = threadIdx.x; e < kRowsPerCta * NV; e += blockDim.x) {
+            const int a = e / NV, v = e % NV;
             const int64_t r = r0 + a;
-            if (lane == 0 && r < rows) {
-                const int64_t orow = map ? (int64_t)map[r] : r;
-                const float sc = scales[r];
+            if (r < rows) {
+                float s = 0.f;
 #pragma unroll
-                for (int v = 0; v < NV; ++v) y[(int64_t)v * ldy + orow] = acc[a][v] * sc;
+                for (int w = 0; w < kProductWarps; ++w) s += part[w][a][v];
+                const int64_t orow = map ? (int64_t)map[r] : r;
+                y[(int64_t)v * ldy + orow] = s * scales[r];
             }
         }
+        __syncthreads();  // part is rewritten by the next rows
+    }
+}
+
+// The product for symbol widths K = 1..4, a lane owning 8 consecutive columns: their 8 states lie within
+// 7K + L <= 40 bits of the row's stream, so three words loaded once give all 8 (two selects and a funnel shift each),
+// and the 8 input values arrive as two float4 loads per vector. A CTA of 8 warps takes kRowsPerCta rows at a time;
+// the warps take 256-column blocks in turn, and their partial sums are added in a fixed order through shared memory.
+template <int NV, int K>
+__global__ void __launch_bounds__(kProductWarps * 32) trellis_product8_kernel(
+    const uint32_t *__restrict__ codes, int64_t rows, int n, int L, const float *__restrict__ scales,
+    const float *__restrict__ table, const uint32_t *__restrict__ map, const float *__restrict__ x, int64_t ldx,
+    int xvec, float *__restrict__ y, int64_t ldy) {
+    __shared__ __align__(16) float tab[4096];
+    __shared__ float part[kProductWarps][kRowsPerCta][NV];
+    const int nt = 1 << L;
+    if ((reinterpret_cast<uintptr_t>(table) & 15) == 0 && nt >= 4) {
+#pragma unroll 4
+        for (int i = threadIdx.x; i < nt / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(tab)[i] = __ldg(reinterpret_cast<const float4 *>(table) + i);
+    } else {
+#pragma unroll 16
+        for (int i = threadIdx.x; i < nt; i += blockDim.x) tab[i] = __ldg(table + i);
+    }
+    __syncthreads();
+    const uint32_t smask = (1u << L) - 1u;
+    const int N = (n + 31) / 32 * 32;
+    const int wpr = N / 32 * K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nblk = (n + 255) / 256;
+    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
+        const int64_t r0 = g * kRowsPerCta;
+        float acc[kRowsPerCta][NV];
+#pragma unroll
+        for (int a = 0; a < kRowsPerCta; ++a)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
+        for (int blk = warp; blk < nblk; blk += kProductWarps) {
+            const int jb = blk * 256 + lane * 8;  // this lane's first column
+            if (jb >= n) continue;
+            // column jb + i has its state at bit (N − 1 − jb − i)·K, i.e. (7 − i)·K above that of column jb + 7
+            const int64_t bp = (int64_t)(N - 1 - (jb + 7)) * K;
+            const int64_t w0 = bp >> 5;
+            const int sh0 = (int)(bp & 31);
+            uint32_t wv[kRowsPerCta][3];
+#pragma unroll
+            for (int a = 0; a < kRowsPerCta; ++a) {
+                const uint32_t *row = codes + min(r0 + a, rows - 1) * wpr;
+#pragma unroll
+                for (int q = 0; q < 3; ++q) wv[a][q] = (w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
+            }
+            const bool full = xvec && jb + 8 <= n;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float xv[NV][4];
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    const float *xp = x + (int64_t)v * ldx + jb + 4 * h;
+                    if (full) {
+                        const float4 t = __ldg(reinterpret_cast<const float4 *>(xp));
+                        xv[v][0] = t.x; xv[v][1] = t.y; xv[v][2] = t.z; xv[v][3] = t.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) xv[v][i] = (jb + 4 * h + i < n) ? __ldg(xp + i) : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int shift = sh0 + (7 - (4 * h + i)) * K;  // < 32 + 7K + 1, inside the three words
+                    const bool up = shift >= 32;
+#pragma unroll
+                    for (int a = 0; a < kRowsPerCta; ++a) {
+                        const uint32_t lo = up ? wv[a][1] : wv[a][0], hi = up ? wv[a][2] : wv[a][1];
+                        const float val = tab[__funnelshift_r(lo, hi, shift & 31) & smask];
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) acc[a][v] = fmaf(val, xv[v][i], acc[a][v]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < kRowsPerCta; ++a)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                float s = acc[a][v];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (lane == 0) part[warp][a][v] = s;
+            }
+        __syncthreads();
+        for (int e = threadIdx.x; e < kRowsPerCta * NV; e += blockDim.x) {
+            const int a = e / NV, v = e % NV;
+            const int64_t r = r0 + a;
+            if (r < rows) {
+                float s = 0.f;
+#pragma unroll
+                for (int w = 0; w < kProductWarps; ++w) s += part[w][a][v];
+                const int64_t orow = map ? (int64_t)map[r] : r;
+                y[(int64_t)v * ldy + orow] = s * scales[r];
+            }
+        }
+        __syncthreads();  // part is rewritten by the next rows
     }
 }
 
@@ -155,10 +287,22 @@ int grid_for(int64_t work, int threads) {
 template <int NV>
 void launch_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales, const float *table,
                     const uint32_t *map, const float *x, int64_t ldx, float *y, int64_t ldy, cudaStream_t s) {
-    const int64_t groups = (rows + kRowsPerWarp - 1) / kRowsPerWarp;
-    const int grid = (int)std::min<int64_t>((groups + kProductWarps - 1) / kProductWarps, 148 * 8);
-    trellis_product_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, k, L, scales, table, map, x, ldx, y,
-                                                                   ldy);
+    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    const int grid = (int)std::min<int64_t>(groups, 148 * 6);
+    const int xvec = ((uintptr_t)x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
+    switch (k) {  // the widths of the trellis codes; wider symbols take the general kernel
+        case 1: trellis_product8_kernel<NV, 1><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
+                                                                                  x, ldx, xvec, y, ldy); break;
+        case 2: trellis_product8_kernel<NV, 2><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
+                                                                                  x, ldx, xvec, y, ldy); break;
+        case 3: trellis_product8_kernel<NV, 3><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
+                                                                                  x, ldx, xvec, y, ldy); break;
+        case 4: trellis_product8_kernel<NV, 4><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
+                                                                                  x, ldx, xvec, y, ldy); break;
+        default:
+            trellis_product_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, k, L, scales, table, map, x,
+                                                                           ldx, y, ldy);
+    }
 }
 
 }  // namespace

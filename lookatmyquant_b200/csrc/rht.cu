@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRhtThreads / 32;
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const double *src = p.in + row * p.ldi;
+#pragma unroll 8
         for (int e = threadIdx.x; e < n; e += kRhtThreads) sv[e] = p.pre ? src[e] * p.pre[e] : src[e];
         __syncthreads();
         // phase 1: Z[pr][q] = Σ_q' Be[q][q'] · V[pr][q'], a warp per row pr of V, lanes over q
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
         }
         __syncthreads();
         double *dst = p.out + row * p.ldo;
+#pragma unroll 8
         for (int e = threadIdx.x; e < n; e += kRhtThreads) {
             const double y = sv[e] * p.scale;
             dst[e] = p.post ? y * p.post[e] : y;
