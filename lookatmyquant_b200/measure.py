@@ -7,7 +7,8 @@ and option `word(option, W, H, seed, trellis)` (quantize.py:332-347: the column 
 960-wide model, two-sided rotation), the weight swapped in, `kl() − floor` recorded, the weight restored.
 
 Here: H from the tcgen05 statistics kernel (bf16 activations, as the reference's fp32 Xᵀ·X of the bf16 stream), the
-word from the column-trellis sweep kernel, the forward through the model's own bf16 layers, and the KL from the fused
+word from the column-trellis sweep kernel, the forward through the model's own bf16 layers — from the quantized
+piece's layer on, the earlier layers' outputs being kept from the reference pass (Probe) — and the KL from the fused
 LM-head/log-softmax/KL kernel (kl.KLReference) on the final hidden states — no logits are formed. The model is a
 random-initialised SmolLM2-360M-architecture Llama (weights N(0, 0.02²), bf16) and the windows are seeded Zipf tokens.
 """
@@ -97,22 +98,62 @@ def capture(model, layers, chunks) -> dict:
 
 
 class Probe:
-    """Held windows, their reference distribution (once) and the KL of the current model to it."""
+    """Held windows, their reference distribution (once) and the KL of the current model to it.
 
-    def __init__(self, model, held: torch.Tensor, batch: int = 2, weights: torch.Tensor | None = None):
+    A probe quantizes one piece of one decoder layer, so the layers before it see exactly the reference model: the
+    hidden state entering every layer (and the arguments the model passes to its layers) is kept from the reference
+    pass, and `kl(start=i)` runs only layers i, i + 1, … — the same modules on the same inputs, so the hidden states are
+    bit-identical to a full forward's, for about half the work on average (the reference re-runs the whole model)."""
+
+    def __init__(self, model, held: torch.Tensor, batch: int = 2, weights: torch.Tensor | None = None,
+                 prefix_cache: bool = True):
         self.model, self.held, self.batch = model, held, batch
         self.w = weights
+        self.cache = self._capture_prefix() if prefix_cache else None
         self.ref = KLReference(self.hidden(), model.lm_head.weight)
 
     @torch.no_grad()
-    def hidden(self) -> torch.Tensor:
+    def _capture_prefix(self) -> list:
+        """[(layer inputs, layer kwargs)] per batch of windows, from one pass of the unquantized model."""
         dev = self.model.lm_head.weight.device
-        hs = [self.model.model(self.held[b:b + self.batch].to(dev), use_cache=False).last_hidden_state
-              for b in range(0, len(self.held), self.batch)]
+        cache = []
+        for b in range(0, len(self.held), self.batch):
+            ins, kw, hooks = [], {}, []
+
+            def pre(m, args, kwargs):
+                ins.append(args[0] if args else kwargs["hidden_states"])
+                if not kw:
+                    kw.update({k: v for k, v in kwargs.items() if k != "hidden_states"})
+            for layer in self.model.model.layers:
+                hooks.append(layer.register_forward_pre_hook(pre, with_kwargs=True))
+            try:
+                self.model.model(self.held[b:b + self.batch].to(dev), use_cache=False)
+            finally:
+                for h in hooks:
+                    h.remove()
+            cache.append((ins, kw))
+        return cache
+
+    @torch.no_grad()
+    def hidden(self, start: int | None = None) -> torch.Tensor:
+        """The final hidden states of the held windows; with `start`, only layers start, start + 1, … are run, from
+        the cached input of layer `start` (the layers before it must be unchanged since the reference pass)."""
+        dev = self.model.lm_head.weight.device
+        if start is None or self.cache is None:
+            hs = [self.model.model(self.held[b:b + self.batch].to(dev), use_cache=False).last_hidden_state
+                  for b in range(0, len(self.held), self.batch)]
+        else:
+            layers = self.model.model.layers
+            hs = []
+            for ins, kw in self.cache:
+                h = ins[start]
+                for layer in layers[start:]:
+                    h = layer(h, **kw)
+                hs.append(self.model.model.norm(h))
         return torch.cat(hs).reshape(-1, hs[0].shape[-1])
 
-    def kl(self) -> float:
-        return self.ref.kl(self.hidden(), self.w)
+    def kl(self, start: int | None = None) -> float:
+        return self.ref.kl(self.hidden(start), self.w)
 
 
 def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, windows: int = 8, T: int = 2048,
@@ -157,7 +198,7 @@ def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, wind
                         ts = time.time()
                         word = codes.ldlq_words([W], Hs, trellis[(k, Tm)], [seed_])[0]
                         mod.weight.data = word.matrix().to(torch.bfloat16)
-                        d = probe.kl() - floor
+                        d = probe.kl(start=i) - floor
                         mod.weight.data = orig
                         dt = time.time() - ts
                         t_probe += dt

@@ -31,3 +31,19 @@ def test_probe_floor_and_one_option():
     assert res["probes"] == 7
     dkl = [r["dkl"] for r in res["records"]]
     assert all(d >= -1e-6 for d in dkl) and max(dkl) > 0
+
+
+def test_probe_from_a_cached_layer_input_equals_the_full_forward():
+    """The hidden states of a probe that starts at the quantized piece's layer (earlier layers' outputs kept from the
+    reference pass) are bit-identical to a full forward of the modified model."""
+    from lookatmyquant_b200 import measure
+    model = measure.build_model(layers=3)
+    held = measure.zipf_tokens(4, 64, model.config.vocab_size, 5)
+    probe = measure.Probe(model, held, batch=2)
+    assert probe.kl(start=0) == 0.0 and probe.kl(start=2) == 0.0
+    mod = model.model.layers[1].mlp.up_proj
+    orig = mod.weight.data.clone()
+    mod.weight.data = (orig.float() * 1.01).to(torch.bfloat16)
+    assert torch.equal(probe.hidden(start=1), probe.hidden())
+    assert probe.kl(start=1) == probe.kl() and probe.kl() > 0
+    mod.weight.data = orig
