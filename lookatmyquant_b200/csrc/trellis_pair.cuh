@@ -4,9 +4,9 @@
 //   cost_t[s] = best_t[s >> k] + (x_t − C[s])²,   best_t[r] = min_{h < 2^k} cost_{t−1}[h·R + r]   (smallest h on ties)
 // Thread p (0..63) of the pair owns RT = R/64 consecutive r and keeps the 64 table values C[h·R + r] of its
 // predecessors in registers as fp32 pairs (half the registers of one warp per row, so twice the warps fit on an SM).
-// (x − C)² and its add to the best predecessor cost are computed two states at a time with sub/mul/add.rn.f32x2
-// (states r and r + 1 share their predecessors): every value is rounded exactly as the reference's scalar fp32 sub, mul
-// and add (explicit rounding, never fused). The minimum over the 2^k predecessors is a knock-out tournament (for
+// (x − C) and its add to the best predecessor cost are computed two states at a time with sub/add.rn.f32x2 (states r
+// and r + 1 share their predecessors), the square with two scalar mul.rn: every value is rounded exactly as the
+// reference's scalar fp32 sub, mul and add (never fused). The minimum over the 2^k predecessors is a knock-out tournament (for
 // k >= 3 two states at a time on packed differences) whose decisions are the sign bits of fp32 differences (the fp32
 // pipe, not the half-rate compare/select pipe); the winner's k index bits are assembled from them by bit selects and
 // appended to one back-pointer word per thread per step, so the traceback reads each step's choice with one shift. The pair exchanges the R best values through shared memory
@@ -58,22 +58,28 @@ __device__ __forceinline__ u64 sub2(u64 a, u64 b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
-__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
-    u64 r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
 __device__ __forceinline__ u64 add2(u64 a, u64 b) {
     u64 r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 
+// (d_lo², d_hi²), each square rounded by itself with the scalar multiply (mul.rn.f32, which is never contracted).
+// A packed multiply — and a packed fma with a −0 addend — was fused with the add that follows into one rounding,
+// which moved rare near-ties away from the reference's separately rounded fp32 cost (found by comparing a full table
+// fit against the one-warp kernel, whose intrinsics the reference's paths match).
+__device__ __forceinline__ u64 sq2(u64 d) {
+    float lo, hi;
+    upk2(d, lo, hi);
+    return pk2(__fmul_rn(lo, lo), __fmul_rn(hi, hi));
+}
+
 __device__ __forceinline__ void pair_sync(int bar) { asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory"); }
 
-// cv[h][j] = (C[h·R + p·RT + 2j], C[h·R + p·RT + 2j + 1]) as fp32 (rounded from the fp64 table like values.float()).
-template <int K>
-__device__ __forceinline__ void load_pair_values(const double *__restrict__ table, int p,
+// cv[h][j] = (C[h·R + p·RT + 2j], C[h·R + p·RT + 2j + 1]) as fp32 (from an fp32 table, or rounded from the fp64 one
+// like values.float()).
+template <int K, typename TT>
+__device__ __forceinline__ void load_pair_values(const TT *__restrict__ table, int p,
                                                  u64 (&cv)[PairTrellis<K>::NB][PairTrellis<K>::RT / 2]) {
     using T = PairTrellis<K>;
 #pragma unroll
@@ -212,7 +218,7 @@ __device__ __forceinline__ void acs_pair(const float *__restrict__ bin, float *_
 #pragma unroll
             for (int h = 0; h < T::NB; ++h) {
                 const u64 d = sub2(xx, cv[h][ii >> 1]);  // (x − C) for r = ii and ii + 1
-                c2[h] = add2(bb[h][(CH == 4) ? (i >> K) : 0], mul2(d, d));  // best + (x − C)²
+                c2[h] = add2(bb[h][(CH == 4) ? (i >> K) : 0], sq2(d));  // best + (x − C)²
             }
             if constexpr (kPairedTournament<K>) {
                 upk2(tournament2<K>(c2, words[0]), nb4[i & 3], nb4[(i & 3) + 1]);
@@ -253,7 +259,7 @@ __device__ __forceinline__ int final_argmin_pair(const float *__restrict__ best,
         for (int i = 0; i < T::RT; i += 2) {
             const float b = best[pslot<K>(h * (T::R >> K) + ((p * T::RT + i) >> K))];
             const u64 d = sub2(xx, cv[h][i >> 1]);
-            const u64 c = add2(pk2(b, b), mul2(d, d));
+            const u64 c = add2(pk2(b, b), sq2(d));
             float lo, hi;
             upk2(c, lo, hi);
             const int s = h * T::R + p * T::RT + i;  // states visited in increasing order

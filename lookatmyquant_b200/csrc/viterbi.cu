@@ -2,10 +2,14 @@
 //
 // Used for whole-row decodes (RowTrellisCode.apply without a sweep, codes.py:406-410), the column runs of
 // TrellisCode.project (codes.py:375-378) and the kernel-level parity tests. Sequences of up to 32 entries keep their
-// back-pointers in shared memory; longer ones keep them in the caller's workspace (256 bytes per entry per row).
+// back-pointers in shared memory; longer ones (the column runs: 256 or 320 entries, and only tens to hundreds of
+// them per block) are decoded by a warp pair each (trellis_pair.cuh: half the states per thread, one back-pointer
+// word per thread per step, all of them in shared memory), two sequences per CTA, unless their back-pointers do not
+// fit; then one warp per sequence keeps them in the caller's workspace (256 bytes per entry per row).
 #include <mutex>
 
 #include "lamq_common.cuh"
+#include "trellis_pair.cuh"
 #include "trellis_warp.cuh"
 
 namespace lamq {
@@ -78,6 +82,96 @@ __global__ void __launch_bounds__(kVitWarps * 32, 1) viterbi_kernel(VitParams p,
     }
 }
 
+// A long sequence decoded by a warp pair (64 threads, pt = the thread's index in the pair): x, the two best buffers,
+// every step's back-pointer words and the final reduction's scratch live in the pair's share of shared memory.
+template <int K>
+__device__ void viterbi_pair_long(const VitParams &p, int64_t row, int pair, int pt, unsigned char *base) {
+    using Tr = PairTrellis<K>;
+    const int T = p.T;
+    float *xs = reinterpret_cast<float *>(base);
+    float *best0 = xs + (T + 3) / 4 * 4;
+    float *best1 = best0 + Tr::R;
+    uint32_t *args = reinterpret_cast<uint32_t *>(best1 + Tr::R);
+    float *red = reinterpret_cast<float *>(args + (int64_t)T * 64);
+    const int bar = 1 + pair;
+    u64 cv[Tr::NB][Tr::RT / 2];
+    load_pair_values<K>(p.values, pt, cv);
+    for (int t = pt; t < T; t += 64) xs[t] = __ldg(p.X + row * (int64_t)T + t);
+    const bool has_start = p.start != nullptr;
+    const int start = has_start ? (int)(p.start[row] & (kStates - 1)) : 0;
+    init_best_pair<K>(best0, pt, has_start, start);
+    pair_sync(bar);
+    float *bin = best0, *bout = best1;
+    for (int t = 1; t < T; ++t) {
+        uint32_t words[Tr::WORDS];
+        acs_pair<K>(bin, bout, xs[t - 1], pt, cv, words);
+        args[(int64_t)t * 64 + pt] = words[0];
+        pair_sync(bar);
+        float *tmp = bin;
+        bin = bout;
+        bout = tmp;
+    }
+    const int fs = final_argmin_pair<K>(bin, xs[T - 1], pt, bar, cv, red);
+    if (pt >= 32) return;  // the first warp walks the path (broadcast reads), lane 0 writes it
+    int64_t *out = p.states + row * (int64_t)T;
+    int s = fs;
+    if (pt == 0) out[T - 1] = s;
+    for (int t = T - 1; t > 0; --t) {
+        const int r = s >> K;
+        s = decode_choice<K>(args + (int64_t)t * 64, r) * Tr::R + r;
+        if (pt == 0) out[t - 1] = s;
+    }
+}
+
+// Shared memory of one pair: x (padded to 16 bytes), two best buffers of R floats, T x 64 back-pointer words, 4 words.
+size_t pair_long_bytes(int T, int k) {
+    const size_t R = (size_t)1 << (kL - k);
+    const size_t b = (size_t)(T + 3) / 4 * 16 + 2 * R * sizeof(float) + (size_t)T * 64 * sizeof(uint32_t) + 16;
+    return (b + 15) / 16 * 16;
+}
+
+__global__ void __launch_bounds__(128) viterbi_pair_long_kernel(VitParams p, int k, int64_t pair_bytes) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, pair = warp >> 1, pt = (warp & 1) * 32 + (threadIdx.x & 31);
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 64) + pair;
+    if (row >= p.rows) return;  // both warps of the pair leave together: no barrier of this pair is pending
+    unsigned char *base = smem + pair * pair_bytes;
+    switch (k) {
+        case 1: viterbi_pair_long<1>(p, row, pair, pt, base); break;
+        case 2: viterbi_pair_long<2>(p, row, pair, pt, base); break;
+        case 3: viterbi_pair_long<3>(p, row, pair, pt, base); break;
+        default: viterbi_pair_long<4>(p, row, pair, pt, base); break;
+    }
+}
+
+// Launches the pair decoder when a pair's shared memory fits (two pairs per CTA when both fit); returns false
+// otherwise, leaving the call to the one-warp kernel.
+bool launch_pair_long(const VitParams &p, int k, cudaStream_t stream, int *rc) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const size_t pb = pair_long_bytes(p.T, k);
+    const int pairs = 2 * pb <= (size_t)optin ? 2 : (pb <= (size_t)optin ? 1 : 0);
+    if (pairs == 0) return false;
+    const size_t smem = pairs * pb;
+    *rc = LAMQ_OK;
+    const cudaError_t e = smem_limit_once((const void *)viterbi_pair_long_kernel, optin);
+    if (e != cudaSuccess) {
+        set_error("lamq_viterbi: %s", cudaGetErrorString(e));
+        *rc = LAMQ_ERR_CUDA;
+        return true;
+    }
+    const int64_t grid = (p.rows + pairs - 1) / pairs;
+    viterbi_pair_long_kernel<<<(unsigned)grid, 64 * pairs, smem, stream>>>(p, k, (int64_t)pb);
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+        set_error("lamq_viterbi: %s", cudaGetErrorString(le));
+        *rc = LAMQ_ERR_CUDA;
+    }
+    count_launch();
+    return true;
+}
+
 }  // namespace
 
 }  // namespace lamq
@@ -104,6 +198,10 @@ extern "C" int lamq_viterbi(const float *X, int64_t rows, int T, const float *va
                  "lamq_viterbi: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     VitParams p{X, rows, T, values, start, states,
                 need ? reinterpret_cast<unsigned long long *>(workspace) : nullptr};
+    if (T > kShortT) {
+        int rc = LAMQ_OK;
+        if (launch_pair_long(p, k, (cudaStream_t)stream, &rc)) return rc;
+    }
     const size_t per_warp = 2 * 2048 * sizeof(float) + (need ? 0 : (size_t)kShortT * 32 * 8);
     const size_t smem = kVitWarps * per_warp;
     cudaError_t e = cudaFuncSetAttribute(viterbi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
