@@ -68,7 +68,9 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=["artifact", "fit"], help="write only this fixture (the others stay as committed)")
+    ap.add_argument("--only", choices=["artifact", "fit", "neartie"],
+                    help="write only this fixture (the others stay as committed)")
+    ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
     C = setup_reference(args.reference.resolve())
     import torch
@@ -81,6 +83,9 @@ def main():
         return
     if args.only == "fit":
         write_fit_fixture(C, torch)
+        return
+    if args.only == "neartie":
+        write_neartie_fixture(C, torch, args.case)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -202,6 +207,18 @@ def main():
     write_artifact_fixture(C, Q, CA, torch)
     write_fit_fixture(C, torch)
     print("golden vectors written to", HERE)
+
+
+def write_neartie_fixture(C, torch, case: Path):
+    """9. A Viterbi near-tie (codes.py:151-181): one 256-step sequence whose best path, in the reference's separately
+    rounded fp32 costs, beats another by one ulp at the end — a fused multiply-add in the branch cost picks the other
+    one. The input (`case`) is row 131 of batch 1977 of the k = 2, T = 256 e-means table fit (codes.py:187-220) with
+    the table of that batch: the fit replayed on a GPU, where a decoder with fused costs first departed from the
+    reference's paths. The expected states are the reference's own viterbi of it."""
+    d = np.load(case)
+    X, v, k = np.asarray(d["X"], dtype=np.float64).reshape(1, -1), np.asarray(d["values"], dtype=np.float64), int(d["k"])
+    states = C.viterbi(torch.as_tensor(X), torch.as_tensor(v), 12, k).numpy()
+    np.savez_compressed(HERE / "viterbi_neartie.npz", X=X, values=v, k=np.int64(k), states=states)
 
 
 def write_fit_fixture(C, torch):

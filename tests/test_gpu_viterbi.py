@@ -54,3 +54,11 @@ def test_ties_break_like_torch():
 
 def test_empty():
     assert gpu_viterbi(np.zeros((0, 24)), table(2), 12, 2).shape == (0, 24)
+
+
+def test_near_tie_matches_reference(golden):
+    """A 256-step sequence whose best path beats another by one fp32 ulp in the reference's separately rounded costs
+    (tests/golden/viterbi_neartie.npz, states from the reference's own viterbi): a decoder whose branch cost fuses the
+    square into the add picks the other path."""
+    g = golden("viterbi_neartie")
+    assert np.array_equal(gpu_viterbi(g["X"], g["values"], 12, int(g["k"])), g["states"])

@@ -146,3 +146,10 @@ def test_packed_artifact_matches_reference(golden):
     import torch
     u = torch.rand(200, generator=torch.Generator().manual_seed(int(g["in_seed"])), dtype=torch.float64).numpy()
     assert np.array_equal(g["signs"], np.where(u < .5, -1, 1).astype(np.int8))
+
+
+def test_oracle_viterbi_near_tie(golden):
+    """The near-tie sequence of tests/golden/viterbi_neartie.npz: the oracle's separately rounded fp32 costs choose the
+    reference's path."""
+    g = golden("viterbi_neartie")
+    assert np.array_equal(O.viterbi(g["X"], g["values"], 12, int(g["k"])), g["states"])
