@@ -85,6 +85,18 @@ int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const float *value
                          const int64_t *start, int64_t *states, lamq_stream_t stream);
 
 /*
+ * Scalar-level LDLQ rounding in fp64 (opgraph/ldlq_gpu.py:29-49, `ldlq_round`; used by nested.py:117-119): X (rows x n,
+ * in place, the inputs after each block receive the block's errors) is rounded input by input to the nearest of the
+ * sorted `levels` (the bucketize of ldlq_gpu.py:35-41: ties to the lower level), each error e = (x − q) / U[j][j]
+ * carried into the block's later inputs through U's row, and after each block of `block` (<= 128) inputs into the rest
+ * through one product. Q (rows x n) receives the chosen levels. Workspace: lamq_ldlq_round_workspace_size(rows).
+ */
+size_t lamq_ldlq_round_workspace_size(int64_t rows);
+int lamq_ldlq_round(double *X, int64_t ldX, int64_t rows, int n, const double *U, int64_t ldU, const double *levels,
+                    int nlevels, int block, double *Q, int64_t ldQ, void *workspace, size_t workspace_bytes,
+                    lamq_stream_t stream);
+
+/*
  * The block-LDLQ sweep with a row trellis as its projection (opgraph/syntax.py:86-124 with codes.py:397-404,442-450):
  * the lm2 build's per-matrix hot loop, fused into one persistent kernel: tiles of 16 rows of one width per CTA, the
  * trellis decode per warp, the end-of-run refit on fp64 tensor cores.

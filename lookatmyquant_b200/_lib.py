@@ -28,6 +28,8 @@ SIGNATURES = {
     "lamq_viterbi_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "lamq_viterbi": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "lamq_viterbi_noalloc": (_I32, [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P]),
+    "lamq_ldlq_round_workspace_size": (_SZ, [_I64]),
+    "lamq_ldlq_round": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _I32, _I32, _P, _I64, _P, _SZ, _P]),
     "lamq_xtx_accumulate": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _I64, _I64, _P, _P]),
     "lamq_xtx_accumulate_scaled": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _c.c_float, _P, _I64, _I64, _P, _P]),
     "lamq_gather_rows": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P]),

@@ -286,6 +286,48 @@ def trellis_states(values, table) -> np.ndarray:
     return order[pos].astype(np.int16)
 
 
+# ----------------------------------------------------------------------------- scalar-level LDLQ (ldlq_gpu.py:15-49)
+
+
+def ldlq_factor(Hr, damp: float = 0.01) -> np.ndarray:
+    """`opgraph.ldlq_gpu.ldlq_factor` (ldlq_gpu.py:15-26): H symmetrized; damping d·mean(diag H)·I for d = damp,
+    10·damp, 100·damp until it factors; the upper Cholesky factor U of its inverse (Uᵀ·U = H⁻¹)."""
+    H = np.asarray(Hr, dtype=np.float64)
+    H = 0.5 * (H + H.T)
+    mean = float(np.mean(np.diag(H)))
+    for d in (damp, 10 * damp, 100 * damp):
+        try:
+            L = np.linalg.cholesky(H + d * mean * np.eye(len(H)))
+        except np.linalg.LinAlgError:
+            continue
+        Li = np.linalg.inv(L)
+        return np.linalg.cholesky(Li.T @ Li).T
+    raise AssertionError("H is not positive definite even with damping")
+
+
+def ldlq_round(X, U, levels, block: int = 128) -> np.ndarray:
+    """`opgraph.ldlq_gpu.ldlq_round` (ldlq_gpu.py:29-49): every entry to a level, inputs in order within blocks of
+    `block`, q = levels[number of midpoints below x], e = (x − q) / U[j][j] carried into the block's later inputs
+    through U's row, then into the inputs after the block through one product."""
+    X = np.array(X, dtype=np.float64)
+    U = np.asarray(U, dtype=np.float64)
+    lv = np.asarray(levels, dtype=np.float64)
+    mids = (lv[1:] + lv[:-1]) / 2
+    Q = np.empty_like(X)
+    n = X.shape[1]
+    for a in range(0, n, block):
+        b = min(a + block, n)
+        Err = np.empty((X.shape[0], b - a))
+        for j in range(a, b):
+            q = lv[np.searchsorted(mids, X[:, j], side="left")]
+            Q[:, j] = q
+            e = (X[:, j] - q) / U[j, j]
+            X[:, j + 1:b] -= e[:, None] * U[j, j + 1:b][None, :]
+            Err[:, j - a] = e
+        X[:, b:] -= Err @ U[a:b, b:]
+    return Q
+
+
 # ----------------------------------------------------------------------------- statistics (quantize.py:1457-1470, 1330-1335)
 
 

@@ -68,7 +68,7 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=["artifact", "fit", "neartie"],
+    ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -86,6 +86,9 @@ def main():
         return
     if args.only == "neartie":
         write_neartie_fixture(C, torch, args.case)
+        return
+    if args.only == "ldlq_gpu":
+        write_ldlq_gpu_fixture(torch, Environment)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -207,6 +210,46 @@ def main():
     write_artifact_fixture(C, Q, CA, torch)
     write_fit_fixture(C, torch)
     print("golden vectors written to", HERE)
+
+
+def write_ldlq_gpu_fixture(torch, Environment):
+    """10. Scalar-level LDLQ (opgraph/ldlq_gpu.py, the rounding of nested.py:117-119) and the generic sweep
+    (opgraph/syntax.py:86-124) with a Python projection, by the reference on seeded inputs: ldlq_factor of a
+    lognormally scaled H (and of one needing more damping), ldlq_round to 8 and 16 levels with blocks of 128 and 48
+    over 192 inputs, and syntax.sweep with a nearest-level projection at width 1 and 4 with a dead input."""
+    from opgraph import syntax
+    from opgraph.ldlq_gpu import ldlq_factor, ldlq_round
+    g = torch.Generator().manual_seed(11)
+    n, rows = 192, 70
+    A = torch.randn(2 * n, n, generator=g, dtype=torch.float64) * torch.exp(torch.randn(n, generator=g,
+                                                                                       dtype=torch.float64))
+    H = A.T @ A / (2 * n)
+    X = torch.randn(rows, n, generator=g, dtype=torch.float64)
+    out = {"H": H.numpy(), "X": X.numpy()}
+    U = ldlq_factor(H)
+    out["U"] = U.numpy()
+    for nl, block in ((8, 128), (16, 48)):
+        lv = torch.sort(torch.randn(nl, generator=g, dtype=torch.float64) * 1.2).values
+        out[f"levels{nl}"] = lv.numpy()
+        out[f"Q{nl}_b{block}"] = ldlq_round(X, U, lv, block=block).numpy()
+    # an H that needs more than the first damping: one eigenvalue pushed far below zero
+    ev, V = torch.linalg.eigh(H[:64, :64])
+    ev[0] = -0.05 * ev.mean()
+    Hbad = (V * ev) @ V.T
+    out["Hbad"], out["Ubad"] = Hbad.numpy(), ldlq_factor(Hbad).numpy()
+    # the generic sweep with a nearest-level projection, a dead input
+    Hd = H.clone()  # input 5 is dead: its row and column of H are zero
+    Hd[5, :] = 0
+    Hd[:, 5] = 0
+    env = Environment(Hd)
+    lv = torch.as_tensor(out["levels8"])
+    mids = (lv[1:] + lv[:-1]) / 2
+
+    def nearest(j, cols, T):
+        return lv[torch.bucketize(cols.contiguous(), mids)]
+    out["sweep_w1"] = syntax.sweep(X, env, nearest, width=1, lazy=64).numpy()
+    out["sweep_w4"] = syntax.sweep(X, env, nearest, width=4, lazy=64).numpy()
+    np.savez_compressed(HERE / "ldlq_gpu.npz", **out)
 
 
 def write_neartie_fixture(C, torch, case: Path):

@@ -1,6 +1,7 @@
-"""Host logic that needs no GPU: table lookup and caching."""
+"""Host logic that needs no GPU: table lookup and caching, the generic sweep's steps on host tensors."""
 
 import numpy as np
+import pytest
 import torch
 
 
@@ -37,3 +38,32 @@ def test_shipped_tables_match_their_sums():
     for name, h in sums.items():
         assert hashlib.sha256((codes.TABLES / name).read_bytes()).hexdigest() == h
         assert np.fromfile(codes.TABLES / name, dtype="<f8").shape == (4096,)
+
+
+class _Env:
+    """The two attributes the sweep reads from an environment."""
+
+    def __init__(self, U, dead):
+        self.U, self.dead = U, dead
+
+
+@pytest.mark.parametrize("width", [1, 4])
+def test_generic_sweep_matches_reference_on_cpu(golden, width):
+    """syntax.sweep (syntax.py:86-124) with a Python nearest-level projection, on the host, against the reference's
+    own sweep of the same inputs (the environment's U from the oracle, itself pinned to the reference's)."""
+    from lookatmyquant_b200 import syntax
+    from oracle import core as O
+    g = golden("ldlq_gpu")
+    Hd = g["H"].copy()
+    Hd[5, :] = 0
+    Hd[:, 5] = 0
+    U, dead, _ = O.environment(Hd)
+    lv = torch.as_tensor(g["levels8"])
+    mids = (lv[1:] + lv[:-1]) / 2
+
+    def nearest(j, cols, T):
+        return lv[torch.bucketize(cols.contiguous(), mids)]
+    got = syntax.sweep(torch.as_tensor(g["X"]), _Env(torch.as_tensor(U), torch.as_tensor(dead)), nearest, width=width,
+                       lazy=64).numpy()
+    ref = g[f"sweep_w{width}"]
+    assert np.abs(got - ref).max() <= 1e-10 * np.abs(ref).max()

@@ -153,3 +153,12 @@ def test_oracle_viterbi_near_tie(golden):
     reference's path."""
     g = golden("viterbi_neartie")
     assert np.array_equal(O.viterbi(g["X"], g["values"], 12, int(g["k"])), g["states"])
+
+
+def test_oracle_scalar_ldlq_matches_reference(golden):
+    """ldlq_gpu.ldlq_factor / ldlq_round (ldlq_gpu.py:15-49) restated, against the reference's own outputs."""
+    g = golden("ldlq_gpu")
+    assert np.abs(O.ldlq_factor(g["H"]) - g["U"]).max() <= 1e-12 * np.abs(g["U"]).max()
+    assert np.abs(O.ldlq_factor(g["Hbad"]) - g["Ubad"]).max() <= 1e-12 * np.abs(g["Ubad"]).max()
+    for nl, block in ((8, 128), (16, 48)):
+        assert np.array_equal(O.ldlq_round(g["X"], g["U"], g[f"levels{nl}"], block), g[f"Q{nl}_b{block}"])
