@@ -231,6 +231,20 @@ class TrellisCode:
         return Q.reshape(o // self.T, w, self.T).permute(0, 2, 1).reshape(o, w)
 
 
+class _Domain:
+    """What a Net core records of its code (frame.py's domain): the value table and whether sequences start at 0."""
+
+    def __init__(self, levels, fixed_start):
+        self.levels, self.fixed_start = levels, fixed_start
+
+
+class _Core:
+    """A Net core's tensor (`.data`) and, for the code core, its domain."""
+
+    def __init__(self, data, domain=None):
+        self.data, self.domain = data, domain
+
+
 class TrellisWord:
     """One matrix's trellis word: W ≈ R_outᵀ·diag(S)·V[states]·R_in. The fields are device tensors:
     `states` (rows × n int16), `scales` S (rows fp64), `settled` V[states] (fp64, units of S); the rotations are
@@ -249,6 +263,17 @@ class TrellisWord:
         if self.R_out is not None:
             W = self.R_out.rows_t(W.T.contiguous()).T.contiguous()
         return W.to(device=device or W.device, dtype=dtype)
+
+    @property
+    def cores(self) -> dict:
+        """The reference Net's cores that its callers read (quantize.py:513-527, :1541-1552): "W" (the settled table
+        values, with the code's `domain.levels` and `domain.fixed_start`), "W.S" (the row scales), and "I[u]" (the
+        output signs) when the word has an output rotation."""
+        levels = self.values.double().cpu() if hasattr(self.values, "double") else self.values
+        out = {"W": _Core(self.settled, _Domain(levels, self.fixed_start)), "W.S": _Core(self.scales[:, None])}
+        if self.R_out is not None:
+            out["I[u]"] = _Core(getattr(self.R_out, "signs", None))
+        return out
 
     def rate_bits(self) -> float:
         """Stored bits (frame.py:137-147): k per entry, plus L − k per sequence without a fixed start, 16 per row

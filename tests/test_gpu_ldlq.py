@@ -128,3 +128,26 @@ def test_config1_shape_against_oracle():
     E = Wq - W.numpy()
     proxy = float(np.sum((E @ H.numpy()) * E))
     assert abs(proxy - ref["proxy"]) <= 0.005 * ref["proxy"]
+
+
+def test_word_cores_give_the_states_as_the_reference_saves_them():
+    """quantize.word for a trellis program returns a Net-like word whose cores are what quantize.py reads to save codes
+    (trellis_code_entry, quantize.py:513-527): the states recovered from cores["W"] by table lookup are the word's."""
+    from lookatmyquant_b200 import codes
+    from lookatmyquant_b200.quantize import word
+    g = torch.Generator().manual_seed(2)
+    W = 0.02 * torch.randn(64, 256, generator=g, dtype=torch.float64)
+    A = torch.randn(1024, 256, generator=g, dtype=torch.float64)
+    H = A.T @ A / 1024
+    w = word("tr2", W.cuda(), H.cuda(), 7, {2: codes.RowTrellisCode(12, 2)}, in_seed=301, out_rot=False)
+    core = w.cores["W"]
+    table = torch.as_tensor(core.domain.levels, dtype=torch.float64)
+    assert len(table) == 4096 and core.domain.fixed_start and "I[u]" not in w.cores
+    v = core.data.double().cpu()
+    st, order = table.sort()
+    pos = torch.searchsorted(st, v.contiguous()).clamp(1, len(st) - 1)
+    pos = torch.where((v - st[pos - 1]).abs() <= (st[pos] - v).abs(), pos - 1, pos)
+    # tables can hold equal values; compare the values the states stand for
+    assert torch.equal(table[order[pos]], table[w.states.long().cpu()])
+    assert w.cores["W.S"].data.flatten().shape == (64,)
+    assert w.matrix().shape == W.shape and w.rate_bits() > 0

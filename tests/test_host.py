@@ -67,3 +67,18 @@ def test_generic_sweep_matches_reference_on_cpu(golden, width):
                        lazy=64).numpy()
     ref = g[f"sweep_w{width}"]
     assert np.abs(got - ref).max() <= 1e-10 * np.abs(ref).max()
+
+
+def test_program_names_parse_like_reference():
+    from lookatmyquant_b200.quantize import Dense, parse, word
+    assert parse("tr2") == ("tr", 2, False) and parse("tr3x") == ("tr", 3, True)
+    assert parse("fp16") == ("fp", 16, False) and parse("gptaq4") == ("gptaq", 4, True)
+    for bad in ("tr", "rtn2x", "q4", "orig"):
+        with pytest.raises(ValueError, match="unknown program"):
+            parse(bad)
+    W = torch.randn(4, 8, dtype=torch.float64)
+    d = word("fp16", W, None, 0, {})
+    assert isinstance(d, Dense) and d.rate_bits() == 16 * 32
+    assert torch.equal(d.matrix(), W.to(torch.bfloat16).double())
+    with pytest.raises(NotImplementedError):
+        word("rtn4", W, None, 0, {})
