@@ -1,4 +1,5 @@
-// Standalone Viterbi over the 12-bit bitshift trellis: opgraph/codes.py:151-181 (`viterbi`), a warp (or a warp pair) per row.
+// Standalone Viterbi over the 12-bit bitshift trellis: opgraph/codes.py:151-181 (`viterbi`), a warp (or a warp pair)
+// per row.
 //
 // Used for whole-row decodes (RowTrellisCode.apply without a sweep, codes.py:406-410), the column runs of
 // TrellisCode.project (codes.py:375-378) and the kernel-level parity tests. Sequences of up to 32 entries keep their
