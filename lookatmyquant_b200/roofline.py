@@ -278,10 +278,10 @@ def run(device="cuda", log=print, only=None) -> list:
                     code_bytes + 4.0 * weights, "GB/s", hbm, "codes read, fp32 weights written", "hbm"))
 
     if want("a15"):
-        st = trellis_paths(9728, 2560, 2, dev, 11)
+        st = trellis_paths(9728, 2560, 2, dev, 11).to(torch.int16)
         ms = timer(lambda: pack_trellis(st, 2))
         add(_record("a15", "pack_trellis_kernel (path check + k-bit reversed stream)", "9728 x 2560, k = 2", ms,
-                    8.0 * st.numel() + st.numel() * 2 / 8, "GB/s", hbm, "int64 states read, codes written", "hbm"))
+                    2.0 * st.numel() + st.numel() * 2 / 8, "GB/s", hbm, "int16 states read, codes written", "hbm"))
     return recs
 
 
