@@ -82,3 +82,22 @@ def test_program_names_parse_like_reference():
     assert torch.equal(d.matrix(), W.to(torch.bfloat16).double())
     with pytest.raises(NotImplementedError):
         word("rtn4", W, None, 0, {})
+
+
+def test_generic_sweep_without_environment_returns_the_columns():
+    """With no environment there is no Refit: the columns as they stood are W's, and the projection sees each one."""
+    from lookatmyquant_b200 import syntax
+    W = torch.randn(5, 12, dtype=torch.float64)
+    seen = []
+
+    def project(j, cols, T):
+        seen.append(j)
+        return cols.round()
+    out = syntax.sweep(W, None, project, width=3, lazy=6)
+    assert torch.equal(out, W) and seen == [0, 3, 6, 9]
+
+
+def test_scalar_ldlq_rejects_blocks_over_128():
+    from lookatmyquant_b200.ldlq_gpu import ldlq_round
+    with pytest.raises(ValueError, match="block"):
+        ldlq_round(torch.zeros(2, 4), torch.eye(4), torch.tensor([0.0, 1.0]), block=256)
