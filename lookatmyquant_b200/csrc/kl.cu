@@ -512,12 +512,13 @@ int run_pass(int mode, const uint16_t *H, int64_t ldh, int64_t ntok, int d, cons
     return LAMQ_OK;
 }
 
-int check_args(const uint16_t *H, int64_t ldh, int64_t ntok, int d, const uint16_t *E, int64_t lde, int V) {
-    LAMQ_REQUIRE(ntok > 0 && d > 0 && V > 0, "lamq_kl_head: bad shape");
-    LAMQ_REQUIRE(H && E, "lamq_kl_head: null pointer");
+int check_args(const char *fn, const uint16_t *H, int64_t ldh, int64_t ntok, int d, const uint16_t *E, int64_t lde,
+               int V) {
+    LAMQ_REQUIRE(ntok > 0 && d > 0 && V > 0, "%s: bad shape", fn);
+    LAMQ_REQUIRE(H && E, "%s: null pointer", fn);
     LAMQ_REQUIRE(d % 8 == 0 && ldh % 8 == 0 && lde % 8 == 0 && ldh >= d && lde >= d,
-                 "lamq_kl_head: d and leading dimensions must be multiples of 8 (16-byte rows for TMA)");
-    LAMQ_REQUIRE(((uintptr_t)H % 16) == 0 && ((uintptr_t)E % 16) == 0, "lamq_kl_head: operands not 16-byte aligned");
+                 "%s: d and leading dimensions must be multiples of 8 (16-byte rows for TMA)", fn);
+    LAMQ_REQUIRE(((uintptr_t)H % 16) == 0 && ((uintptr_t)E % 16) == 0, "%s: operands not 16-byte aligned", fn);
     return LAMQ_OK;
 }
 
@@ -531,7 +532,7 @@ extern "C" size_t lamq_kl_workspace_size(int64_t ntok) { return ntok <= 0 ? 0 : 
 extern "C" int lamq_kl_reference(const uint16_t *H, int64_t ldh, int64_t ntok, int d, const uint16_t *E, int64_t lde,
                                  int V, float *pdist, int64_t ldp, float *lse_ref, double *stat_a, double *stat_p,
                                  void *workspace, size_t workspace_bytes, int *status, lamq_stream_t stream) {
-    int st = check_args(H, ldh, ntok, d, E, lde, V);
+    int st = check_args("lamq_kl_reference", H, ldh, ntok, d, E, lde, V);
     if (st) return st;
     LAMQ_REQUIRE(pdist && lse_ref && stat_a && stat_p && workspace && status, "lamq_kl_reference: null pointer");
     LAMQ_REQUIRE(ldp >= V && ldp % 4 == 0 && ((uintptr_t)pdist % 16) == 0,
@@ -561,7 +562,7 @@ extern "C" int lamq_kl_head(const uint16_t *H, int64_t ldh, int64_t ntok, int d,
                             const float *pdist, int64_t ldp, const float *lse_ref, const double *stat_a,
                             const double *stat_p, const float *w, float *kl_pos, double *kl_out, void *workspace,
                             size_t workspace_bytes, int *status, lamq_stream_t stream) {
-    int st = check_args(H, ldh, ntok, d, E, lde, V);
+    int st = check_args("lamq_kl_head", H, ldh, ntok, d, E, lde, V);
     if (st) return st;
     LAMQ_REQUIRE(pdist && lse_ref && stat_a && stat_p && kl_pos && kl_out && workspace && status,
                  "lamq_kl_head: null pointer");

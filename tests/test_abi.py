@@ -47,3 +47,78 @@ def test_abi_version_and_errors_without_gpu(lib):
 def test_workspace_sizes(lib):
     assert lib.lamq_viterbi_workspace_size(100, 24, 12, 2) == 0  # short sequences keep back-pointers on chip
     assert lib.lamq_viterbi_workspace_size(3, 256, 12, 2) == 3 * 256 * 32 * 8
+
+
+# One call per entry point that breaks an argument rule: (name, arguments, a fragment of lamq_last_error()). Every
+# entry point checks its arguments before it touches the device, so these run without a GPU.
+N = None
+INVALID = [
+    ("lamq_viterbi_noalloc", (N, 4, 8, N, 12, 5, N, N, N), b"k must be 1..4"),
+    ("lamq_ldlq_round", (N, 4, 4, 4, N, 4, N, 2, 200, N, 4, N, 0, N), b"block in 1..128"),
+    ("lamq_ldlq_round", (N, 4, 4, 4, N, 4, N, 2, 16, N, 4, N, 0, N), b"null pointer"),
+    ("lamq_xtx_accumulate", (N, 8, N, 8, -1, 8, 1, N, 8, 0, N, N), b"bad shape"),
+    ("lamq_xtx_accumulate_scaled", (N, 8, N, 8, 16, 8, 1, 1.0, N, 8, 0, N, N), b"null pointer"),
+    ("lamq_gather_rows", (N, 12, N, 4, 12, N, N), b"bad shape"),
+    ("lamq_weighted_split", (N, 8, N, 8, N, N, 4, 0, N, N, N), b"bad shape"),
+    ("lamq_hessian_finalize", (N, N, 4, 4, 0.0, N, N, N), b"bad shape"),
+    ("lamq_hessian_finalize", (N, N, 4, 4, 1.0, N, N, N), b"null pointer"),
+    ("lamq_rht_rows", (N, 4, N, 4, 2, 0, 4, N, N, N, N, 1.0, N), b"factor orders"),
+    ("lamq_transpose_f64", (N, 4, N, 4, -1, 4, N), b"negative shape"),
+    ("lamq_dgemm", (0, -1, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N), b"negative shape"),
+    ("lamq_dgemm", (0, 4, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N), b"null pointer"),
+    ("lamq_cholesky_inverse_lower", (N, 2, 4, N, 0, N, N), b"bad shape"),
+    ("lamq_env_factor", (N, 4, 4, 0.01, N, 4, N, N, 0, N, N), b"null or aliased"),
+    ("lamq_ridge", (N, 2, N, 4, 4, 0.1, N), b"bad shape"),
+    ("lamq_cross_apply", (N, 4, 6, 4, N, 4, N, 4, 0.5, N, 4, N, 0, N), b"needs rows == n"),
+    ("lamq_kl_reference", (N, 8, 0, 8, N, 8, 16, N, 16, N, N, N, N, 0, N, N), b"lamq_kl_reference: bad shape"),
+    ("lamq_kl_head", (N, 8, 4, 8, N, 8, 16, N, 16, N, N, N, N, N, N, N, 0, N, N), b"lamq_kl_head: null pointer"),
+    ("lamq_ldlq_coltrellis", (N, 8, 8, 8, N, 8, N, N, N, 2, 11, 8, 1, 8, N, N, N, 0, N), b"L = 12"),
+    ("lamq_ldlq_coltrellis", (N, 8, 12, 8, N, 8, N, N, N, 2, 12, 8, 1, 8, N, N, N, 0, N), b"multiple of the run"),
+    ("lamq_pack_trellis", (N, 32, 4, 32, 0, 12, N, N, N), b"unsupported widths"),
+    ("lamq_unpack_trellis", (N, 4, 32, 2, 13, N, 32, N), b"unsupported widths"),
+    ("lamq_decode_trellis", (N, 4, 32, 2, 12, N, N, N, N, 16, N), b"leading dimension"),
+    ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, -1, N, 4, N), b"bad vector shape"),
+]
+
+# Empty inputs are a successful no-op, as the reference's loops over no rows are.
+EMPTY = [
+    ("lamq_viterbi_noalloc", (N, 0, 8, N, 12, 2, N, N, N)),
+    ("lamq_ldlq_round", (N, 4, 0, 4, N, 4, N, 2, 16, N, 4, N, 0, N)),
+    ("lamq_ldlq_rowtrellis", (N, 16, 0, 16, N, 16, N, N, N, N, 2, 12, 16, 20, 128, N, N, N, 0, N)),
+    ("lamq_xtx_accumulate", (N, 8, N, 8, 0, 8, 1, N, 8, 0, N, N)),
+    ("lamq_gather_rows", (N, 8, N, 0, 8, N, N)),
+    ("lamq_weighted_split", (N, 8, N, 8, N, N, 0, 8, N, N, N)),
+    ("lamq_rht_rows", (N, 4, N, 4, 0, 2, 2, N, N, N, N, 1.0, N)),
+    ("lamq_transpose_f64", (N, 4, N, 4, 0, 4, N)),
+    ("lamq_dgemm", (0, 0, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N)),
+    ("lamq_cholesky_inverse_lower", (N, 0, 0, N, 0, N, N)),
+    ("lamq_env_factor", (N, 0, 0, 0.01, N, 0, N, N, 0, N, N)),
+    ("lamq_ridge", (N, 0, N, 0, 0, 0.1, N)),
+    ("lamq_cross_apply", (N, 4, 0, 0, N, 4, N, 4, 0.5, N, 4, N, 0, N)),
+    ("lamq_pack_trellis", (N, 32, 0, 32, 2, 12, N, N, N)),
+    ("lamq_unpack_trellis", (N, 0, 32, 2, 12, N, 32, N)),
+    ("lamq_decode_trellis", (N, 0, 32, 2, 12, N, N, N, N, 32, N)),
+    ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, 0, N, 4, N)),
+]
+
+
+@pytest.mark.parametrize("name,args,text", INVALID, ids=[f"{c[0]}-{i}" for i, c in enumerate(INVALID)])
+def test_entry_point_rejects_bad_arguments(lib, name, args, text):
+    before = lib.lamq_kernel_launches()
+    assert getattr(lib, name)(*args) == _lib.LAMQ_ERR_INVALID
+    assert text in lib.lamq_last_error()
+    assert lib.lamq_kernel_launches() == before
+
+
+@pytest.mark.parametrize("name,args", EMPTY, ids=[c[0] for c in EMPTY])
+def test_entry_point_accepts_empty_input(lib, name, args):
+    before = lib.lamq_kernel_launches()
+    assert getattr(lib, name)(*args) == _lib.LAMQ_OK
+    assert lib.lamq_kernel_launches() == before
+
+
+def test_invalid_and_empty_tables_cover_every_compute_entry_point():
+    compute = {n for n in declared() if not n.endswith(("_workspace_size", "_words_per_row"))}
+    compute -= {"lamq_abi_version", "lamq_last_error", "lamq_kernel_launches"}
+    covered = {c[0] for c in INVALID} | {c[0] for c in EMPTY} | {"lamq_viterbi", "lamq_ldlq_rowtrellis"}
+    assert compute <= covered, sorted(compute - covered)
