@@ -24,6 +24,7 @@
  *   lamq_unpack_trellis
  *   lamq_decode_trellis    compiler_artifact.py:433-442  decode_rotated: table[state]·scale per group row
  *   lamq_trellis_product   runtime_mlx/fast_q35.py:69-172 the product kernel: y = S ⊙ (V[state]·(R_in x)) per group
+ *   lamq_trellis_product_groups                       the same for all row groups that read one input, one launch
  *   lamq_kl_reference,     compiler.py:176-187        the KL probe: ref_lp once, then per probe the KL of the held
  *   lamq_kl_head                                      positions' log_softmax(lm_head(h)) to it
  */
@@ -294,6 +295,31 @@ int lamq_decode_trellis(const uint32_t *codes, int64_t rows, int n, int k, int L
 int lamq_trellis_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales,
                          const float *table, const uint32_t *map, const float *x, int64_t ldx, int nvec, float *y,
                          int64_t ldy, lamq_stream_t stream);
+
+/*
+ * One packed row group of a grouped product: `rows` packed rows of k-bit symbols (1 <= k <= 4) and L-bit states,
+ * their scales and 2^L-entry fp32 table, the output row of each (map, or NULL for row r) and the output y (nvec rows
+ * of leading dimension ldy). 64 bytes, no padding.
+ */
+typedef struct lamq_product_group {
+    const uint32_t *codes;
+    int64_t rows;
+    int k, L;
+    const float *scales;
+    const float *table;
+    const uint32_t *map;
+    float *y;
+    int64_t ldy;
+} lamq_product_group;
+
+/*
+ * lamq_trellis_product for ngroups row groups that all read the same rotated input x (nvec x n): the row groups of
+ * one matrix, or of every matrix of a stage (runtime_mlx/fast_q35.py's q/k/v and gate/up share their input), in one
+ * launch per 32 groups and 16 vectors. Each output row equals lamq_trellis_product's bit for bit. `groups` is host
+ * memory, read before the call returns.
+ */
+int lamq_trellis_product_groups(const lamq_product_group *groups, int ngroups, int n, const float *x, int64_t ldx,
+                                int nvec, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -55,10 +55,17 @@ SIGNATURES = {
     "lamq_unpack_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _I64, _P]),
     "lamq_decode_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _P]),
     "lamq_trellis_product": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P]),
+    "lamq_trellis_product_groups": (_I32, [_P, _I32, _I32, _P, _I64, _I32, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64, _I32]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),
 }
+
+
+class ProductGroup(_c.Structure):
+    """lamq_product_group: one packed row group of a grouped product (64 bytes, the header's field order)."""
+    _fields_ = [("codes", _P), ("rows", _I64), ("k", _I32), ("L", _I32), ("scales", _P), ("table", _P),
+                ("map", _P), ("y", _P), ("ldy", _I64)]
 
 
 class LamqError(RuntimeError):

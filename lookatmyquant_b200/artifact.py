@@ -1,5 +1,6 @@
 """Packed trellis rows on B200: the opgraph-packed-1 trellis encoding and the product with packed rows
-(liblamq_b200: lamq_pack_trellis, lamq_unpack_trellis, lamq_decode_trellis, lamq_trellis_product).
+(liblamq_b200: lamq_pack_trellis, lamq_unpack_trellis, lamq_decode_trellis, lamq_trellis_product,
+lamq_trellis_product_groups).
 
 Reference (ShinMegamiBoson/lookatmyquant):
   valid_path, pack_trellis, unpack_trellis      compiler_artifact.py:261-297
@@ -166,9 +167,10 @@ def decode_rotated(tensors: dict, meta: dict) -> torch.Tensor:
 
 class TrellisProduct:
     """y = W·x for a packed grouped matrix, W = diag(S)·V[state]·R_in (the product of runtime_mlx/fast_q35.py):
-    x is rotated once (R_in x, fp64 through the Kronecker factors, then fp32) and every row group multiplies its packed
-    rows with it (lamq_trellis_product). With DENSE_PRODUCT_VECTORS or more vectors, each group is decoded once into
-    bf16 and the product runs as a dense bf16 GEMM with fp32 accumulation."""
+    x is rotated once (R_in x, fp64 through the Kronecker factors, then fp32) and the row groups multiply their packed
+    rows with it, all in one launch (lamq_trellis_product_groups; `product_rotated` does the same for every matrix of
+    a stage). With DENSE_PRODUCT_VECTORS or more vectors, each group is decoded once into bf16 and the product runs
+    as a dense bf16 GEMM with fp32 accumulation."""
 
     def __init__(self, tensors: dict, meta: dict, device=None):
         self.meta = meta
@@ -211,10 +213,49 @@ class TrellisProduct:
         if nvec >= DENSE_PRODUCT_VECTORS:
             return (xr.to(torch.bfloat16) @ self.dense_rotated().T).float()
         y = torch.empty(nvec, self.m, dtype=torch.float32, device=self.device)
-        lib = _lib.load()
-        for g, codes, rows, scales, table in self.groups:
-            with torch.cuda.device(self.device):
-                check(lib.lamq_trellis_product(ptr(codes), rows.numel(), self.n, g["bits"], g["state_bits"],
-                                               ptr(scales), ptr(table), ptr(rows), ptr(xr), xr.stride(0), nvec,
-                                               ptr(y), y.stride(0), stream_ptr(self.device)), "lamq_trellis_product")
+        _grouped_product([(self, y)], xr)
         return y
+
+    def product_groups(self, y: torch.Tensor) -> list:
+        """(lamq_product_group, row group) for each row group of this matrix, writing its rows of y (nvec × m)."""
+        return [(_lib.ProductGroup(ptr(codes), rows.numel(), g["bits"], g["state_bits"], ptr(scales), ptr(table),
+                                   ptr(rows), ptr(y), y.stride(0)), (g, codes, rows, scales, table))
+                for g, codes, rows, scales, table in self.groups]
+
+
+def _grouped_product(pairs: list, xr: torch.Tensor):
+    """Every row group of the (TrellisProduct, y) pairs times xr: the groups of 1-4-bit symbols in one
+    lamq_trellis_product_groups call, wider symbols (up to 8 bits) one lamq_trellis_product call each."""
+    device, n, nvec = pairs[0][0].device, pairs[0][0].n, xr.shape[0]
+    lib = _lib.load()
+    narrow, wide = [], []
+    for prod, y in pairs:
+        for desc, grp in prod.product_groups(y):
+            (narrow if desc.k <= 4 else wide).append((desc, grp, y))
+    with torch.cuda.device(device):
+        if narrow:
+            arr = (_lib.ProductGroup * len(narrow))(*[d for d, _, _ in narrow])
+            check(lib.lamq_trellis_product_groups(arr, len(narrow), n, ptr(xr), xr.stride(0), nvec,
+                                                  stream_ptr(device)), "lamq_trellis_product_groups")
+        for _, (g, codes, rows, scales, table), y in wide:
+            check(lib.lamq_trellis_product(ptr(codes), rows.numel(), n, g["bits"], g["state_bits"], ptr(scales),
+                                           ptr(table), ptr(rows), ptr(xr), xr.stride(0), nvec, ptr(y), y.stride(0),
+                                           stream_ptr(device)), "lamq_trellis_product")
+
+
+def product_rotated(products: list, xr: torch.Tensor) -> list:
+    """[p.rotated(xr) for p in products] for matrices that read one rotated input (a stage's q/k/v or gate/up, whose
+    entries share their input signs), with every row group of every matrix in one launch. Results are equal to the
+    per-matrix calls', bit for bit."""
+    if not products:
+        return []
+    n, device = products[0].n, products[0].device
+    if any(p.n != n or p.device != device for p in products):
+        raise ValueError("product_rotated: the matrices must share the input width and the device")
+    xr = xr.to(device, torch.float32).contiguous()
+    nvec = xr.shape[0]
+    if nvec >= DENSE_PRODUCT_VECTORS:
+        return [p.rotated(xr) for p in products]
+    ys = [torch.empty(nvec, p.m, dtype=torch.float32, device=device) for p in products]
+    _grouped_product(list(zip(products, ys)), xr)
+    return ys

@@ -178,17 +178,8 @@ __global__ void __launch_bounds__(kProductWarps * 32) trellis_product_kernel(
     }
 }
 
-// The product for symbol widths K = 1..4, a lane owning 8 consecutive columns: their 8 states lie within
-// 7K + L <= 40 bits of the row's stream, so three words loaded once give all 8 (two selects and a funnel shift each),
-// and the 8 input values arrive as two float4 loads per vector. A CTA of 8 warps takes kRowsPerCta rows at a time;
-// the warps take 256-column blocks in turn, and their partial sums are added in a fixed order through shared memory.
-template <int NV, int K>
-__global__ void __launch_bounds__(kProductWarps * 32) trellis_product8_kernel(
-    const uint32_t *__restrict__ codes, int64_t rows, int n, int L, const float *__restrict__ scales,
-    const float *__restrict__ table, const uint32_t *__restrict__ map, const float *__restrict__ x, int64_t ldx,
-    int xvec, float *__restrict__ y, int64_t ldy) {
-    __shared__ __align__(16) float tab[4096];
-    __shared__ float part[kProductWarps][kRowsPerCta][NV];
+// The 2^L values of a table into shared memory, 16 bytes a load where the table's alignment allows.
+__device__ __forceinline__ void load_table(float *tab, const float *__restrict__ table, int L) {
     const int nt = 1 << L;
     if ((reinterpret_cast<uintptr_t>(table) & 15) == 0 && nt >= 4) {
 #pragma unroll 4
@@ -198,85 +189,159 @@ __global__ void __launch_bounds__(kProductWarps * 32) trellis_product8_kernel(
 #pragma unroll 16
         for (int i = threadIdx.x; i < nt; i += blockDim.x) tab[i] = __ldg(table + i);
     }
-    __syncthreads();
-    const uint32_t smask = (1u << L) - 1u;
+}
+
+// The product for symbol widths K = 1..4, a lane owning 8 consecutive columns: their 8 states lie within
+// 7K + L <= 40 bits of the row's stream, so three words loaded once give all 8 (two selects and a funnel shift each),
+// and the 8 input values arrive as two float4 loads per vector. The CTA's 8 warps take the 256-column blocks of rows
+// r0 .. r0 + kRowsPerCta − 1 in turn, and their partial sums are added in a fixed order through shared memory, so a
+// row's result does not depend on which launch or CTA computed it. Every thread of the CTA calls this; it ends with
+// a barrier, after which `tab` and `part` may be rewritten.
+template <int NV, int K>
+__device__ __forceinline__ void product8_rows(const uint32_t *__restrict__ codes, int64_t rows, int n, uint32_t smask,
+                                              const float *__restrict__ scales, const float *tab,
+                                              const uint32_t *__restrict__ map, const float *__restrict__ x,
+                                              int64_t ldx, int xvec, float *__restrict__ y, int64_t ldy, int64_t r0,
+                                              float (*part)[kRowsPerCta][NV]) {
     const int N = (n + 31) / 32 * 32;
     const int wpr = N / 32 * K;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nblk = (n + 255) / 256;
-    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
-    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
-        const int64_t r0 = g * kRowsPerCta;
-        float acc[kRowsPerCta][NV];
+    float acc[kRowsPerCta][NV];
 #pragma unroll
-        for (int a = 0; a < kRowsPerCta; ++a)
+    for (int a = 0; a < kRowsPerCta; ++a)
 #pragma unroll
-            for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
-        for (int blk = warp; blk < nblk; blk += kProductWarps) {
-            const int jb = blk * 256 + lane * 8;  // this lane's first column
-            if (jb >= n) continue;
-            // column jb + i has its state at bit (N − 1 − jb − i)·K, i.e. (7 − i)·K above that of column jb + 7
-            const int64_t bp = (int64_t)(N - 1 - (jb + 7)) * K;
-            const int64_t w0 = bp >> 5;
-            const int sh0 = (int)(bp & 31);
-            uint32_t wv[kRowsPerCta][3];
+        for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
+    for (int blk = warp; blk < nblk; blk += kProductWarps) {
+        const int jb = blk * 256 + lane * 8;  // this lane's first column
+        if (jb >= n) continue;
+        // column jb + i has its state at bit (N − 1 − jb − i)·K, i.e. (7 − i)·K above that of column jb + 7
+        const int64_t bp = (int64_t)(N - 1 - (jb + 7)) * K;
+        const int64_t w0 = bp >> 5;
+        const int sh0 = (int)(bp & 31);
+        uint32_t wv[kRowsPerCta][3];
 #pragma unroll
-            for (int a = 0; a < kRowsPerCta; ++a) {
-                const uint32_t *row = codes + min(r0 + a, rows - 1) * wpr;
+        for (int a = 0; a < kRowsPerCta; ++a) {
+            const uint32_t *row = codes + min(r0 + a, rows - 1) * wpr;
 #pragma unroll
-                for (int q = 0; q < 3; ++q) wv[a][q] = (w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
-            }
-            const bool full = xvec && jb + 8 <= n;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float xv[NV][4];
-#pragma unroll
-                for (int v = 0; v < NV; ++v) {
-                    const float *xp = x + (int64_t)v * ldx + jb + 4 * h;
-                    if (full) {
-                        const float4 t = __ldg(reinterpret_cast<const float4 *>(xp));
-                        xv[v][0] = t.x; xv[v][1] = t.y; xv[v][2] = t.z; xv[v][3] = t.w;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) xv[v][i] = (jb + 4 * h + i < n) ? __ldg(xp + i) : 0.f;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int shift = sh0 + (7 - (4 * h + i)) * K;  // < 32 + 7K + 1, inside the three words
-                    const bool up = shift >= 32;
-#pragma unroll
-                    for (int a = 0; a < kRowsPerCta; ++a) {
-                        const uint32_t lo = up ? wv[a][1] : wv[a][0], hi = up ? wv[a][2] : wv[a][1];
-                        const float val = tab[__funnelshift_r(lo, hi, shift & 31) & smask];
-#pragma unroll
-                        for (int v = 0; v < NV; ++v) acc[a][v] = fmaf(val, xv[v][i], acc[a][v]);
-                    }
-                }
-            }
+            for (int q = 0; q < 3; ++q) wv[a][q] = (w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
         }
+        const bool full = xvec && jb + 8 <= n;
 #pragma unroll
-        for (int a = 0; a < kRowsPerCta; ++a)
+        for (int h = 0; h < 2; ++h) {
+            float xv[NV][4];
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
-                float s = acc[a][v];
+                const float *xp = x + (int64_t)v * ldx + jb + 4 * h;
+                if (full) {
+                    const float4 t = __ldg(reinterpret_cast<const float4 *>(xp));
+                    xv[v][0] = t.x; xv[v][1] = t.y; xv[v][2] = t.z; xv[v][3] = t.w;
+                } else {
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if (lane == 0) part[warp][a][v] = s;
+                    for (int i = 0; i < 4; ++i) xv[v][i] = (jb + 4 * h + i < n) ? __ldg(xp + i) : 0.f;
+                }
             }
-        __syncthreads();
-        for (int e = threadIdx.x; e < kRowsPerCta * NV; e += blockDim.x) {
-            const int a = e / NV, v = e % NV;
-            const int64_t r = r0 + a;
-            if (r < rows) {
-                float s = 0.f;
 #pragma unroll
-                for (int w = 0; w < kProductWarps; ++w) s += part[w][a][v];
-                const int64_t orow = map ? (int64_t)map[r] : r;
-                y[(int64_t)v * ldy + orow] = s * scales[r];
+            for (int i = 0; i < 4; ++i) {
+                const int shift = sh0 + (7 - (4 * h + i)) * K;  // < 32 + 7K + 1, inside the three words
+                const bool up = shift >= 32;
+#pragma unroll
+                for (int a = 0; a < kRowsPerCta; ++a) {
+                    const uint32_t lo = up ? wv[a][1] : wv[a][0], hi = up ? wv[a][2] : wv[a][1];
+                    const float val = tab[__funnelshift_r(lo, hi, shift & 31) & smask];
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) acc[a][v] = fmaf(val, xv[v][i], acc[a][v]);
+                }
             }
         }
-        __syncthreads();  // part is rewritten by the next rows
+    }
+#pragma unroll
+    for (int a = 0; a < kRowsPerCta; ++a)
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            float s = acc[a][v];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) part[warp][a][v] = s;
+        }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kRowsPerCta * NV; e += blockDim.x) {
+        const int a = e / NV, v = e % NV;
+        const int64_t r = r0 + a;
+        if (r < rows) {
+            float s = 0.f;
+#pragma unroll
+            for (int w = 0; w < kProductWarps; ++w) s += part[w][a][v];
+            const int64_t orow = map ? (int64_t)map[r] : r;
+            y[(int64_t)v * ldy + orow] = s * scales[r];
+        }
+    }
+    __syncthreads();  // part (and, between matrices, tab) is rewritten next
+}
+
+// One packed matrix (one row group of one width) times NV vectors; a persistent grid loads the table once per CTA.
+template <int NV, int K>
+__global__ void __launch_bounds__(kProductWarps * 32) trellis_product8_kernel(
+    const uint32_t *__restrict__ codes, int64_t rows, int n, int L, const float *__restrict__ scales,
+    const float *__restrict__ table, const uint32_t *__restrict__ map, const float *__restrict__ x, int64_t ldx,
+    int xvec, float *__restrict__ y, int64_t ldy) {
+    __shared__ __align__(16) float tab[4096];
+    __shared__ float part[kProductWarps][kRowsPerCta][NV];
+    load_table(tab, table, L);
+    __syncthreads();
+    const uint32_t smask = (1u << L) - 1u;
+    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x)
+        product8_rows<NV, K>(codes, rows, n, smask, scales, tab, map, x, ldx, xvec, y, ldy, g * kRowsPerCta, part);
+}
+
+// Several packed matrices that read the same input vectors (the row groups of a stage's matrices, each of its own
+// width, table, scales and output), in one launch: their kRowsPerCta-row units are numbered one after another and
+// every CTA takes a contiguous share of them, so it crosses few matrix boundaries and loads few tables. A row's
+// result is the same as from trellis_product8_kernel, bit for bit (the same body and reduction order).
+constexpr int kMaxProductGroups = 32;
+
+struct ProductGroups {
+    const uint32_t *codes[kMaxProductGroups];
+    const float *scales[kMaxProductGroups];
+    const float *table[kMaxProductGroups];
+    const uint32_t *map[kMaxProductGroups];
+    float *y[kMaxProductGroups];
+    int64_t rows[kMaxProductGroups];
+    int64_t ldy[kMaxProductGroups];
+    int64_t first[kMaxProductGroups + 1];  // the first unit of each matrix; first[ng] = all units
+    int k[kMaxProductGroups];
+    int L[kMaxProductGroups];
+    int ng;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(kProductWarps * 32) trellis_product_groups_kernel(
+    const __grid_constant__ ProductGroups p, int n, const float *__restrict__ x, int64_t ldx, int xvec) {
+    __shared__ __align__(16) float tab[4096];
+    __shared__ float part[kProductWarps][kRowsPerCta][NV];
+    const int64_t total = p.first[p.ng];
+    const int64_t u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
+    int i = 0, loaded = -1;
+    for (int64_t u = u0; u < u1; ++u) {
+        while (u >= p.first[i + 1]) ++i;  // u < total, so i stays below ng; empty matrices are skipped
+        if (i != loaded) {  // the previous rows' product ended with a barrier: nobody reads tab now
+            load_table(tab, p.table[i], p.L[i]);
+            __syncthreads();
+            loaded = i;
+        }
+        const uint32_t smask = (1u << p.L[i]) - 1u;
+        const int64_t r0 = (u - p.first[i]) * kRowsPerCta;
+        switch (p.k[i]) {
+            case 1: product8_rows<NV, 1>(p.codes[i], p.rows[i], n, smask, p.scales[i], tab, p.map[i], x, ldx, xvec,
+                                         p.y[i], p.ldy[i], r0, part); break;
+            case 2: product8_rows<NV, 2>(p.codes[i], p.rows[i], n, smask, p.scales[i], tab, p.map[i], x, ldx, xvec,
+                                         p.y[i], p.ldy[i], r0, part); break;
+            case 3: product8_rows<NV, 3>(p.codes[i], p.rows[i], n, smask, p.scales[i], tab, p.map[i], x, ldx, xvec,
+                                         p.y[i], p.ldy[i], r0, part); break;
+            default: product8_rows<NV, 4>(p.codes[i], p.rows[i], n, smask, p.scales[i], tab, p.map[i], x, ldx, xvec,
+                                          p.y[i], p.ldy[i], r0, part); break;
+        }
     }
 }
 
@@ -303,6 +368,12 @@ void launch_product(const uint32_t *codes, int64_t rows, int n, int k, int L, co
             trellis_product_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, k, L, scales, table, map, x,
                                                                            ldx, y, ldy);
     }
+}
+
+template <int NV>
+void launch_groups(const ProductGroups &p, int n, const float *x, int64_t ldx, int xvec, cudaStream_t s) {
+    const int grid = (int)std::min<int64_t>(p.first[p.ng], 148 * 6);
+    trellis_product_groups_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(p, n, x, ldx, xvec);
 }
 
 }  // namespace
@@ -372,6 +443,65 @@ extern "C" int lamq_trellis_product(const uint32_t *codes, int64_t rows, int n, 
         else if (left >= 2) launch_product<2>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 2;
         else launch_product<1>(codes, rows, n, k, L, scales, table, map, xv, ldx, yv, ldy, s), v += 1;
         LAMQ_CHECK_LAUNCH("lamq_trellis_product");
+    }
+    return LAMQ_OK;
+}
+
+static_assert(sizeof(lamq_product_group) == 64, "lamq_product_group is 64 bytes in the C ABI");
+
+extern "C" int lamq_trellis_product_groups(const lamq_product_group *groups, int ngroups, int n, const float *x,
+                                           int64_t ldx, int nvec, lamq_stream_t stream) {
+    LAMQ_REQUIRE(ngroups >= 0 && n > 0 && nvec >= 0 && ldx >= n, "lamq_trellis_product_groups: bad shape");
+    if (ngroups == 0 || nvec == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(groups && x, "lamq_trellis_product_groups: null pointer");
+    for (int i = 0; i < ngroups; ++i) {
+        const lamq_product_group &g = groups[i];
+        LAMQ_REQUIRE(g.rows >= 0, "lamq_trellis_product_groups: group %d has %lld rows", i, (long long)g.rows);
+        LAMQ_REQUIRE(g.k >= 1 && g.k <= 4 && g.L > g.k && g.L <= 12,
+                     "lamq_trellis_product_groups: group %d: widths k in 1..4 and L in k+1..12 (k %d, L %d)", i, g.k,
+                     g.L);
+        LAMQ_REQUIRE(g.rows == 0 || (g.codes && g.scales && g.table && g.y),
+                     "lamq_trellis_product_groups: group %d: null pointer", i);
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    const int xvec = ((uintptr_t)x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
+    for (int b = 0; b < ngroups; b += kMaxProductGroups) {
+        ProductGroups p{};
+        int64_t units = 0;
+        int ng = 0;
+        for (int i = b; i < std::min(ngroups, b + kMaxProductGroups); ++i, ++ng) {
+            const lamq_product_group &g = groups[i];
+            p.codes[ng] = g.codes;
+            p.scales[ng] = g.scales;
+            p.table[ng] = g.table;
+            p.map[ng] = g.map;
+            p.y[ng] = g.y;
+            p.rows[ng] = g.rows;
+            p.ldy[ng] = g.ldy;
+            p.k[ng] = g.k;
+            p.L[ng] = g.L;
+            p.first[ng] = units;
+            units += (g.rows + kRowsPerCta - 1) / kRowsPerCta;
+        }
+        p.first[ng] = units;
+        p.ng = ng;
+        if (units == 0) continue;
+        for (int v = 0; v < nvec;) {
+            const int left = nvec - v;
+            const int nv = left >= 16 ? 16 : left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+            ProductGroups q = p;
+            for (int i = 0; i < ng; ++i) q.y[i] = p.y[i] + (int64_t)v * p.ldy[i];
+            const float *xv = x + (int64_t)v * ldx;
+            switch (nv) {
+                case 16: launch_groups<16>(q, n, xv, ldx, xvec, s); break;
+                case 8: launch_groups<8>(q, n, xv, ldx, xvec, s); break;
+                case 4: launch_groups<4>(q, n, xv, ldx, xvec, s); break;
+                case 2: launch_groups<2>(q, n, xv, ldx, xvec, s); break;
+                default: launch_groups<1>(q, n, xv, ldx, xvec, s); break;
+            }
+            LAMQ_CHECK_LAUNCH("lamq_trellis_product_groups");
+            v += nv;
+        }
     }
     return LAMQ_OK;
 }

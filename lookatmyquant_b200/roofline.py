@@ -111,7 +111,7 @@ def packed_layer(device, seed: int = 0):
 
 
 def run(device="cuda", log=print, only=None) -> list:
-    from . import _lib, codes
+    from . import _lib, artifact, codes
     from .artifact import decode_rotated, pack_trellis
     from .frame import Environment
     from .hessian import Statistics
@@ -235,15 +235,17 @@ def run(device="cuda", log=print, only=None) -> list:
         code_bytes = sum(t.numel() * t.element_size() for v in layer.values() for key, t in v[2].items()
                          if not key.endswith(".signs"))
         first = {}  # the first matrix of each stage rotates the stage's input for all of them
+        stages = {}  # the matrices of each stage: one grouped product launch reads the stage's rotated input
         for nm, v in layer.items():
             first.setdefault(v[4], nm)
+            stages.setdefault(v[4], []).append(v[0])
         for batch in (1, 16, 2048):
             xs = {st: torch.randn(batch, layer[nm][1], device=dev, generator=g).to(torch.bfloat16)
                   for st, nm in first.items()}
 
             def product():
                 xr = {st: layer[nm][0].rotate(xs[st]) for st, nm in first.items()}
-                return [v[0].rotated(xr[v[4]]) for v in layer.values()]
+                return [y for st, ps in stages.items() for y in artifact.product_rotated(ps, xr[st])]
             if batch >= 64:
                 for v in layer.values():
                     v[0].dense_rotated()  # decoded once per layer, as the product caches it
@@ -264,12 +266,12 @@ def run(device="cuda", log=print, only=None) -> list:
                 product()
             ms = timer(graph.replay)
             io = sum(2 * x.numel() for x in xs.values()) + sum(4 * batch * v[0].m for v in layer.values())
-            add(_record("a14", "trellis_product_kernel per row group + one input rotation per stage (one CUDA graph)",
+            add(_record("a14", "trellis_product_groups_kernel per stage + one input rotation per stage (one CUDA graph)",
                         f"layer ({weights / 1e6:.1f} M weights), batch {batch}", ms, code_bytes + io, "GB/s", hbm,
                         f"{weights * batch / (ms * 1e-3) / 1e12:.2f} T weight-products/s", "hbm"))
             xr = {st: layer[nm][0].rotate(xs[st]) for st, nm in first.items()}
-            ms = timer(lambda: [v[0].rotated(xr[v[4]]) for v in layer.values()])
-            add(_record("a14", "trellis_product_kernel alone (rotated inputs given)",
+            ms = timer(lambda: [artifact.product_rotated(ps, xr[st]) for st, ps in stages.items()])
+            add(_record("a14", "trellis_product_groups_kernel alone (rotated inputs given, one launch per stage)",
                         f"layer, batch {batch}", ms, code_bytes + io, "GB/s", hbm,
                         f"{weights * batch / (ms * 1e-3) / 1e12:.2f} T weight-products/s", "hbm"))
             del graph

@@ -78,6 +78,8 @@ INVALID = [
     ("lamq_unpack_trellis", (N, 4, 32, 2, 13, N, 32, N), b"unsupported widths"),
     ("lamq_decode_trellis", (N, 4, 32, 2, 12, N, N, N, N, 16, N), b"leading dimension"),
     ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, -1, N, 4, N), b"bad vector shape"),
+    ("lamq_trellis_product_groups", (N, 1, 0, N, 32, 1, N), b"bad shape"),
+    ("lamq_trellis_product_groups", (N, 1, 32, N, 32, 1, N), b"null pointer"),
 ]
 
 # Empty inputs are a successful no-op, as the reference's loops over no rows are.
@@ -99,6 +101,7 @@ EMPTY = [
     ("lamq_unpack_trellis", (N, 0, 32, 2, 12, N, 32, N)),
     ("lamq_decode_trellis", (N, 0, 32, 2, 12, N, N, N, N, 32, N)),
     ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, 0, N, 4, N)),
+    ("lamq_trellis_product_groups", (N, 0, 32, N, 32, 1, N)),
 ]
 
 
@@ -122,3 +125,20 @@ def test_invalid_and_empty_tables_cover_every_compute_entry_point():
     compute -= {"lamq_abi_version", "lamq_last_error", "lamq_kernel_launches"}
     covered = {c[0] for c in INVALID} | {c[0] for c in EMPTY} | {"lamq_viterbi", "lamq_ldlq_rowtrellis"}
     assert compute <= covered, sorted(compute - covered)
+
+
+def test_product_group_layout_matches_the_header(lib):
+    """The ctypes lamq_product_group reaches the library field for field: the checks quote rows, k and L back."""
+    assert ctypes.sizeof(_lib.ProductGroup) == 64
+    x = ctypes.c_float(0.0)
+    bad = [_lib.ProductGroup(None, 0, 1, 12, None, None, None, None, 0),
+           _lib.ProductGroup(None, -7, 1, 12, None, None, None, None, 0)]
+    arr = (_lib.ProductGroup * 2)(*bad)
+    assert lib.lamq_trellis_product_groups(arr, 2, 32, ctypes.addressof(x), 32, 1, None) == _lib.LAMQ_ERR_INVALID
+    assert b"group 1 has -7 rows" in lib.lamq_last_error()
+    arr[1] = _lib.ProductGroup(None, 4, 5, 11, None, None, None, None, 0)
+    assert lib.lamq_trellis_product_groups(arr, 2, 32, ctypes.addressof(x), 32, 1, None) == _lib.LAMQ_ERR_INVALID
+    assert b"group 1: widths" in lib.lamq_last_error() and b"(k 5, L 11)" in lib.lamq_last_error()
+    arr[1] = _lib.ProductGroup(None, 4, 3, 12, None, None, None, None, 0)
+    assert lib.lamq_trellis_product_groups(arr, 2, 32, ctypes.addressof(x), 32, 1, None) == _lib.LAMQ_ERR_INVALID
+    assert b"group 1: null pointer" in lib.lamq_last_error()

@@ -104,3 +104,68 @@ def test_product_matches_dense(golden, nvec):
     ref = xr @ g["decoded"].astype(np.float64).T
     tol = 1e-2 if nvec >= A.DENSE_PRODUCT_VECTORS else 1e-5  # bf16 dense path vs the fp32 packed product
     assert np.abs(y - ref).max() <= tol * np.abs(ref).max()
+
+
+def _random_product(m, n, widths, seed, name="w"):
+    """A grouped matrix of m rows whose row groups have the given symbol widths (random rows, valid paths, a random
+    4096-entry table each)."""
+    from lookatmyquant_b200 import artifact as A
+    gen = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(m, generator=gen)
+    cuts = np.linspace(0, m, len(widths) + 1).astype(int)
+    tensors = {name + ".signs": A.input_signs(n, seed)}
+    groups = []
+    for i, k in enumerate(widths):
+        rows = perm[cuts[i]:cuts[i + 1]].sort().values
+        key = f"{name}.g{i}"
+        states = torch.as_tensor(_path(rows.numel(), n, k, seed + i)).cuda()
+        tensors.update({key + ".rows": rows.to(torch.int32).cuda(), key + ".codes": A.pack_trellis(states, k),
+                        key + ".scales": (0.5 + torch.rand(rows.numel(), generator=gen)).float().cuda(),
+                        key + ".table": torch.randn(4096, generator=gen).float().cuda()})
+        groups.append({"rows": rows.numel(), "bits": k})
+    return A.TrellisProduct(tensors, A.grouped_matrix_meta(name, [m, n], groups))
+
+
+def _per_group(prod, xr):
+    """The product with one lamq_trellis_product launch per row group (the per-group kernel)."""
+    from lookatmyquant_b200 import _lib
+    from lookatmyquant_b200._lib import check, ptr, stream_ptr
+    lib = _lib.load()
+    y = torch.full((xr.shape[0], prod.m), float("nan"), device="cuda")
+    for g, codes, rows, scales, table in prod.groups:
+        check(lib.lamq_trellis_product(ptr(codes), rows.numel(), prod.n, g["bits"], g["state_bits"], ptr(scales),
+                                       ptr(table), ptr(rows), ptr(xr), xr.stride(0), xr.shape[0], ptr(y), y.stride(0),
+                                       stream_ptr(y.device)), "lamq_trellis_product")
+    return y
+
+
+@pytest.mark.parametrize("nvec", [1, 5, 21])
+def test_grouped_product_equals_per_group_launches(nvec):
+    """lamq_trellis_product_groups over a stage (three matrices, 1-4-bit groups and a 6-bit one, 39 row groups: two
+    launches of at most 32) gives every row exactly the per-group kernel's value, for aligned and unaligned inputs."""
+    from lookatmyquant_b200 import artifact as A
+    n = 284  # two column blocks, the last one ragged (n is 4 mod 8); R_in of order 284 is one Paley factor
+    prods = [_random_product(300, n, [1, 2, 3, 4] * 3, 11), _random_product(77, n, [2, 4, 6], 12, "v"),
+             _random_product(130, n, [4, 3, 2, 1] * 6, 13, "u")]
+    gen = torch.Generator().manual_seed(nvec)
+    base = torch.randn(nvec, n + 1, generator=gen).float().cuda()
+    for xr in (base[:, :n].contiguous(), base[:, 1:]):  # 16-byte rows, then rows at an odd offset and stride
+        ys = A.product_rotated(prods, xr)
+        for p, y in zip(prods, ys):
+            ref = _per_group(p, xr)
+            assert not torch.isnan(ref).any()
+            assert torch.equal(y, ref)
+            assert torch.equal(p.rotated(xr), ref)
+
+
+def test_grouped_product_skips_empty_groups():
+    from lookatmyquant_b200 import _lib
+    from lookatmyquant_b200._lib import check, ptr, stream_ptr
+    p = _random_product(40, 64, [3, 1], 5)
+    xr = torch.randn(2, 64).float().cuda()
+    y = torch.zeros(2, 40, device="cuda")
+    (g0, _), (g1, _) = p.product_groups(y)
+    empty = _lib.ProductGroup(None, 0, 2, 12, None, None, None, None, 0)
+    arr = (_lib.ProductGroup * 4)(empty, g0, empty, g1)
+    check(_lib.load().lamq_trellis_product_groups(arr, 4, 64, ptr(xr), 64, 2, stream_ptr()), "groups")
+    assert torch.equal(y, _per_group(p, xr))
