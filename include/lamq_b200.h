@@ -315,7 +315,7 @@ typedef struct lamq_product_group {
 /*
  * lamq_trellis_product for ngroups row groups that all read the same rotated input x (nvec x n): the row groups of
  * one matrix, or of every matrix of a stage (runtime_mlx/fast_q35.py's q/k/v and gate/up share their input), in one
- * launch per 32 groups and 16 vectors. Each output row equals lamq_trellis_product's bit for bit. `groups` is host
+ * launch per 32 groups and 8 vectors. Each output row equals lamq_trellis_product's bit for bit. `groups` is host
  * memory, read before the call returns.
  */
 int lamq_trellis_product_groups(const lamq_product_group *groups, int ngroups, int n, const float *x, int64_t ldx,

@@ -486,14 +486,15 @@ extern "C" int lamq_trellis_product_groups(const lamq_product_group *groups, int
         p.first[ng] = units;
         p.ng = ng;
         if (units == 0) continue;
+        // at most 8 vectors a launch: 16 take 255 registers a thread and one CTA per SM, and two 8-vector passes
+        // over the (L2-resident) codes of a layer were faster than one 16-vector pass (0.44 against 0.50 ms)
         for (int v = 0; v < nvec;) {
             const int left = nvec - v;
-            const int nv = left >= 16 ? 16 : left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+            const int nv = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
             ProductGroups q = p;
             for (int i = 0; i < ng; ++i) q.y[i] = p.y[i] + (int64_t)v * p.ldy[i];
             const float *xv = x + (int64_t)v * ldx;
             switch (nv) {
-                case 16: launch_groups<16>(q, n, xv, ldx, xvec, s); break;
                 case 8: launch_groups<8>(q, n, xv, ldx, xvec, s); break;
                 case 4: launch_groups<4>(q, n, xv, ldx, xvec, s); break;
                 case 2: launch_groups<2>(q, n, xv, ldx, xvec, s); break;

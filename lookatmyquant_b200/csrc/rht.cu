@@ -8,6 +8,7 @@
 //
 // One CTA transforms one row in shared memory, in place: phase 1 (one warp per row p of V) forms Z = V·Beᵀ, phase 2
 // (one warp per column q) forms Y = Ae·Z; each lane keeps the sign bits of the factor rows it produces in registers.
+// Fewer than kSplitRows rows (a decode step's few input vectors) are spread over many CTAs instead (the split form).
 // The general form computed is y = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)), so R (Ae = A, Be = B, pre = s) and Rᵀ
 // (Ae = Aᵀ, Be = Bᵀ, post = s) are both one pass.
 #include "lamq_common.cuh"
@@ -133,6 +134,85 @@ __global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
     }
 }
 
+// The split form, for a few rows: one CTA per row leaves most SMs idle and runs a row's a·b·(a + b) additions on one
+// SM, so each row is spread over many CTAs in two launches instead. Row pr of Z = V·Beᵀ depends on row pr of V only,
+// and column q of Y = Ae·Z on column q of Z only, so rht_split_rows_kernel writes kSplitWarps rows of Z per CTA into
+// `out` and rht_split_cols_kernel turns kSplitWarps columns of Z per CTA into Y in place: the CTAs of a launch share
+// no data and no scratch is needed. The sums run in the same order as in rht_rows_kernel, so the results are equal.
+constexpr int kSplitWarps = 8;
+constexpr int64_t kSplitRows = 128;  // fewer rows than this take the split form
+
+template <int NB>
+__global__ void __launch_bounds__(kSplitWarps * 32) rht_split_rows_kernel(RhtParams p) {
+    extern __shared__ __align__(16) double sz[];  // kSplitWarps rows of V, b each
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slices = (p.a + kSplitWarps - 1) / kSplitWarps;
+    const int64_t row = blockIdx.x / slices;
+    const int pr0 = (int)(blockIdx.x % slices) * kSplitWarps;
+    const int nr = min(kSplitWarps, p.a - pr0);
+    const int64_t off = (int64_t)pr0 * p.b;
+    const double *src = p.in + row * p.ldi + off;
+    for (int e = threadIdx.x; e < nr * p.b; e += blockDim.x) sz[e] = p.pre ? src[e] * p.pre[off + e] : src[e];
+    __syncthreads();
+    if (warp >= nr) return;
+    uint32_t bits[NB][8];
+#pragma unroll
+    for (int c = 0; c < NB; ++c) {
+        const int q = lane + 32 * c;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) bits[c][w] = (q < p.b && w < p.wb) ? __ldg(p.bbits + q * p.wb + w) : 0u;
+    }
+    double acc[NB];
+#pragma unroll
+    for (int c = 0; c < NB; ++c) acc[c] = 0.0;
+    signed_sums<NB>(sz + warp * p.b, 1, p.b, bits, acc);
+    double *dst = p.out + row * p.ldo + off + (int64_t)warp * p.b;
+#pragma unroll
+    for (int c = 0; c < NB; ++c) {
+        const int q = lane + 32 * c;
+        if (q < p.b) dst[q] = acc[c];
+    }
+}
+
+template <int NA>
+__global__ void __launch_bounds__(kSplitWarps * 32) rht_split_cols_kernel(RhtParams p) {
+    extern __shared__ __align__(16) double sz[];  // kSplitWarps columns of Z, a each, at a stride of a + 1
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slices = (p.b + kSplitWarps - 1) / kSplitWarps;
+    const int64_t row = blockIdx.x / slices;
+    const int q0 = (int)(blockIdx.x % slices) * kSplitWarps;
+    const int nq = min(kSplitWarps, p.b - q0);
+    const int ld = p.a + 1;
+    double *Z = p.out + row * p.ldo;
+    for (int e = threadIdx.x; e < nq * p.a; e += blockDim.x) {  // consecutive threads: consecutive columns of a row
+        const int pr = e / nq, w = e - pr * nq;
+        sz[w * ld + pr] = Z[(int64_t)pr * p.b + q0 + w];
+    }
+    __syncthreads();
+    if (warp >= nq) return;
+    uint32_t bits[NA][8];
+#pragma unroll
+    for (int c = 0; c < NA; ++c) {
+        const int pr = lane + 32 * c;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) bits[c][w] = (pr < p.a && w < p.wa) ? __ldg(p.abits + pr * p.wa + w) : 0u;
+    }
+    double acc[NA];
+#pragma unroll
+    for (int c = 0; c < NA; ++c) acc[c] = 0.0;
+    signed_sums<NA>(sz + warp * ld, 1, p.a, bits, acc);
+    const int q = q0 + warp;
+#pragma unroll
+    for (int c = 0; c < NA; ++c) {
+        const int pr = lane + 32 * c;
+        if (pr < p.a) {
+            const int64_t e = (int64_t)pr * p.b + q;
+            const double y = acc[c] * p.scale;
+            Z[e] = p.post ? y * p.post[e] : y;
+        }
+    }
+}
+
 constexpr int kTile = 32;
 
 __global__ void transpose_kernel(const double *__restrict__ in, int64_t ldi, double *__restrict__ out, int64_t ldo,
@@ -167,6 +247,18 @@ int launch_rht(const RhtParams &p, cudaStream_t stream) {
     return LAMQ_OK;
 }
 
+template <int NA, int NB>
+int launch_rht_split(const RhtParams &p, cudaStream_t stream) {
+    const int64_t sa = (p.a + kSplitWarps - 1) / kSplitWarps, sb = (p.b + kSplitWarps - 1) / kSplitWarps;
+    rht_split_rows_kernel<NB><<<(unsigned)(p.rows * sa), kSplitWarps * 32, (size_t)kSplitWarps * p.b * sizeof(double),
+                                stream>>>(p);
+    LAMQ_CHECK_LAUNCH("lamq_rht_rows (rows of V)");
+    rht_split_cols_kernel<NA><<<(unsigned)(p.rows * sb), kSplitWarps * 32,
+                                (size_t)kSplitWarps * (p.a + 1) * sizeof(double), stream>>>(p);
+    LAMQ_CHECK_LAUNCH("lamq_rht_rows (columns of Z)");
+    return LAMQ_OK;
+}
+
 }  // namespace
 
 }  // namespace lamq
@@ -189,7 +281,8 @@ extern "C" int lamq_rht_rows(const double *in, int64_t ldi, double *out, int64_t
     const int na = wa <= 1 ? 1 : wa <= 2 ? 2 : wa <= 4 ? 4 : 8;
     const int nb = wb;
 #define LAMQ_RHT_CASE(NA_, NB_) \
-    if (na == NA_ && nb == NB_) return launch_rht<NA_, NB_>(p, s);
+    if (na == NA_ && nb == NB_)                                                                     \
+        return rows < kSplitRows ? launch_rht_split<NA_, NB_>(p, s) : launch_rht<NA_, NB_>(p, s);
 #define LAMQ_RHT_ROW(NA_) \
     LAMQ_RHT_CASE(NA_, 1) LAMQ_RHT_CASE(NA_, 2) LAMQ_RHT_CASE(NA_, 3) LAMQ_RHT_CASE(NA_, 4) \
     LAMQ_RHT_CASE(NA_, 5) LAMQ_RHT_CASE(NA_, 6) LAMQ_RHT_CASE(NA_, 7) LAMQ_RHT_CASE(NA_, 8)

@@ -33,3 +33,19 @@ def test_conjugation(n):
     got = Rotation(n, 11, "cuda").conj(torch.as_tensor(H).cuda()).cpu().numpy()
     ref = R @ H @ R.T
     assert np.abs(got - ref).max() < 1e-12 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("n", [64, 200, 960, 2560, 4096, 9728])
+def test_few_rows_equal_the_one_row_per_cta_form(n):
+    """Fewer than 128 rows take the split form (many CTAs per row, two launches); its results equal those of the
+    one-CTA-per-row form bit for bit, both directions, out of place and in place."""
+    from lookatmyquant_b200.rotation import Rotation
+    rot = Rotation(n, 17, "cuda")
+    M = torch.randn(160, n, dtype=torch.float64, generator=torch.Generator().manual_seed(n)).cuda()
+    for run in (rot.rows, rot.rows_t):
+        whole = run(M)  # 160 rows: one CTA per row
+        for k in (1, 5, 127):
+            assert torch.equal(run(M[:k]), whole[:k])
+            inplace = M[:k].clone()
+            run(inplace, out=inplace)
+            assert torch.equal(inplace, whole[:k])
