@@ -191,8 +191,26 @@ __device__ __forceinline__ void load_table(float *tab, const float *__restrict__
     }
 }
 
+// The three stream words that hold the states of columns jb .. jb + 7 of rows r0 .. r0 + kRowsPerCta − 1 (rows past
+// the end repeat the last row; words past the row's end read as zero), and the bit offset of column jb + 7's state in
+// the first word: column jb + i has its state at bit (N − 1 − jb − i)·K, (7 − i)·K above that of column jb + 7.
+template <int K>
+__device__ __forceinline__ void load_words(const uint32_t *__restrict__ codes, int64_t rows, int wpr, int N,
+                                           int64_t r0, int jb, uint32_t (&wv)[kRowsPerCta][3], int &sh0) {
+    const int64_t bp = (int64_t)(N - 1 - (jb + 7)) * K;
+    const int64_t w0 = bp >> 5;
+    sh0 = (int)(bp & 31);
+#pragma unroll
+    for (int a = 0; a < kRowsPerCta; ++a) {
+        const uint32_t *row = codes + min(r0 + a, rows - 1) * wpr;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) wv[a][q] = (w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
+    }
+}
+
 // The product for symbol widths K = 1..4, a lane owning 8 consecutive columns: their 8 states lie within
-// 7K + L <= 40 bits of the row's stream, so three words loaded once give all 8 (two selects and a funnel shift each),
+// 7K + L <= 40 bits of the row's stream, so three words loaded once give all 8 (a 64-bit window, then a funnel shift
+// by a constant each),
 // and the 8 input values arrive as two float4 loads per vector. The CTA's 8 warps take the 256-column blocks of rows
 // r0 .. r0 + kRowsPerCta − 1 in turn, and their partial sums are added in a fixed order through shared memory, so a
 // row's result does not depend on which launch or CTA computed it. Every thread of the CTA calls this; it ends with
@@ -214,43 +232,43 @@ __device__ __forceinline__ void product8_rows(const uint32_t *__restrict__ codes
         for (int v = 0; v < NV; ++v) acc[a][v] = 0.f;
     for (int blk = warp; blk < nblk; blk += kProductWarps) {
         const int jb = blk * 256 + lane * 8;  // this lane's first column
-        if (jb >= n) continue;
-        // column jb + i has its state at bit (N − 1 − jb − i)·K, i.e. (7 − i)·K above that of column jb + 7
-        const int64_t bp = (int64_t)(N - 1 - (jb + 7)) * K;
-        const int64_t w0 = bp >> 5;
-        const int sh0 = (int)(bp & 31);
-        uint32_t wv[kRowsPerCta][3];
+        if (jb < n) {
+            uint32_t wv[kRowsPerCta][3];
+            int sh0;
+            load_words<K>(codes, rows, wpr, N, r0, jb, wv, sh0);
+            // bits [sh0, sh0 + 64) of each row's stream: column jb + i's state starts (7 − i)·K <= 28 bits in, and
+            // 28 + L <= 40, so every state is one funnel shift by a constant
+            uint32_t lo[kRowsPerCta], hi[kRowsPerCta];
 #pragma unroll
-        for (int a = 0; a < kRowsPerCta; ++a) {
-            const uint32_t *row = codes + min(r0 + a, rows - 1) * wpr;
-#pragma unroll
-            for (int q = 0; q < 3; ++q) wv[a][q] = (w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
-        }
-        const bool full = xvec && jb + 8 <= n;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float xv[NV][4];
-#pragma unroll
-            for (int v = 0; v < NV; ++v) {
-                const float *xp = x + (int64_t)v * ldx + jb + 4 * h;
-                if (full) {
-                    const float4 t = __ldg(reinterpret_cast<const float4 *>(xp));
-                    xv[v][0] = t.x; xv[v][1] = t.y; xv[v][2] = t.z; xv[v][3] = t.w;
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) xv[v][i] = (jb + 4 * h + i < n) ? __ldg(xp + i) : 0.f;
-                }
+            for (int a = 0; a < kRowsPerCta; ++a) {
+                lo[a] = __funnelshift_r(wv[a][0], wv[a][1], sh0);
+                hi[a] = __funnelshift_r(wv[a][1], wv[a][2], sh0);
             }
+            const bool full = xvec && jb + 8 <= n;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int shift = sh0 + (7 - (4 * h + i)) * K;  // < 32 + 7K + 1, inside the three words
-                const bool up = shift >= 32;
+            for (int h = 0; h < 2; ++h) {
+                float xv[NV][4];
 #pragma unroll
-                for (int a = 0; a < kRowsPerCta; ++a) {
-                    const uint32_t lo = up ? wv[a][1] : wv[a][0], hi = up ? wv[a][2] : wv[a][1];
-                    const float val = tab[__funnelshift_r(lo, hi, shift & 31) & smask];
+                for (int v = 0; v < NV; ++v) {
+                    const float *xp = x + (int64_t)v * ldx + jb + 4 * h;
+                    if (full) {
+                        const float4 t = __ldg(reinterpret_cast<const float4 *>(xp));
+                        xv[v][0] = t.x; xv[v][1] = t.y; xv[v][2] = t.z; xv[v][3] = t.w;
+                    } else {
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) acc[a][v] = fmaf(val, xv[v][i], acc[a][v]);
+                        for (int i = 0; i < 4; ++i) xv[v][i] = (jb + 4 * h + i < n) ? __ldg(xp + i) : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    constexpr int kLast = 7 * K;
+                    const int r = kLast - (4 * h + i) * K;  // a constant after unrolling
+#pragma unroll
+                    for (int a = 0; a < kRowsPerCta; ++a) {
+                        const float val = tab[__funnelshift_r(lo[a], hi[a], r) & smask];
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) acc[a][v] = fmaf(val, xv[v][i], acc[a][v]);
+                    }
                 }
             }
         }
@@ -349,30 +367,49 @@ int grid_for(int64_t work, int threads) {
     return (int)std::min<int64_t>((work + threads - 1) / threads, 148 * 32);
 }
 
+// The CTAs of a product kernel that are resident together on the whole GPU (registers and shared memory decide how
+// many fit on an SM): the persistent grids are no larger, so no CTA waits for a second wave with a full share of rows.
+int resident_grid(const void *kernel) {
+    int dev = 0, sms = 148, per = 1;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, kProductWarps * 32, 0) != cudaSuccess || per < 1)
+        per = 1;
+    return sms * per;
+}
+
+template <int NV, int K>
+void launch_product8(int64_t units, const uint32_t *codes, int64_t rows, int n, int L, const float *scales,
+                     const float *table, const uint32_t *map, const float *x, int64_t ldx, int xvec, float *y,
+                     int64_t ldy, cudaStream_t s) {
+    const int grid = (int)std::min<int64_t>(units, resident_grid((const void *)trellis_product8_kernel<NV, K>));
+    trellis_product8_kernel<NV, K><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map, x, ldx,
+                                                                       xvec, y, ldy);
+}
+
 template <int NV>
 void launch_product(const uint32_t *codes, int64_t rows, int n, int k, int L, const float *scales, const float *table,
                     const uint32_t *map, const float *x, int64_t ldx, float *y, int64_t ldy, cudaStream_t s) {
-    const int64_t groups = (rows + kRowsPerCta - 1) / kRowsPerCta;
-    const int grid = (int)std::min<int64_t>(groups, 148 * 6);
+    const int64_t units = (rows + kRowsPerCta - 1) / kRowsPerCta;
     const int xvec = ((uintptr_t)x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;
     switch (k) {  // the widths of the trellis codes; wider symbols take the general kernel
-        case 1: trellis_product8_kernel<NV, 1><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
-                                                                                  x, ldx, xvec, y, ldy); break;
-        case 2: trellis_product8_kernel<NV, 2><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
-                                                                                  x, ldx, xvec, y, ldy); break;
-        case 3: trellis_product8_kernel<NV, 3><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
-                                                                                  x, ldx, xvec, y, ldy); break;
-        case 4: trellis_product8_kernel<NV, 4><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, L, scales, table, map,
-                                                                                  x, ldx, xvec, y, ldy); break;
-        default:
+        case 1: launch_product8<NV, 1>(units, codes, rows, n, L, scales, table, map, x, ldx, xvec, y, ldy, s); break;
+        case 2: launch_product8<NV, 2>(units, codes, rows, n, L, scales, table, map, x, ldx, xvec, y, ldy, s); break;
+        case 3: launch_product8<NV, 3>(units, codes, rows, n, L, scales, table, map, x, ldx, xvec, y, ldy, s); break;
+        case 4: launch_product8<NV, 4>(units, codes, rows, n, L, scales, table, map, x, ldx, xvec, y, ldy, s); break;
+        default: {
+            const int grid = (int)std::min<int64_t>(units, 148 * 6);
             trellis_product_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(codes, rows, n, k, L, scales, table, map, x,
                                                                            ldx, y, ldy);
+        }
     }
 }
 
 template <int NV>
 void launch_groups(const ProductGroups &p, int n, const float *x, int64_t ldx, int xvec, cudaStream_t s) {
-    const int grid = (int)std::min<int64_t>(p.first[p.ng], 148 * 6);
+    const int grid =
+        (int)std::min<int64_t>(p.first[p.ng], resident_grid((const void *)trellis_product_groups_kernel<NV>));
     trellis_product_groups_kernel<NV><<<grid, kProductWarps * 32, 0, s>>>(p, n, x, ldx, xvec);
 }
 
