@@ -101,3 +101,66 @@ def test_scalar_ldlq_rejects_blocks_over_128():
     from lookatmyquant_b200.ldlq_gpu import ldlq_round
     with pytest.raises(ValueError, match="block"):
         ldlq_round(torch.zeros(2, 4), torch.eye(4), torch.tensor([0.0, 1.0]), block=256)
+
+
+@pytest.mark.parametrize("width", [1, 4])
+def test_generic_sweep_refit_is_least_squares(width):
+    """As the reference's test_frame.py:51-62 and test_codes.py:64-75: just before a block is settled, the sweep's
+    running values of the unsettled columns are the least-squares best continuation of the settled ones,
+    X_r = W_r + (W_s − Q_s)·H_sr·H_rr⁻¹, with H the damped statistics whose inverse the environment's U factors."""
+    from lookatmyquant_b200 import syntax
+    from oracle import core as O
+    rng = np.random.default_rng(3)
+    n, rows = 16, 5
+    A = rng.standard_normal((64, n))
+    U, dead, Hd = O.environment(A.T @ A / 64)
+    W = rng.standard_normal((rows, n))
+    settled = np.zeros((rows, n))
+
+    def quarter(j, cols, T):
+        q = torch.round(cols * 4) / 4
+        settled[:, j:j + width] = q.reshape(rows, width).numpy()
+        return q
+    before = syntax.sweep(torch.as_tensor(W), _Env(torch.as_tensor(U), torch.as_tensor(dead)), quarter, width=width,
+                          lazy=8).numpy()
+    for j in range(0, n, width):
+        s, r = slice(0, j), slice(j, n)
+        best = W[:, r] + (W[:, s] - settled[:, s]) @ Hd[s, r] @ np.linalg.inv(Hd[r, r])
+        assert np.abs(before[:, j:j + width] - best[:, :width]).max() < 1e-10
+
+
+def test_generic_sweep_rows_do_not_interact():
+    """As the reference's test_codes.py:87-99: under Refit the rows are independent, so sweeping a stacked matrix
+    equals sweeping its halves apart — the property that lets the rows of a stage be split across GPUs."""
+    from lookatmyquant_b200 import syntax
+    from oracle import core as O
+    rng = np.random.default_rng(4)
+    n = 24
+    A = rng.standard_normal((96, n))
+    U, dead, _ = O.environment(A.T @ A / 96)
+    env = _Env(torch.as_tensor(U), torch.as_tensor(dead))
+    W = torch.as_tensor(rng.standard_normal((7, n)))
+
+    def half(j, cols, T):
+        return torch.round(cols * 2) / 2
+    whole = syntax.sweep(W, env, half, width=4, lazy=8)
+    parts = torch.cat([syntax.sweep(W[:3], env, half, width=4, lazy=8), syntax.sweep(W[3:], env, half, width=4,
+                                                                                       lazy=8)])
+    assert torch.allclose(whole, parts, rtol=0, atol=1e-12)
+
+
+def test_shipped_two_bit_trellis_beats_scalar_on_gaussians():
+    """As the reference's test_codes.py:134-144 (2 bits per weight on unit Gaussians: the 4-level Lloyd-Max scalar
+    quantizer has distortion ≈ 0.1175, a trellis code beats it by more than 0.01), for the shipped 4096-state k = 2
+    table that the B200 sweep uses, decoded by the oracle's Viterbi (the GPU decoder's states equal it bit for bit)."""
+    from lookatmyquant_b200 import codes
+    from oracle import core as O
+    X = np.random.default_rng(5).standard_normal((48, 256))
+    levels = np.array([-1.510, -0.4528, 0.4528, 1.510])  # the Lloyd-Max quantizer of N(0, 1) at 2 bits
+    scalar = np.mean(np.min((X[..., None] - levels) ** 2, axis=-1))
+    assert abs(scalar - 0.1175) < 0.005
+    values = codes.trellis_values(12, 2, 256).numpy()
+    states = O.viterbi(X, values, 12, 2)
+    assert O.is_trellis_path(states, 12, 2)
+    trellis = np.mean((X - values.astype(np.float32)[states]) ** 2)
+    assert trellis < scalar - 0.01
