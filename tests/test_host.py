@@ -164,3 +164,20 @@ def test_shipped_two_bit_trellis_beats_scalar_on_gaussians():
     assert O.is_trellis_path(states, 12, 2)
     trellis = np.mean((X - values.astype(np.float32)[states]) ** 2)
     assert trellis < scalar - 0.01
+
+
+def test_column_trellis_layout_and_price():
+    """As the reference's test_codes.py:120-131: a column trellis cuts each column into sequences of T consecutive
+    outputs (its W.reshape(o/T, T, w).permute(0, 2, 1) layout), and a word whose sequences start anywhere pays L − k
+    bits per sequence on top of k per entry (plus 16 per row scale and one sign per rotated input, as our words
+    carry both)."""
+    from lookatmyquant_b200 import codes
+    code = codes.TrellisCode(12, 2, 256)
+    W = torch.randn(512, 8, dtype=torch.float64)
+    assert torch.equal(code._seqs(W), W.reshape(2, 256, 8).permute(0, 2, 1).reshape(-1, 256))
+    m, n, T = 512, 8, 256
+    word = codes.TrellisWord(torch.zeros(m, n, dtype=torch.int16), torch.ones(m), torch.zeros(m, n), code.values, 12,
+                             2, None, None, fixed_start=False, T=T)
+    assert word.rate_bits() == m * n * 2 + 16 * m + (m * n // T) * (12 - 2)
+    word.fixed_start = True
+    assert word.rate_bits() == m * n * 2 + 16 * m
