@@ -139,12 +139,13 @@ def _per_group(prod, xr):
     return y
 
 
+@pytest.mark.parametrize("n", [284, 4352])
 @pytest.mark.parametrize("nvec", [1, 5, 21])
-def test_grouped_product_equals_per_group_launches(nvec):
+def test_grouped_product_equals_per_group_launches(nvec, n):
     """lamq_trellis_product_groups over a stage (three matrices, 1-4-bit groups and a 6-bit one, 39 row groups: two
-    launches of at most 32) gives every row exactly the per-group kernel's value, for aligned and unaligned inputs."""
+    launches of at most 32) gives every row exactly the per-group kernel's value, for aligned and unaligned inputs.
+    n = 284: two 256-column blocks, the last one ragged (n is 4 mod 8); n = 4352: 17 blocks, so warps take several."""
     from lookatmyquant_b200 import artifact as A
-    n = 284  # two column blocks, the last one ragged (n is 4 mod 8); R_in of order 284 is one Paley factor
     prods = [_random_product(300, n, [1, 2, 3, 4] * 3, 11), _random_product(77, n, [2, 4, 6], 12, "v"),
              _random_product(130, n, [4, 3, 2, 1] * 6, 13, "u")]
     gen = torch.Generator().manual_seed(nvec)
@@ -169,3 +170,20 @@ def test_grouped_product_skips_empty_groups():
     arr = (_lib.ProductGroup * 4)(empty, g0, empty, g1)
     check(_lib.load().lamq_trellis_product_groups(arr, 4, 64, ptr(xr), 64, 2, stream_ptr()), "groups")
     assert torch.equal(y, _per_group(p, xr))
+
+
+@pytest.mark.parametrize("n", [284, 4352])
+def test_grouped_product_matches_decoded_rows(n):
+    """The grouped product against the decoded rows (decode_rotated, another kernel) times the input in fp64, for
+    short rows and for rows whose column blocks outnumber the CTA's warps."""
+    from lookatmyquant_b200 import artifact as A
+    prod = _random_product(96, n, [1, 2, 3, 4], 21)
+    tensors = {}
+    for g, codes, rows, scales, table in prod.groups:
+        tensors.update({g["key"] + ".codes": codes, g["key"] + ".rows": rows, g["key"] + ".scales": scales,
+                        g["key"] + ".table": table})
+    Wd = A.decode_rotated(tensors, prod.meta).double()
+    xr = torch.randn(5, n, generator=torch.Generator().manual_seed(n)).float().cuda()
+    y = A.product_rotated([prod], xr)[0].double()
+    ref = xr.double() @ Wd.T
+    assert (y - ref).abs().max() <= 1e-5 * ref.abs().max()
