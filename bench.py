@@ -165,15 +165,8 @@ class Config1:
         return sweep_roofline(kms, algo_bytes, edges, pk)
 
     def cpu_sample(self, threads):
-        """The oracle on the first 256 rows (a tenth of the matrix; rows are independent, so time scales with rows)."""
-        from oracle import core as O
-        O.set_threads(threads)
-        rows = 256
-        W = self.W_host[:rows].numpy()
-        t0 = time.perf_counter()
-        O.ldlq_row_words(W, self.H_host.numpy(), self.code.values.numpy(), 12, 2, self.in_seed)
-        dt = time.perf_counter() - t0
-        return dt * self.m / rows, f"oracle ldlq_row_words on 256 of 2560 rows, scaled x{self.m / rows:g}"
+        return config1_cpu_sample(threads, self.W_host.numpy(), self.H_host.numpy(), self.in_seed,
+                                  self.code.values.numpy())
 
 
 class Config3:
@@ -330,15 +323,85 @@ class Config3:
         return config3_cpu_sample(threads, self.tokens)
 
 
+_ROTATIONS = {}
+GROUPS_PER_MATRIX = 4  # ldlq_words calls per matrix under a 1-4-bit row plan: one per width (quantize.py:530-565)
+
+
+def _dense_rotation(n, seed=301):
+    """The reference's dense rht(n) (codes.py:129-132) from the oracle, formed once per width outside timed work."""
+    from oracle import core as O
+    if (n, seed) not in _ROTATIONS:
+        _ROTATIONS[(n, seed)] = O.rht(n, seed)
+    return _ROTATIONS[(n, seed)]
+
+
+def _words_seconds(W, R, U, dead, values):
+    """Seconds of the reference's per-row word work (ldlq_words, codes.py:425-462) on the oracle for the rows of W:
+    X = W·R_inᵀ, the row scales, the sweep (a Viterbi per block, the refit) and W_q = (S⊙V)·R_in. The sample's matrix
+    products are small, so BLAS keeps one thread and the OpenMP Viterbi the cores (two thread pools spinning against
+    each other made small samples several times slower than their rows' share of a full call)."""
+    from threadpoolctl import threadpool_limits
+    from oracle import core as O
+    with threadpool_limits(limits=1, user_api="blas"):
+        t0 = time.perf_counter()
+        X = W @ R.T
+        S = O.row_scale(X)
+        _, settled, _ = O.row_trellis_sweep(X, S, U, dead, values, 12, 2)
+        (settled * S[:, None]) @ R
+        return time.perf_counter() - t0
+
+
+def words_fit(W, R, U, dead, values, r1=16, r2=128):
+    """(seconds per call, seconds per row) of the word work at W's width: a line through its times on the first r1
+    and r2 rows of W (a call's cost is one part per block of columns, whatever its rows, plus one part per row).
+    Times out of order (noise) give the larger sample's time per row and nothing per call."""
+    t1 = _words_seconds(W[:r1], R, U, dead, values)
+    t2 = _words_seconds(W[:r2], R, U, dead, values)
+    if t2 <= t1:
+        return 0.0, t2 / r2
+    per_row = (t2 - t1) / (r2 - r1)
+    return max(t1 - per_row * r1, 0.0), per_row
+
+
+def _warm_oracle(values):
+    """Loads the oracle's C Viterbi (and builds it if needed) before anything is timed."""
+    from oracle import core as O
+    O.viterbi(np.zeros((1, 2)), values, 12, 2)
+
+
+def config1_cpu_sample(threads, W, H, in_seed, values):
+    """The reference's path for one word (config 1) on the oracle: R·H·Rᵀ and the environment once (all threads),
+    then the word work of one call over all of W's rows, from its line fitted on 64 and 512 rows."""
+    from oracle import core as O
+    O.set_threads(threads)
+    _warm_oracle(values)
+    R = _dense_rotation(W.shape[1], in_seed)
+    t0 = time.perf_counter()
+    U, dead, _ = O.environment(R @ H @ R.T)
+    t_fix = time.perf_counter() - t0
+    per_call, per_row = words_fit(W, R, U, dead, values, 64, 512)
+    t_w = per_call + per_row * W.shape[0]
+    return t_fix + t_w, (f"oracle on {threads} host threads: R·H·Rᵀ + environment ({t_fix:.2f} s), then the word's "
+                         f"sweep fitted on 64 and 512 of {W.shape[0]} rows: {per_call:.2f} s per call + "
+                         f"{per_row * 1e3:.1f} ms per row ({t_w:.0f} s)")
+
+
 def config3_cpu_sample(threads, tokens=384 * 2048, stages=None):
-    """The reference's CPU path (the oracle port) on a bounded sample, extrapolated to one layer: the fp32 Hessian/QEP
-    GEMMs on 8192 tokens at d = 2560 (scaled by tokens and by d² over every stage's H and D), the fp64 environment and
-    QEP solve at n = 2560 (scaled by n³ per stage), and row-trellis words on 64 rows per stage (scaled by rows)."""
+    """The reference's CPU path (the oracle port) on a bounded sample, extrapolated to one layer:
+    - the fp32 Hessian/QEP GEMMs on 8192 tokens at d = 2560, scaled by tokens and by d² over every stage's H and D;
+    - the work per stage that does not depend on its rows (R·H·Rᵀ, the environment, the QEP solve) at n = 2560,
+      scaled by n³ per stage, once per stage (the reference repeats it for every row group: a lower bound);
+    - the word work per width: seconds per call and per row fitted on 16 and 128 rows (words_fit), then
+      GROUPS_PER_MATRIX calls per matrix plus the stage's rows. The sweep's cost does not depend on U's values, so an
+      identity U stands in for the stage's.
+    The dense rotations are formed once per width, outside the timed work."""
     from lookatmyquant_b200.layer import qwen3_4b_stages
     from lookatmyquant_b200.workloads import stage_activations, token_weights
     from oracle import core as O
     O.set_threads(threads)
     torch.set_num_threads(threads)
+    values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
+    _warm_oracle(values)
     stages = stages or qwen3_4b_stages()
     x, xr = (t.float().numpy() for t in stage_activations(8192, 2560, seed=3000, device="cpu"))
     w = token_weights(8192, seed=7, device="cpu").numpy()
@@ -346,26 +409,27 @@ def config3_cpu_sample(threads, tokens=384 * 2048, stages=None):
     O.hessian_accumulate([x], [w], [xr])
     t_h = time.perf_counter() - t0
     h_total = t_h * (tokens / 8192) * sum((s.d / 2560) ** 2 for s in stages)
-    A = np.random.default_rng(0).standard_normal((4096, 2560))
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((4096, 2560))
     Hs = A.T @ A / 4096
+    R = _dense_rotation(2560)
     t0 = time.perf_counter()
-    O.environment(Hs)
+    O.environment(R @ Hs @ R.T)
     O.cross_target(Hs, 0.01 * Hs, 0.5)
     t_e = time.perf_counter() - t0
     e_total = t_e * sum((s.d / 2560) ** 3 for s in stages)
-    values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
-    t_w = 0.0
-    rng = np.random.default_rng(1)
-    for s in stages:
-        Wt = 0.02 * rng.standard_normal((64, s.d))
-        Hd = np.diag(np.exp(rng.standard_normal(s.d))) + np.eye(s.d)
-        t0 = time.perf_counter()
-        O.ldlq_row_words(Wt, Hd, values, 12, 2, 301)
-        t_w += (time.perf_counter() - t0) * sum(r for _, r in s.matrices) / 64
+    fits = {}
+    for d in sorted({s.d for s in stages}):
+        W = 0.02 * rng.standard_normal((128, d))
+        fits[d] = words_fit(W, _dense_rotation(d), np.eye(d), np.zeros(d, dtype=bool), values)
+    t_w = sum(GROUPS_PER_MATRIX * len(s.matrices) * fits[s.d][0] + sum(r for _, r in s.matrices) * fits[s.d][1]
+              for s in stages)
+    per_row = ", ".join(f"d={d}: {a:.2f} s/call + {b * 1e3:.1f} ms/row" for d, (a, b) in fits.items())
     v = h_total + e_total + t_w
     return v, (f"oracle on {threads} host threads, extrapolated to one layer: H/D fp32 GEMMs on 8192 of {tokens} "
-               f"tokens ({h_total:.0f} s), environment + QEP solve at n=2560 scaled by n^3 ({e_total:.0f} s), "
-               f"row-trellis words on 64 rows per stage scaled by rows ({t_w:.0f} s)")
+               f"tokens ({h_total:.0f} s), R·H·Rᵀ + environment + QEP solve at n=2560 scaled by n^3 per stage "
+               f"({e_total:.0f} s), row-trellis words fitted on 16 and 128 rows per width ({per_row}) over "
+               f"{GROUPS_PER_MATRIX} calls per matrix and the layer's rows ({t_w:.0f} s)")
 
 
 WORKLOADS = {"config1": Config1, "config3": Config3}
@@ -421,14 +485,9 @@ def run_reference(args):
             v, sample = config3_cpu_sample(threads)
         else:
             from lookatmyquant_b200.workloads import config1
-            from oracle import core as O
-            O.set_threads(threads)
             W, H, seed, in_seed = config1()
             values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
-            t0 = time.perf_counter()
-            O.ldlq_row_words(W[:256].numpy(), H.numpy(), values, 12, 2, in_seed)
-            v = (time.perf_counter() - t0) * W.shape[0] / 256
-            sample = f"oracle ldlq_row_words on 256 of 2560 rows per step, scaled x{W.shape[0] / 256:g}"
+            v, sample = config1_cpu_sample(threads, W.numpy(), H.numpy(), in_seed, values)
         if i >= args.warmup:
             times.append(v)
     v = statistics.mean(times)
