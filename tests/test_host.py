@@ -181,3 +181,16 @@ def test_column_trellis_layout_and_price():
     assert word.rate_bits() == m * n * 2 + 16 * m + (m * n // T) * (12 - 2)
     word.fixed_start = True
     assert word.rate_bits() == m * n * 2 + 16 * m
+
+
+def test_cpu_baseline_fit_separates_call_and_row_costs(monkeypatch):
+    """The CPU baseline's word timing: a line through two sample sizes gives the cost per call and per row, so a
+    small sample's fixed cost is not multiplied by the layer's rows; times out of order fall back to the larger
+    sample's time per row."""
+    import bench
+    times = {16: 1.0 + 16 * 0.01, 128: 1.0 + 128 * 0.01}
+    monkeypatch.setattr(bench, "_words_seconds", lambda W, *a: times[W.shape[0]])
+    per_call, per_row = bench.words_fit(np.zeros((128, 8)), None, None, None, None)
+    assert abs(per_call - 1.0) < 1e-9 and abs(per_row - 0.01) < 1e-12
+    times[128] = 0.9  # noise: the larger sample ran faster
+    assert bench.words_fit(np.zeros((128, 8)), None, None, None, None) == (0.0, 0.9 / 128)
