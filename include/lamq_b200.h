@@ -17,6 +17,7 @@
  *   lamq_rht_rows,         opgraph/codes.py:97-132    rht(n, seed) applied as X = W·R_inᵀ (:430), Hr = R_in·H·R_inᵀ
  *   lamq_transpose_f64                                (:439) and W_q = (S⊙V)·R_in, without forming R
  *   lamq_env_factor        opgraph/frame.py:515-522   Environment(H, damp): dead inputs, damping, U
+ *   lamq_proxy_loss        quantize.py:1320-1325      best_word's error (E @ H * E).sum(), E = word − target
  *   lamq_cholesky_inverse_lower, lamq_ridge, lamq_dgemm, lamq_cross_apply
  *                          quantize.py:1330-1335      cross_target: M = I + α·(solve(H + λ·mean(diag H)·I, Dᵀ))ᵀ
  *                          quantize.py:1503           target = W @ M
@@ -64,7 +65,9 @@ uint64_t lamq_kernel_launches(void);
  * states: rows x T int64 out. Supported: L = 12, k in 1..4, T >= 1.
  * Each row's costs are fp32 and rounded exactly as the reference's tensor ops; ties go to the smallest predecessor and
  * the smallest final state, so the states are identical to the reference's.
- * workspace: lamq_viterbi_workspace_size(rows, T, L, k) bytes of device memory (the back-pointers).
+ * workspace: lamq_viterbi_workspace_size(rows, T, L, k) bytes of device memory (the back-pointers); 0 when the call
+ * needs none (T <= 32, or longer sequences whose warp-pair decoder keeps its back-pointers in shared memory on the
+ * current device). Shapes whose back-pointers would overflow a size_t are rejected with LAMQ_ERR_INVALID.
  */
 size_t lamq_viterbi_workspace_size(int64_t rows, int T, int L, int k);
 int lamq_viterbi(const float *X, int64_t rows, int T, const float *values, int L, int k, const int64_t *start,
@@ -204,6 +207,18 @@ int lamq_transpose_f64(const double *in, int64_t ldi, double *out, int64_t ldo, 
  */
 int lamq_dgemm(int transB, int M, int N, int K, double alpha, const double *A, int64_t lda, const double *B,
                int64_t ldb, double beta, double *C, int64_t ldc, lamq_stream_t stream);
+
+/*
+ * The proxy loss of quantize.py:1320-1325 (best_word: E = net.matrix() − target, err = (E @ H * E).sum()):
+ * row_loss[r] = Σ_ij E[r][i]·H[i][j]·E[r][j] for E = Wq − W (W NULL: E = Wq), and *total = Σ_r row_loss[r] summed in a
+ * fixed order (deterministic). All fp64, rows x n row-major; E·H runs on the fp64 tensor cores in blocks of 4096
+ * rows. row_loss may be NULL. Workspace: lamq_proxy_loss_workspace_size(rows, n). With rows or n zero the loss is 0
+ * and the call returns LAMQ_OK without touching the device (nothing is written to *total).
+ */
+size_t lamq_proxy_loss_workspace_size(int64_t rows, int n);
+int lamq_proxy_loss(const double *Wq, int64_t ldq, const double *W, int64_t ldw, int64_t rows, int n, const double *H,
+                    int64_t ldh, double *row_loss, double *total, void *workspace, size_t workspace_bytes,
+                    lamq_stream_t stream);
 
 /* Workspace bytes for lamq_env_factor and lamq_cholesky_inverse_lower of order n. */
 size_t lamq_factor_workspace_size(int n);

@@ -44,6 +44,8 @@ SIGNATURES = {
     "lamq_ridge": (_I32, [_P, _I64, _P, _I64, _I32, _D, _P]),
     "lamq_cross_apply_workspace_size": (_SZ, [_I32, _I32]),
     "lamq_cross_apply": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P, _I64, _D, _P, _I64, _P, _SZ, _P]),
+    "lamq_proxy_loss_workspace_size": (_SZ, [_I64, _I32]),
+    "lamq_proxy_loss": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _SZ, _P]),
     "lamq_trellis_words_per_row": (_I64, [_I32, _I32]),
     "lamq_kl_workspace_size": (_SZ, [_I64]),
     "lamq_kl_reference": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _SZ, _P, _P]),

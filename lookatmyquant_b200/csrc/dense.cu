@@ -17,6 +17,7 @@
 // (L22, X22) = rec(A22), X21 = −X22·(L21·X11) — 0.58n³ multiply-adds in large GEMMs; 128 x 128 leaves are factored
 // and inverted by one CTA, the block held in registers (right-looking, one barrier per column).
 #include <algorithm>
+#include <climits>
 #include <vector>
 
 #include "lamq_common.cuh"
@@ -515,6 +516,43 @@ __global__ void ridge_diag_kernel(double *A, int64_t lda, int n, double lam) {
     for (int i = threadIdx.x; i < n; i += blockDim.x) A[(int64_t)i * lda + i] += add;
 }
 
+// E = A − B (B may be null: E = A), rows x n, into a dense buffer.
+__global__ void diff_kernel(const double *A, int64_t lda, const double *B, int64_t ldb, double *E, int rows, int n) {
+    const int64_t total = (int64_t)rows * n;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = e / n, j = e % n;
+        E[e] = B ? A[r * lda + j] - B[r * ldb + j] : A[r * lda + j];
+    }
+}
+
+// loss[r] = Σ_j P[r][j]·E[r][j] (P = E·H): one warp per row, lanes strided over j, then a fixed shuffle tree.
+__global__ void row_dot_kernel(const double *P, const double *E, int rows, int n, double *loss) {
+    const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const double *p = P + (int64_t)warp * n, *e = E + (int64_t)warp * n;
+    double acc = 0.0;
+    for (int j = lane; j < n; j += 32) acc = fma(p[j], e[j], acc);
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+    if (lane == 0) loss[warp] = acc;
+}
+
+// total = Σ_r loss[r] in a fixed order (one CTA: strided partial sums, then a tree), so repeated calls agree bit
+// for bit.
+__global__ void sum_rows_kernel(const double *loss, int64_t rows, double *total) {
+    __shared__ double red[256];
+    double acc = 0.0;
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) acc += loss[r];
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+        if ((int)threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *total = red[0];
+}
+
+constexpr int kProxyRowBlock = 4096;  // rows per E·H product (bounds the workspace)
+
 int grid_for(int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, 148 * 16); }
 
 template <class T>
@@ -706,5 +744,41 @@ extern "C" int lamq_ridge(const double *H, int64_t ldh, double *A, int64_t lda, 
     LAMQ_CHECK_LAUNCH("lamq_ridge copy");
     ridge_diag_kernel<<<1, 1024, 0, s>>>(A, lda, n, lam);
     LAMQ_CHECK_LAUNCH("lamq_ridge");
+    return LAMQ_OK;
+}
+
+extern "C" size_t lamq_proxy_loss_workspace_size(int64_t rows, int n) {
+    if (rows <= 0 || n <= 0) return 0;
+    const size_t rb = (size_t)std::min<int64_t>(rows, kProxyRowBlock);
+    return (2 * rb * (size_t)n + (size_t)rows) * sizeof(double);
+}
+
+extern "C" int lamq_proxy_loss(const double *Wq, int64_t ldq, const double *W, int64_t ldw, int64_t rows, int n,
+                               const double *H, int64_t ldh, double *row_loss, double *total, void *workspace,
+                               size_t workspace_bytes, lamq_stream_t stream) {
+    LAMQ_REQUIRE(rows >= 0 && n >= 0 && ldq >= n && ldh >= n && (W == nullptr || ldw >= n),
+                 "lamq_proxy_loss: bad shape");
+    LAMQ_REQUIRE(rows <= INT_MAX, "lamq_proxy_loss: %lld rows exceed the product's range", (long long)rows);
+    LAMQ_REQUIRE(total != nullptr, "lamq_proxy_loss: null pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (rows == 0 || n == 0) return LAMQ_OK;  // the loss of an empty word is 0; nothing is written
+    LAMQ_REQUIRE(Wq && H && workspace, "lamq_proxy_loss: null pointer");
+    LAMQ_REQUIRE(workspace_bytes >= lamq_proxy_loss_workspace_size(rows, n), "lamq_proxy_loss: workspace too small");
+    const int64_t rb = std::min<int64_t>(rows, kProxyRowBlock);
+    double *E = reinterpret_cast<double *>(workspace);
+    double *P = E + (size_t)rb * n;
+    double *loss = row_loss ? row_loss : P + (size_t)rb * n;
+    for (int64_t r0 = 0; r0 < rows; r0 += rb) {
+        const int m = (int)std::min<int64_t>(rb, rows - r0);
+        diff_kernel<<<grid_for((int64_t)m * n), 256, 0, s>>>(Wq + r0 * ldq, ldq, W ? W + r0 * ldw : nullptr, ldw, E,
+                                                            m, n);
+        LAMQ_CHECK_LAUNCH("lamq_proxy_loss difference");
+        const int st = dgemm(s, 0, m, n, n, 1.0, E, n, H, ldh, 0.0, P, n);
+        if (st) return st;
+        row_dot_kernel<<<(m + 7) / 8, 256, 0, s>>>(P, E, m, n, loss + r0);
+        LAMQ_CHECK_LAUNCH("lamq_proxy_loss rows");
+    }
+    sum_rows_kernel<<<1, 256, 0, s>>>(loss, rows, total);
+    LAMQ_CHECK_LAUNCH("lamq_proxy_loss total");
     return LAMQ_OK;
 }

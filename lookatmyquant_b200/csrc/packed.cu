@@ -469,6 +469,9 @@ extern "C" int lamq_trellis_product(const uint32_t *codes, int64_t rows, int n, 
     LAMQ_REQUIRE(nvec >= 0 && ldx >= n, "lamq_trellis_product: bad vector shape");
     if (rows == 0 || nvec == 0) return LAMQ_OK;
     LAMQ_REQUIRE(codes && scales && table && x && y, "lamq_trellis_product: null pointer");
+    // each vector's output row holds every group row (map or not): shorter rows would overlap the next vector's
+    LAMQ_REQUIRE(nvec <= 1 || ldy >= rows, "lamq_trellis_product: ldy %lld below the group's %lld rows",
+                 (long long)ldy, (long long)rows);
     cudaStream_t s = (cudaStream_t)stream;
     for (int v = 0; v < nvec;) {
         const int left = nvec - v;
@@ -499,6 +502,9 @@ extern "C" int lamq_trellis_product_groups(const lamq_product_group *groups, int
                      g.L);
         LAMQ_REQUIRE(g.rows == 0 || (g.codes && g.scales && g.table && g.y),
                      "lamq_trellis_product_groups: group %d: null pointer", i);
+        LAMQ_REQUIRE(nvec <= 1 || g.ldy >= g.rows,
+                     "lamq_trellis_product_groups: group %d: ldy %lld below its %lld rows", i, (long long)g.ldy,
+                     (long long)g.rows);
     }
     cudaStream_t s = (cudaStream_t)stream;
     const int xvec = ((uintptr_t)x % 16 == 0 && ldx % 4 == 0) ? 1 : 0;

@@ -7,6 +7,8 @@
 // them per block) are decoded by a warp pair each (trellis_pair.cuh: half the states per thread, one back-pointer
 // word per thread per step, all of them in shared memory), two sequences per CTA, unless their back-pointers do not
 // fit; then one warp per sequence keeps them in the caller's workspace (256 bytes per entry per row).
+#include <climits>
+#include <cstdint>
 #include <mutex>
 
 #include "lamq_common.cuh"
@@ -179,11 +181,54 @@ bool launch_pair_long(const VitParams &p, int k, cudaStream_t stream, int *rc) {
 
 using namespace lamq;
 
+namespace lamq {
+namespace {
+
+// Back-pointer bytes of the one-warp kernel for sequences longer than kShortT (32 words of 8 bytes per entry), or
+// SIZE_MAX when rows x T x 256 does not fit a size_t.
+size_t backptr_bytes(int64_t rows, int T) {
+    if (rows <= 0 || T <= kShortT) return 0;
+    const size_t per_row = (size_t)T * 32 * sizeof(unsigned long long);
+    if ((size_t)rows > SIZE_MAX / per_row) return SIZE_MAX;
+    return (size_t)rows * per_row;
+}
+
+// Whether the warp-pair decoder takes sequences of T entries on the current device (its back-pointers then live in
+// shared memory and no workspace is read).
+bool pair_long_fits(int T, int k) {
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
+    return pair_long_bytes(T, k) <= (size_t)optin;
+}
+
+// The one-warp kernel's shared memory: 8 warps x (two best buffers + 32 steps of back-pointers). Raised once per
+// device to the larger of its two sizes, so calls on other host threads never lower it under a pending launch.
+constexpr int kVitSmemMax = kVitWarps * (2 * 2048 * (int)sizeof(float) + kShortT * 32 * 8);
+
+int launch_viterbi_warp(const VitParams &p, int k, cudaStream_t stream, const char *fn) {
+    const size_t per_warp = 2 * 2048 * sizeof(float) + (p.gargs ? 0 : (size_t)kShortT * 32 * 8);
+    const size_t smem = kVitWarps * per_warp;
+    const cudaError_t e = smem_limit_once((const void *)viterbi_kernel, kVitSmemMax);
+    if (e != cudaSuccess) {
+        set_error("%s: %s", fn, cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    const int64_t grid = (p.rows + kVitWarps - 1) / kVitWarps;
+    LAMQ_REQUIRE(grid <= INT_MAX, "%s: %lld sequences exceed the launch grid", fn, (long long)p.rows);
+    viterbi_kernel<<<(unsigned)grid, kVitWarps * 32, smem, stream>>>(p, k);
+    LAMQ_CHECK_LAUNCH(fn);
+    return LAMQ_OK;
+}
+
+}  // namespace
+}  // namespace lamq
+
 extern "C" size_t lamq_viterbi_workspace_size(int64_t rows, int T, int L, int k) {
     (void)L;
-    (void)k;
     if (rows <= 0 || T <= kShortT) return 0;
-    return (size_t)rows * (size_t)T * 32 * sizeof(unsigned long long);
+    if (k >= 1 && k <= 4 && pair_long_fits(T, k)) return 0;  // the pair decoder keeps its back-pointers on chip
+    return backptr_bytes(rows, T);
 }
 
 extern "C" int lamq_viterbi(const float *X, int64_t rows, int T, const float *values, int L, int k,
@@ -194,26 +239,20 @@ extern "C" int lamq_viterbi(const float *X, int64_t rows, int T, const float *va
     LAMQ_REQUIRE(rows >= 0 && T >= 0, "lamq_viterbi: negative shape");
     if (rows == 0 || T == 0) return LAMQ_OK;
     LAMQ_REQUIRE(X && values && states, "lamq_viterbi: null pointer");
-    const size_t need = lamq_viterbi_workspace_size(rows, T, L, k);
+    if (T > kShortT && pair_long_fits(T, k)) {
+        LAMQ_REQUIRE((rows + 1) / 2 <= INT_MAX, "lamq_viterbi: %lld sequences exceed the launch grid", (long long)rows);
+        VitParams p{X, rows, T, values, start, states, nullptr};
+        int rc = LAMQ_OK;
+        if (launch_pair_long(p, k, (cudaStream_t)stream, &rc)) return rc;
+    }
+    const size_t need = backptr_bytes(rows, T);
+    LAMQ_REQUIRE(need != SIZE_MAX, "lamq_viterbi: %lld sequences of %d entries overflow the workspace size",
+                 (long long)rows, T);
     LAMQ_REQUIRE(workspace_bytes >= need && (need == 0 || workspace != nullptr),
                  "lamq_viterbi: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     VitParams p{X, rows, T, values, start, states,
                 need ? reinterpret_cast<unsigned long long *>(workspace) : nullptr};
-    if (T > kShortT) {
-        int rc = LAMQ_OK;
-        if (launch_pair_long(p, k, (cudaStream_t)stream, &rc)) return rc;
-    }
-    const size_t per_warp = 2 * 2048 * sizeof(float) + (need ? 0 : (size_t)kShortT * 32 * 8);
-    const size_t smem = kVitWarps * per_warp;
-    cudaError_t e = cudaFuncSetAttribute(viterbi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-        set_error("lamq_viterbi: %s", cudaGetErrorString(e));
-        return LAMQ_ERR_CUDA;
-    }
-    const int64_t grid = (rows + kVitWarps - 1) / kVitWarps;
-    viterbi_kernel<<<(unsigned)grid, kVitWarps * 32, smem, (cudaStream_t)stream>>>(p, k);
-    LAMQ_CHECK_LAUNCH("lamq_viterbi");
-    return LAMQ_OK;
+    return launch_viterbi_warp(p, k, (cudaStream_t)stream, "lamq_viterbi");
 }
 
 // ----------------------------------------------------------------------------- allocation-free variant
@@ -275,11 +314,13 @@ extern "C" int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const f
     LAMQ_REQUIRE(k >= 1 && k <= 4, "lamq_viterbi_noalloc: k must be 1..4 (got %d)", k);
     LAMQ_REQUIRE(rows >= 0 && T >= 0, "lamq_viterbi_noalloc: negative shape");
     if (rows == 0 || T == 0) return LAMQ_OK;
-    const size_t need = lamq_viterbi_workspace_size(rows, T, L, k);
-    LAMQ_REQUIRE(need <= kNoAllocScratchBytes,
-                 "lamq_viterbi_noalloc: %lld sequences of %d entries need %zu bytes of back-pointers, more than the "
-                 "built-in %zu (rows x T at most %zu for T > 32); use lamq_viterbi with a workspace",
-                 (long long)rows, T, need, kNoAllocScratchBytes, kNoAllocScratchBytes / (32 * 8));
+    // rows x T is bounded before it is multiplied, so the size check below cannot be passed by a wrapped product
+    const size_t max_entries = kNoAllocScratchBytes / (32 * 8);
+    LAMQ_REQUIRE(T <= kShortT || (size_t)rows <= max_entries / (size_t)T,
+                 "lamq_viterbi_noalloc: %lld sequences of %d entries need more back-pointers than the built-in %zu "
+                 "bytes (rows x T at most %zu for T > 32); use lamq_viterbi with a workspace",
+                 (long long)rows, T, kNoAllocScratchBytes, max_entries);
+    const size_t need = backptr_bytes(rows, T);
     LAMQ_REQUIRE(X && values && states, "lamq_viterbi_noalloc: null pointer");
     unsigned long long *scratch = nullptr;
     if (need != 0) {
@@ -287,15 +328,5 @@ extern "C" int lamq_viterbi_noalloc(const float *X, int64_t rows, int T, const f
         if (st != LAMQ_OK) return st;
     }
     VitParams p{X, rows, T, values, start, states, need ? scratch : nullptr};
-    const size_t per_warp = 2 * 2048 * sizeof(float) + (need ? 0 : (size_t)kShortT * 32 * 8);
-    const size_t smem = kVitWarps * per_warp;
-    cudaError_t e = cudaFuncSetAttribute(viterbi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-        set_error("lamq_viterbi_noalloc: %s", cudaGetErrorString(e));
-        return LAMQ_ERR_CUDA;
-    }
-    const int64_t grid = (rows + kVitWarps - 1) / kVitWarps;
-    viterbi_kernel<<<(unsigned)grid, kVitWarps * 32, smem, (cudaStream_t)stream>>>(p, k);
-    LAMQ_CHECK_LAUNCH("lamq_viterbi_noalloc");
-    return LAMQ_OK;
+    return launch_viterbi_warp(p, k, (cudaStream_t)stream, "lamq_viterbi_noalloc");
 }

@@ -109,7 +109,11 @@ def _reduce_finalize(st: Statistics, group, n_tok_total):
     if group is not None:
         torch.distributed.all_reduce(st.accH, group=group)
         torch.distributed.all_reduce(st.accD, group=group)
-        n_tok = n_tok_total if n_tok_total is not None else n_tok * group.size()
+        if n_tok_total is None:  # ranks may hold unequal shares (token_shard splits whole chunks): sum them
+            cnt = torch.tensor([float(n_tok)], dtype=torch.float64, device=st.accH.device)
+            torch.distributed.all_reduce(cnt, group=group)
+            n_tok_total = int(cnt.item())
+        n_tok = n_tok_total
     return st.finalize(n_tok)
 
 

@@ -68,7 +68,7 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu"],
+    ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -89,6 +89,15 @@ def main():
         return
     if args.only == "ldlq_gpu":
         write_ldlq_gpu_fixture(torch, Environment)
+        return
+    if args.only == "statistics":
+        write_statistics_fixture(torch, args.reference.resolve())
+        return
+    if args.only == "kl":
+        write_kl_fixture(torch, Q)
+        return
+    if args.only == "best_word":
+        write_best_word_fixture(C, Q, torch, args.reference.resolve())
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -209,6 +218,9 @@ def main():
     np.savez_compressed(HERE / "column_trellis.npz", **col)
     write_artifact_fixture(C, Q, CA, torch)
     write_fit_fixture(C, torch)
+    write_statistics_fixture(torch, args.reference.resolve())
+    write_kl_fixture(torch, Q)
+    write_best_word_fixture(C, Q, torch, args.reference.resolve())
     print("golden vectors written to", HERE)
 
 
@@ -250,6 +262,144 @@ def write_ldlq_gpu_fixture(torch, Environment):
     out["sweep_w1"] = syntax.sweep(X, env, nearest, width=1, lazy=64).numpy()
     out["sweep_w4"] = syntax.sweep(X, env, nearest, width=4, lazy=64).numpy()
     np.savez_compressed(HERE / "ldlq_gpu.npz", **out)
+
+
+def _reference_code(path: Path, outer: str, pick):
+    """Compiled statements of the reference, taken from its source as written: the function definitions and
+    statements inside `outer` (at any depth) for which pick(ast node, source text) holds, in source order. They run
+    below on seeded tensors, so the golden vectors come from the reference's own expressions, not a restatement."""
+    import ast
+    tree = ast.parse(path.read_text())
+    fn = next(n for n in ast.walk(tree) if isinstance(n, ast.FunctionDef) and n.name == outer)
+    found = []
+    for node in ast.walk(fn):
+        if isinstance(node, (ast.stmt,)) and node is not fn and pick(node, ast.unparse(node)):
+            found.append(node)
+    found.sort(key=lambda n: n.lineno)
+    return [(n.lineno, ast.unparse(n), compile(ast.Module(body=[n], type_ignores=[]), str(path), "exec"))
+            for n in found]
+
+
+def write_statistics_fixture(torch, ref: Path):
+    """11. Input statistics by the reference's own code on seeded bf16 activations (statgen.py):
+    - frame.covariance (opgraph/frame.py:498-505): Σ x xᵀ over 8192-token fp32 chunks, summed in fp64;
+    - quantize_stage's weighted accumulation, run statement by statement from quantize.py as written
+      (quantize.py:1389-1391 `wq`, :1457 D +=, :1466 H +=, :1467 n_tok +=, :1470 H = (H / n_tok)...), then its QEP
+      target (:1482 M = cross_target(H, (D / n_tok).cpu().double() − H) with cross_target of :1330-1335 at α = 0.5 and
+      the default λ) and W·M (:1503).
+    Stored: the outputs (fp64) and a digest of the inputs."""
+    import types
+    sys.path.insert(0, str(HERE))
+    import statgen
+    import quantize as Q
+    import opgraph.codes as C
+    from opgraph.frame import covariance
+    src = ref / "quantize.py"
+    defs = {name: _reference_code(src, "main", lambda n, t, name=name: isinstance(n, ast_def()) and n.name == name)
+            for name in ("wq", "cross_target")}
+    acc = _reference_code(src, "quantize_stage", lambda n, t: t in (
+        "D += grab['r'].T @ wq(c, grab['q'], tkey)", "H += grab['q'].T @ wq(c, grab['q'], tkey)",
+        "n_tok += len(grab['q'])"))
+    fin = _reference_code(src, "quantize_stage", lambda n, t: t == "H = (H / n_tok).cpu().double()")
+    qep = _reference_code(src, "quantize_stage", lambda n, t: t == "M = cross_target(H, (D / n_tok).cpu().double() - H)")
+    tgt = _reference_code(src, "quantize_stage", lambda n, t: t.startswith("target = W @ M if parse(p)[2]"))
+    assert len(acc) == 3 and len(fin) == 1 and len(qep) == 1 and len(tgt) == 1, (acc, fin, qep, tgt)
+    out = {}
+    for name, tokens, nchunks, d, weighted in statgen.STAT_CASES:
+        xq, xr, w, W = statgen.stat_inputs(name)
+        out[f"{name}_digest"] = np.array(statgen.digest(xq + (xr or []) + (w or [])))
+        if not weighted:
+            out[f"{name}_cov"] = covariance(torch.cat(xq)).numpy()
+            out[f"{name}_ntok"] = np.array(tokens * nchunks)
+            continue
+        ns = {"torch": torch, "guided": None, "token_w": tuple(w), "DEV": "cpu", "C": C,
+              "args": types.SimpleNamespace(cross_alpha=statgen.QEP_ALPHA, lam=Q.LAM),
+              "parse": lambda p: (None, None, True), "p": "tr2x"}
+        for code in (defs["wq"][0][2], defs["cross_target"][0][2]):
+            exec(code, ns)
+        ns.update(H=torch.zeros(d, d), D=torch.zeros(d, d), n_tok=0, tkey=None)
+        for c in range(nchunks):
+            ns["c"], ns["grab"] = c, {"q": xq[c].float(), "r": xr[c].float()}
+            for _, _, code in acc:
+                exec(code, ns)
+        Dacc = ns["D"].clone()
+        exec(fin[0][2], ns)
+        exec(qep[0][2], ns)
+        ns["W"] = W
+        exec(tgt[0][2], ns)
+        out[f"{name}_H"] = ns["H"].numpy()
+        out[f"{name}_D"] = ((Dacc / ns["n_tok"]).cpu().double() - ns["H"]).numpy()
+        if name == "qep":
+            out[f"{name}_M"] = ns["M"].numpy()
+        out[f"{name}_target"] = ns["target"].numpy()
+        out[f"{name}_ntok"] = np.array(ns["n_tok"])
+    out["alpha"], out["lam"] = np.array(statgen.QEP_ALPHA), np.array(Q.LAM)
+    out["statements"] = np.array([f"quantize.py:{ln}: {t.splitlines()[0]}" for group in
+                                  (defs["wq"], defs["cross_target"], acc, fin, qep, tgt) for ln, t, _ in group])
+    np.savez_compressed(HERE / "statistics.npz", **out)
+
+
+def write_best_word_fixture(C, Q, torch, ref: Path):
+    """13. best_word (quantize.py:1316-1328), run from the reference's source as written (a closure inside main, with
+    --seeds 3): the row-trellis word of the seed whose (E @ H * E).sum() is least, for a 48 x 128 target. Stored: each
+    candidate's error (the reference's own expression, evaluated on each candidate word) and the chosen word's
+    states and matrix."""
+    import types
+    code = _reference_code(ref / "quantize.py", "main",
+                           lambda n, t: isinstance(n, ast_def()) and n.name == "best_word")[0][2]
+    m, n, k, seed, nseeds = 48, 128, 2, 500, 3
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(501), dtype=torch.float64)).float().double()
+    H = calib_H(n, 2048, 502)
+    trellis = {b: C.RowTrellisCode(12, b, T=256, width=16, look=8) for b in (1, 2, 3, 4)}
+    ns = {"torch": torch, "args": types.SimpleNamespace(seeds=nseeds), "trellis_for": lambda rows: trellis,
+          "word": Q.word, "parse": Q.parse}
+    exec(code, ns)
+    best = ns["best_word"](f"tr{k}", W, H, seed)
+    errs, mats = [], []
+    for t in range(nseeds):  # the candidates, as best_word forms them, to record each one's error
+        net = Q.word(f"tr{k}", W, H, seed + 7919 * t, trellis)
+        E = net.matrix(dtype=torch.float64) - W
+        errs.append(float((E @ H * E).sum()))
+        mats.append(net.matrix(dtype=torch.float64))
+    chosen = [t for t in range(nseeds) if torch.equal(mats[t], best.matrix(dtype=torch.float64))]
+    np.savez_compressed(HERE / "best_word.npz", W=W.float().numpy(), H=H.float().numpy(),
+                        meta=np.array([m, n, k, seed, nseeds]), errs=np.array(errs), chosen=np.array(chosen[0]),
+                        states=Q.trellis_states(best.cores["W"].data, trellis[k].values).numpy())
+
+
+def ast_def():
+    import ast
+    return ast.FunctionDef
+
+
+def write_kl_fixture(torch, Q):
+    """12. The KL of a probe by the reference's quantize.evaluate (quantize.py:903-920; the formula of
+    compiler.py:180-187 and text_kl.py:54-58): a tiny random-init bf16 Llama against a copy with one linear piece
+    perturbed (statgen.kl_inputs). Stored with it: both models' final hidden states (the lm_head's input, bf16 bits)
+    and the tied lm_head weight, which the KL head kernel takes, and the per-position KL of the same formula."""
+    sys.path.insert(0, str(HERE))
+    import statgen
+    import torch.nn.functional as F
+    ref, probe, ids = statgen.kl_inputs()
+    res = Q.evaluate(probe, ref, ids, 2)
+    grab = {}
+
+    def hook(tag):
+        def f(m, a):
+            grab.setdefault(tag, []).append(a[0].detach().reshape(-1, a[0].shape[-1]))
+        return f
+    hs = [ref.lm_head.register_forward_pre_hook(hook("ref")), probe.lm_head.register_forward_pre_hook(hook("probe"))]
+    with torch.no_grad():
+        lr = F.log_softmax(ref(ids, use_cache=False).logits.float(), -1)
+        lp = F.log_softmax(probe(ids, use_cache=False).logits.float(), -1)
+    for h in hs:
+        h.remove()
+    per_pos = (lr.exp() * (lr - lp)).sum(-1).reshape(-1)
+    out = {"ids": ids.numpy(), "kl": np.array(res["kl"]), "ppl": np.array(res["ppl"]), "kl_pos": per_pos.numpy(),
+           "h_ref": torch.cat(grab["ref"]).view(torch.int16).numpy(),
+           "h_probe": torch.cat(grab["probe"]).view(torch.int16).numpy(),
+           "E": ref.lm_head.weight.detach().view(torch.int16).numpy()}
+    np.savez_compressed(HERE / "kl.npz", **out)
 
 
 def write_neartie_fixture(C, torch, case: Path):

@@ -1,0 +1,75 @@
+"""Seeded inputs of the statistics, QEP and KL golden vectors (statistics.npz, kl.npz).
+
+`make_golden.py` draws these inputs, runs the reference on them and stores only the outputs (and checksums of the
+inputs); the tests draw the same inputs again with the same torch CPU generator and compare. A checksum mismatch
+means the generator gave different numbers on this machine, and the tests say so instead of reporting a parity
+failure.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import torch
+
+# (name, tokens per chunk, chunks, d, weighted): the activation streams of quantize_stage (quantize.py:1412-1470)
+STAT_CASES = [("cov", 9000, 3, 96, False),   # frame.covariance: 27,000 tokens, four of its 8192-token chunks
+              ("qep", 4096, 3, 128, True),   # weighted H and D, then cross_target and W·M
+              ("qep_wide", 2048, 2, 256, True)]
+QEP_ROWS = 64       # rows of the W whose target W·M is recorded
+QEP_ALPHA = 0.5     # config 3's α
+
+
+def activations(tokens: int, d: int, g: torch.Generator) -> torch.Tensor:
+    """bf16 activations with per-channel std lognormal(0, 1) and two ×20 outlier channels."""
+    std = torch.exp(torch.randn(d, generator=g))
+    std[torch.randperm(d, generator=g)[:2]] *= 20
+    return (torch.randn(tokens, d, generator=g) * std).to(torch.bfloat16)
+
+
+def stat_inputs(name: str):
+    """(xq chunks, xr chunks or None, token-weight chunks or None, W or None): bf16 chunks on the CPU."""
+    case = next(c for c in STAT_CASES if c[0] == name)
+    _, tokens, nchunks, d, weighted = case
+    g = torch.Generator().manual_seed(7000 + tokens + d)
+    xq, xr, w = [], [], []
+    for _ in range(nchunks):
+        x = activations(tokens, d, g)
+        xq.append(x)
+        if weighted:  # the reference stream: the quantized one with per-channel gains of ±10 % and some noise
+            if not xr:
+                gain = 1.0 + 0.1 * torch.randn(d, generator=g)
+            xr.append((x.float() * gain + 0.05 * x.float().abs().mean() * torch.randn(tokens, d, generator=g))
+                      .to(torch.bfloat16))
+            w.append(torch.where(torch.rand(tokens, generator=g) < 0.08, 10.0, 1.0).float())
+    W = (0.02 * torch.randn(QEP_ROWS, d, generator=g, dtype=torch.float64)) if weighted else None
+    return xq, (xr if weighted else None), (w if weighted else None), W
+
+
+def kl_inputs():
+    """A tiny random-init Llama (bf16; weights N(0, 0.3²) so the logits spread over a few nats), its 'probe' copy with one linear piece perturbed, and held token ids."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=1000, rms_norm_eps=1e-5, rope_theta=1e4,
+                      tie_word_embeddings=True, max_position_embeddings=256, initializer_range=0.3)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(31)
+    ref = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    probe = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    probe.load_state_dict(ref.state_dict())
+    g = torch.Generator().manual_seed(32)
+    with torch.no_grad():
+        w = probe.model.layers[1].mlp.down_proj.weight
+        w.copy_((w.float() + 0.2 * torch.randn(w.shape, generator=g)).to(torch.bfloat16))
+    ranks = torch.arange(1, cfg.vocab_size + 1, dtype=torch.float64).pow(-1.1)
+    ids = torch.multinomial(ranks, 3 * 96, replacement=True, generator=g).reshape(3, 96)
+    return ref, probe, ids
+
+
+def digest(tensors) -> str:
+    """SHA-256 of the tensors' bytes, in order."""
+    h = hashlib.sha256()
+    for t in tensors:
+        h.update(t.contiguous().view(torch.uint8).numpy().tobytes() if t.dtype == torch.bfloat16
+                 else t.contiguous().numpy().tobytes())
+    return h.hexdigest()

@@ -46,13 +46,19 @@ def test_abi_version_and_errors_without_gpu(lib):
 
 def test_workspace_sizes(lib):
     assert lib.lamq_viterbi_workspace_size(100, 24, 12, 2) == 0  # short sequences keep back-pointers on chip
-    assert lib.lamq_viterbi_workspace_size(3, 256, 12, 2) == 3 * 256 * 32 * 8
+    # long sequences: the warp pair keeps them in shared memory where a device can hold them (0), else 256 B an entry
+    assert lib.lamq_viterbi_workspace_size(3, 256, 12, 2) in (0, 3 * 256 * 32 * 8)
+    assert lib.lamq_viterbi_workspace_size(2**60, 4096, 12, 2) in (0, 2**64 - 1)  # SIZE_MAX: the size overflows
 
 
 # One call per entry point that breaks an argument rule: (name, arguments, a fragment of lamq_last_error()). Every
 # entry point checks its arguments before it touches the device, so these run without a GPU.
 N = None
+P = 4096  # a non-null pointer the checks below never dereference
 INVALID = [
+    ("lamq_viterbi_noalloc", (P, 200000, 64, P, 12, 2, N, P, N), b"more back-pointers than the built-in"),
+    ("lamq_viterbi_noalloc", (P, 2**62, 4096, P, 12, 2, N, P, N), b"more back-pointers than the built-in"),
+    ("lamq_trellis_product", (P, 4, 32, 2, 12, P, P, N, P, 32, 2, P, 3, N), b"ldy 3 below the group's 4 rows"),
     ("lamq_viterbi_noalloc", (N, 4, 8, N, 12, 5, N, N, N), b"k must be 1..4"),
     ("lamq_ldlq_round", (N, 4, 4, 4, N, 4, N, 2, 200, N, 4, N, 0, N), b"block in 1..128"),
     ("lamq_ldlq_round", (N, 4, 4, 4, N, 4, N, 2, 16, N, 4, N, 0, N), b"null pointer"),
@@ -69,6 +75,8 @@ INVALID = [
     ("lamq_cholesky_inverse_lower", (N, 2, 4, N, 0, N, N), b"bad shape"),
     ("lamq_env_factor", (N, 4, 4, 0.01, N, 4, N, N, 0, N, N), b"null or aliased"),
     ("lamq_ridge", (N, 2, N, 4, 4, 0.1, N), b"bad shape"),
+    ("lamq_proxy_loss", (N, 2, N, 4, 4, 4, N, 4, N, N, N, 0, N), b"bad shape"),
+    ("lamq_proxy_loss", (N, 4, N, 4, 4, 4, N, 4, N, P, N, 0, N), b"null pointer"),
     ("lamq_cross_apply", (N, 4, 6, 4, N, 4, N, 4, 0.5, N, 4, N, 0, N), b"needs rows == n"),
     ("lamq_kl_reference", (N, 8, 0, 8, N, 8, 16, N, 16, N, N, N, N, 0, N, N), b"lamq_kl_reference: bad shape"),
     ("lamq_kl_head", (N, 8, 4, 8, N, 8, 16, N, 16, N, N, N, N, N, N, N, 0, N, N), b"lamq_kl_head: null pointer"),
@@ -96,6 +104,7 @@ EMPTY = [
     ("lamq_cholesky_inverse_lower", (N, 0, 0, N, 0, N, N)),
     ("lamq_env_factor", (N, 0, 0, 0.01, N, 0, N, N, 0, N, N)),
     ("lamq_ridge", (N, 0, N, 0, 0, 0.1, N)),
+    ("lamq_proxy_loss", (N, 4, N, 4, 4, 0, N, 4, N, P, N, 0, N)),
     ("lamq_cross_apply", (N, 4, 0, 0, N, 4, N, 4, 0.5, N, 4, N, 0, N)),
     ("lamq_pack_trellis", (N, 32, 0, 32, 2, 12, N, N, N)),
     ("lamq_unpack_trellis", (N, 0, 32, 2, 12, N, 32, N)),

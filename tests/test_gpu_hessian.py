@@ -81,3 +81,70 @@ def test_config2_scale_against_fp64():
     Xd = X.double()
     ref = (Xd.T @ (Xd * w.double()[:, None])) / X.shape[0]
     assert float(torch.linalg.norm(H - ref) / torch.linalg.norm(ref)) < 1e-5
+
+
+# ---- against the reference's own outputs (tests/golden/statistics.npz, made by make_golden.py from the reference)
+
+def _stat_inputs(golden, name):
+    import sys
+    from conftest import GOLDEN
+    sys.path.insert(0, str(GOLDEN))
+    import statgen
+    xq, xr, w, W = statgen.stat_inputs(name)
+    if statgen.digest(xq + (xr or []) + (w or [])) != str(golden("statistics")[f"{name}_digest"]):
+        pytest.skip("torch's CPU generator drew different inputs here than where the golden vectors were made")
+    return xq, xr, w, W
+
+
+def test_h_matches_reference_covariance(golden):
+    """frame.covariance (opgraph/frame.py:498-505) of 27,000 bf16 tokens: H·n_tok to 1e-5 relative Frobenius."""
+    from lookatmyquant_b200.hessian import Statistics
+    g = golden("statistics")
+    xq, _, _, _ = _stat_inputs(golden, "cov")
+    st = Statistics(xq[0].shape[1], device="cuda")
+    for x in xq:
+        st.add(x.cuda())
+    H, _ = st.finalize(n_tok=1)
+    st.check_status()
+    assert rel(H.cpu().numpy(), g["cov_cov"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["qep", "qep_wide"])
+def test_weighted_statistics_and_qep_target_match_reference(golden, name):
+    """quantize_stage's token-weighted H and D over three chunks (quantize.py:1457-1470) and the QEP target W·M
+    (:1330-1335, :1482, :1503), all by the reference's own statements in make_golden.py: H and D + H to 1e-5,
+    W·M from the golden H, D to 1e-10, and W·M from this build's own H, D to 1e-4 (D is a 10 % difference of
+    fp32-accumulated moments)."""
+    from lookatmyquant_b200.hessian import Statistics
+    from lookatmyquant_b200.linalg import CrossTarget
+    g = golden("statistics")
+    xq, xr, w, W = _stat_inputs(golden, name)
+    st = Statistics(xq[0].shape[1], cross=True, device="cuda")
+    for a, b, t in zip(xq, xr, w):
+        st.add(a.cuda(), t.cuda(), b.cuda())
+    H, D = st.finalize()
+    st.check_status()
+    gH, gD, tgt = g[f"{name}_H"], g[f"{name}_D"], g[f"{name}_target"]
+    assert rel(H.cpu().numpy(), gH) < 1e-5
+    assert np.linalg.norm((D + H).cpu().numpy() - (gD + gH)) < 1e-5 * np.linalg.norm(gH)
+    alpha, lam = float(g["alpha"]), float(g["lam"])
+    for rows in (W.shape[0], 10 * W.shape[1]):  # W + α((W·D)·Lc⁻ᵀ)·Lc⁻¹, and M formed once
+        ct = CrossTarget(torch.as_tensor(gH).cuda(), torch.as_tensor(gD).cuda(), alpha, lam, rows=rows)
+        got = ct.apply(W.cuda()).cpu().numpy()
+        ct.check()
+        assert np.abs(got - tgt).max() <= 1e-10 * np.abs(tgt).max()
+    ct = CrossTarget(H, D, alpha, lam, rows=W.shape[0])
+    got = ct.apply(W.cuda()).cpu().numpy()
+    assert rel(got, tgt) < 1e-4
+
+
+def test_config2_d9728_token_subset_against_oracle():
+    """Config 2's second pass (d = 9728, token weights 10 on Bernoulli(0.08)) on 8192 tokens: the tcgen05 paired
+    kernel against the oracle's fp32 accumulation (quantize.py:1457-1470) at the 1e-5 bar."""
+    from lookatmyquant_b200.hessian import hessian
+    from lookatmyquant_b200.workloads import activations_bf16, token_weights
+    X = activations_bf16(8192, 9728, seed=21, device="cuda")
+    w = token_weights(8192, seed=22, device="cuda")
+    H, _ = hessian(X, w)
+    ref, _ = O.hessian_accumulate([X.float().cpu().numpy()], [w.cpu().numpy()])
+    assert rel(H.cpu().numpy(), ref) < 1e-5

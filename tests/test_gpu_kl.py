@@ -50,3 +50,17 @@ def test_kl_floor_is_exactly_zero():
     ref = KLReference(h, E)
     value, per_pos = ref.kl(h, per_position=True)
     assert value == 0.0 and bool((per_pos == 0).all())
+
+
+def test_kl_matches_reference_evaluate(golden):
+    """quantize.evaluate (quantize.py:903-920; the formula of compiler.py:180-187) of a tiny random-init bf16 Llama
+    against a copy with one piece perturbed, run by the reference in make_golden.py: the KL head kernel on the two
+    models' recorded final hidden states and the tied lm_head gives the same mean KL to 1e-4 nats."""
+    from lookatmyquant_b200.kl import KLReference
+    g = golden("kl")
+    bf = lambda a: torch.as_tensor(a).view(torch.bfloat16).cuda()
+    ref = KLReference(bf(g["h_ref"]), bf(g["E"]))
+    value, per_pos = ref.kl(bf(g["h_probe"]), per_position=True)
+    assert abs(value - float(g["kl"])) <= 1e-4
+    assert (per_pos.cpu().double() - torch.as_tensor(g["kl_pos"]).double()).abs().max() <= 1e-3
+    assert ref.kl(bf(g["h_ref"])) == 0.0

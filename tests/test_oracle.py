@@ -1,10 +1,11 @@
 """The oracle against the reference's own outputs (golden vectors made by tests/golden/make_golden.py)."""
 
+import sys
 import numpy as np
 import pytest
 import torch
 
-from conftest import table
+from conftest import GOLDEN, table
 from oracle import core as O
 
 
@@ -162,3 +163,51 @@ def test_oracle_scalar_ldlq_matches_reference(golden):
     assert np.abs(O.ldlq_factor(g["Hbad"]) - g["Ubad"]).max() <= 1e-12 * np.abs(g["Ubad"]).max()
     for nl, block in ((8, 128), (16, 48)):
         assert np.array_equal(O.ldlq_round(g["X"], g["U"], g[f"levels{nl}"], block), g[f"Q{nl}_b{block}"])
+
+
+# ---- statistics, QEP and KL against the reference's own outputs (statistics.npz, kl.npz by make_golden.py)
+
+def _stat_inputs(golden, name):
+    sys.path.insert(0, str(GOLDEN))
+    import statgen
+    xq, xr, w, W = statgen.stat_inputs(name)
+    if statgen.digest(xq + (xr or []) + (w or [])) != str(golden("statistics")[f"{name}_digest"]):
+        pytest.skip("torch's CPU generator drew different inputs here than where the golden vectors were made")
+    return xq, xr, w, W
+
+
+def test_oracle_statistics_match_reference_covariance(golden):
+    """frame.covariance (opgraph/frame.py:498-505): Σ x xᵀ of bf16 activations; the oracle's H·n_tok equals it to fp32
+    accumulation error (the reference sums 8192-token fp32 chunks in fp64, the oracle per given chunk)."""
+    g = golden("statistics")
+    xq, _, _, _ = _stat_inputs(golden, "cov")
+    H, _ = O.hessian_accumulate([x.float().numpy() for x in xq])
+    ref = g["cov_cov"] / float(g["cov_ntok"])
+    assert np.linalg.norm(H - ref) <= 1e-6 * np.linalg.norm(ref)
+
+
+@pytest.mark.parametrize("name", ["qep", "qep_wide"])
+def test_oracle_weighted_statistics_and_qep_match_reference(golden, name):
+    """quantize_stage's weighted H, D (quantize.py:1457-1470) and the QEP target W·M (:1330-1335, :1482, :1503), run
+    by make_golden.py statement by statement from the reference's source: the oracle agrees to fp32 rounding on H
+    and D + H, and to 1e-9 on M and W·M from the golden H and D."""
+    g = golden("statistics")
+    xq, xr, w, W = _stat_inputs(golden, name)
+    H, D = O.hessian_accumulate([x.float().numpy() for x in xq], [t.numpy() for t in w],
+                                [x.float().numpy() for x in xr])
+    gH, gD = g[f"{name}_H"], g[f"{name}_D"]
+    assert np.linalg.norm(H - gH) <= 1e-6 * np.linalg.norm(gH)
+    assert np.linalg.norm((D + H) - (gD + gH)) <= 1e-6 * np.linalg.norm(gH)
+    M = O.cross_target(gH, gD, float(g["alpha"]), float(g["lam"]))
+    if f"{name}_M" in g:
+        assert np.abs(M - g[f"{name}_M"]).max() <= 1e-9
+    tgt = g[f"{name}_target"]
+    assert np.abs(W.numpy() @ M - tgt).max() <= 1e-9 * np.abs(tgt).max()
+
+
+def test_kl_fixture_formula(golden):
+    """quantize.evaluate's KL (quantize.py:903-920) is the mean over positions of the per-position KL recorded with it
+    (the formula of compiler.py:180-187 with unit weights), and the probe is far from the floor."""
+    g = golden("kl")
+    assert abs(float(g["kl_pos"].astype(np.float64).mean()) - float(g["kl"])) <= 1e-6
+    assert float(g["kl"]) > 0.1
