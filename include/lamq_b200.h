@@ -26,6 +26,8 @@
  *   lamq_decode_trellis    compiler_artifact.py:433-442  decode_rotated: table[state]·scale per group row
  *   lamq_trellis_product   runtime_mlx/fast_q35.py:69-172 the product kernel: y = S ⊙ (V[state]·(R_in x)) per group
  *   lamq_trellis_product_groups                       the same for all row groups that read one input, one launch
+ *   lamq_trellis_gemm      fast_q35.py:69-201 with    many input vectors: the decode fused into a tcgen05 GEMM
+ *                          compiler_artifact.py:433-442
  *   lamq_kl_reference,     compiler.py:176-187        the KL probe: ref_lp once, then per probe the KL of the held
  *   lamq_kl_head                                      positions' log_softmax(lm_head(h)) to it
  */
@@ -335,6 +337,38 @@ typedef struct lamq_product_group {
  */
 int lamq_trellis_product_groups(const lamq_product_group *groups, int ngroups, int n, const float *x, int64_t ldx,
                                 int nvec, lamq_stream_t stream);
+
+/*
+ * One row group of a trellis-dequant GEMM: `rows` weight rows whose states come either from packed codes
+ * (opgraph-packed-1, k-bit symbols, 1 <= k <= 4, L-bit states, codes = rows x lamq_trellis_words_per_row(n, k) words)
+ * or from an int16 state matrix (states, rows x lds; codes NULL), the rows' fp32 scales, the 2^L-entry fp32 table, the
+ * output row of each (map, or NULL for row r) and the output y (nvec rows of leading dimension ldy, fp32 or bf16).
+ * 80 bytes, no padding.
+ */
+typedef struct lamq_gemm_group {
+    const uint32_t *codes;
+    const int16_t *states;
+    int64_t lds;
+    int64_t rows;
+    int k, L;
+    const float *scales;
+    const float *table;
+    const uint32_t *map;
+    void *y;
+    int64_t ldy;
+} lamq_gemm_group;
+
+/*
+ * The trellis-dequant GEMM for many input vectors (runtime_mlx/fast_q35.py:69-201's product y = S ⊙ (V[state]·x), and
+ * compiler_artifact.py:433-442's decode W = S·V[state], fused): y[v][map[r]] = scales[r]·Σ_j bf16(table[state_rj])·
+ * x[v][j] with fp32 accumulation on the tensor cores, the weights decoded from the states into shared memory and never
+ * written out. x: nvec x n bf16 (the input after the groups' input rotation), 16-byte aligned, ldx a multiple of 8.
+ * y_bf16: 0 writes fp32 outputs, 1 bf16. All groups read the same x; they run in one launch per 16 groups. status
+ * (device int, 0 on entry) becomes LAMQ_ERR_TIMEOUT if a device wait gives up. `groups` is host memory, read before
+ * the call returns.
+ */
+int lamq_trellis_gemm(const lamq_gemm_group *groups, int ngroups, int n, const uint16_t *x, int64_t ldx,
+                      int64_t nvec, int y_bf16, int *status, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

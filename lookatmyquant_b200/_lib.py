@@ -58,6 +58,7 @@ SIGNATURES = {
     "lamq_decode_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _P]),
     "lamq_trellis_product": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P]),
     "lamq_trellis_product_groups": (_I32, [_P, _I32, _I32, _P, _I64, _I32, _P]),
+    "lamq_trellis_gemm": (_I32, [_P, _I32, _I32, _P, _I64, _I64, _I32, _P, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64, _I32]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),
@@ -68,6 +69,12 @@ class ProductGroup(_c.Structure):
     """lamq_product_group: one packed row group of a grouped product (64 bytes, the header's field order)."""
     _fields_ = [("codes", _P), ("rows", _I64), ("k", _I32), ("L", _I32), ("scales", _P), ("table", _P),
                 ("map", _P), ("y", _P), ("ldy", _I64)]
+
+
+class GemmGroup(_c.Structure):
+    """lamq_gemm_group: one row group of a trellis-dequant GEMM (80 bytes, the header's field order)."""
+    _fields_ = [("codes", _P), ("states", _P), ("lds", _I64), ("rows", _I64), ("k", _I32), ("L", _I32),
+                ("scales", _P), ("table", _P), ("map", _P), ("y", _P), ("ldy", _I64)]
 
 
 class LamqError(RuntimeError):

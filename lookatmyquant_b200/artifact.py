@@ -1,13 +1,14 @@
 """Packed trellis rows on B200: the opgraph-packed-1 trellis encoding and the product with packed rows
 (liblamq_b200: lamq_pack_trellis, lamq_unpack_trellis, lamq_decode_trellis, lamq_trellis_product,
-lamq_trellis_product_groups).
+lamq_trellis_product_groups, lamq_trellis_gemm).
 
 Reference (ShinMegamiBoson/lookatmyquant):
   valid_path, pack_trellis, unpack_trellis      compiler_artifact.py:261-297
   _input_signs                                  compiler_artifact.py:300-304
   encode_entry (state-based row-group entries)  compiler_artifact.py:307-360, grouped_matrix_specs :143-167
   decode_rotated                                compiler_artifact.py:433-442
-  the product y = S ⊙ (V[state]·(R_in x))       runtime_mlx/fast_q35.py:69-172 (Metal there)
+  the product y = S ⊙ (V[state]·(R_in x))       runtime_mlx/fast_q35.py:69-172 (Metal there); for many vectors
+                                                the decode fused into a tcgen05 GEMM (lamq_trellis_gemm)
 
 Tensors live on the device; uint32 words and row maps are held in int32 tensors (the same bits). Invalid input raises
 the reference's ValueError messages. There is no host fallback: every entry point runs in liblamq_b200.so.
@@ -23,7 +24,7 @@ from .rotation import Rotation
 
 TABLE_ENTRIES = 4096
 STATE_BITS = 12
-DENSE_PRODUCT_VECTORS = 64  # from this many input vectors on, a group is decoded once and multiplied densely
+GEMM_PRODUCT_VECTORS = 64  # from this many input vectors on, the product runs on the tensor cores (lamq_trellis_gemm)
 
 
 def _dev(t: torch.Tensor) -> torch.device:
@@ -169,8 +170,9 @@ class TrellisProduct:
     """y = W·x for a packed grouped matrix, W = diag(S)·V[state]·R_in (the product of runtime_mlx/fast_q35.py):
     x is rotated once (R_in x, fp64 through the Kronecker factors, then fp32) and the row groups multiply their packed
     rows with it, all in one launch (lamq_trellis_product_groups; `product_rotated` does the same for every matrix of
-    a stage). With DENSE_PRODUCT_VECTORS or more vectors, each group is decoded once into bf16 and the product runs
-    as a dense bf16 GEMM with fp32 accumulation."""
+    a stage). With GEMM_PRODUCT_VECTORS or more vectors, the rotated input is rounded to bf16 and the groups run as
+    one tcgen05 GEMM whose weights are decoded from the packed states into shared memory (lamq_trellis_gemm, fp32
+    accumulation): nothing dense is formed."""
 
     def __init__(self, tensors: dict, meta: dict, device=None):
         self.meta = meta
@@ -191,7 +193,7 @@ class TrellisProduct:
         return self.rot.rows(x.to(self.device, torch.float64).contiguous()).to(torch.float32)
 
     def dense_rotated(self) -> torch.Tensor:
-        """decode_rotated as bf16 (cached): V[state]·S before the input transform."""
+        """decode_rotated as bf16 (cached): V[state]·S before the input transform (a check, not the product path)."""
         if self._dense is None:
             tensors = {}
             for g, codes, rows, scales, table in self.groups:
@@ -208,12 +210,12 @@ class TrellisProduct:
     def rotated(self, xr: torch.Tensor) -> torch.Tensor:
         """y = V[state]·S · xr for an input already rotated (R_in x, fp32, nvec × n): matrices that read the same
         input through the same signs (a stage's q/k/v, gate/up) share one rotation."""
-        xr = xr.to(self.device, torch.float32).contiguous()
         nvec = xr.shape[0]
-        if nvec >= DENSE_PRODUCT_VECTORS:
-            return (xr.to(torch.bfloat16) @ self.dense_rotated().T).float()
         y = torch.empty(nvec, self.m, dtype=torch.float32, device=self.device)
-        _grouped_product([(self, y)], xr)
+        if nvec >= GEMM_PRODUCT_VECTORS:
+            _gemm_product([(self, y)], xr)
+            return y
+        _grouped_product([(self, y)], xr.to(self.device, torch.float32).contiguous())
         return y
 
     def product_groups(self, y: torch.Tensor) -> list:
@@ -221,6 +223,45 @@ class TrellisProduct:
         return [(_lib.ProductGroup(ptr(codes), rows.numel(), g["bits"], g["state_bits"], ptr(scales), ptr(table),
                                    ptr(rows), ptr(y), y.stride(0)), (g, codes, rows, scales, table))
                 for g, codes, rows, scales, table in self.groups]
+
+
+def _bf16_operand(x: torch.Tensor, device) -> torch.Tensor:
+    """x as the GEMM's bf16 operand: 16-byte aligned rows whose length is a multiple of 8 elements (padded)."""
+    x = x.to(device, torch.bfloat16)
+    n = x.shape[1]
+    if x.stride(-1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0:
+        return x
+    ld = (n + 7) // 8 * 8
+    buf = torch.empty(x.shape[0], ld, dtype=torch.bfloat16, device=device)
+    buf[:, :n] = x
+    return buf[:, :n]
+
+
+def gemm_groups(groups: list, n: int, x: torch.Tensor, y_bf16: bool = False):
+    """lamq_trellis_gemm over `groups` (lamq_gemm_group structures) that all read x (nvec × n, bf16 operand)."""
+    device = x.device
+    if not groups:
+        return
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    arr = (_lib.GemmGroup * len(groups))(*groups)
+    with torch.cuda.device(device):
+        check(_lib.load().lamq_trellis_gemm(arr, len(groups), n, ptr(x), x.stride(0), x.shape[0], 1 if y_bf16 else 0,
+                                            ptr(status), stream_ptr(device)), "lamq_trellis_gemm")
+    return status
+
+
+def _gemm_product(pairs: list, xr: torch.Tensor):
+    """Every row group of the (TrellisProduct, y) pairs times xr (nvec × n) on the tensor cores, one launch."""
+    device, n = pairs[0][0].device, pairs[0][0].n
+    x = _bf16_operand(xr, device)
+    groups = []
+    for prod, y in pairs:
+        for g, codes, rows, scales, table in prod.groups:
+            groups.append(_lib.GemmGroup(ptr(codes), None, 0, rows.numel(), g["bits"], g["state_bits"], ptr(scales),
+                                         ptr(table), ptr(rows), ptr(y), y.stride(0)))
+    status = gemm_groups(groups, n, x)
+    if status is not None and int(status.item()):
+        _lib.check(int(status.item()), "lamq_trellis_gemm")
 
 
 def _grouped_product(pairs: list, xr: torch.Tensor):
@@ -252,10 +293,10 @@ def product_rotated(products: list, xr: torch.Tensor) -> list:
     n, device = products[0].n, products[0].device
     if any(p.n != n or p.device != device for p in products):
         raise ValueError("product_rotated: the matrices must share the input width and the device")
-    xr = xr.to(device, torch.float32).contiguous()
     nvec = xr.shape[0]
-    if nvec >= DENSE_PRODUCT_VECTORS:
-        return [p.rotated(xr) for p in products]
     ys = [torch.empty(nvec, p.m, dtype=torch.float32, device=device) for p in products]
-    _grouped_product(list(zip(products, ys)), xr)
+    if nvec >= GEMM_PRODUCT_VECTORS:
+        _gemm_product(list(zip(products, ys)), xr)
+    else:
+        _grouped_product(list(zip(products, ys)), xr.to(device, torch.float32).contiguous())
     return ys

@@ -19,12 +19,27 @@ STAT_CASES = [("cov", 9000, 3, 96, False),   # frame.covariance: 27,000 tokens, 
 QEP_ROWS = 64       # rows of the W whose target W·M is recorded
 QEP_ALPHA = 0.5     # config 3's α
 
+# Every input below is made from integers drawn by torch's CPU generator and combined with exactly rounded
+# elementwise arithmetic (sums of integers, products with powers of two, one fp32 product and sum): no
+# transcendental functions and no reductions, whose vectorised CPU kernels round differently on different CPUs.
 
-def activations(tokens: int, d: int, g: torch.Generator) -> torch.Tensor:
-    """bf16 activations with per-channel std lognormal(0, 1) and two ×20 outlier channels."""
-    std = torch.exp(torch.randn(d, generator=g))
-    std[torch.randperm(d, generator=g)[:2]] *= 20
-    return (torch.randn(tokens, d, generator=g) * std).to(torch.bfloat16)
+
+def _gauss(shape, g: torch.Generator) -> torch.Tensor:
+    """Approximately N(0, 1) fp32 values: the sum of four uniform integers in [-2048, 2048), scaled by 2^-11·√3/2."""
+    u = sum(torch.randint(-2048, 2048, shape, generator=g) for _ in range(4))
+    return u.to(torch.float32) * (0.8660254037844386 / 2048)
+
+
+def activations(tokens: int, d: int, g: torch.Generator, scale: torch.Tensor) -> torch.Tensor:
+    """bf16 activations with the given per-channel scales (powers of two)."""
+    return (_gauss((tokens, d), g) * scale).to(torch.bfloat16)
+
+
+def channel_scales(d: int, g: torch.Generator) -> torch.Tensor:
+    """Per-channel scales 2^e, e uniform in -2..2 (a coarse lognormal), with two ×16 outlier channels."""
+    e = torch.randint(-2, 3, (d,), generator=g)
+    e[torch.randperm(d, generator=g)[:2]] += 4
+    return torch.tensor([2.0 ** int(v) for v in e], dtype=torch.float32)
 
 
 def stat_inputs(name: str):
@@ -32,17 +47,16 @@ def stat_inputs(name: str):
     case = next(c for c in STAT_CASES if c[0] == name)
     _, tokens, nchunks, d, weighted = case
     g = torch.Generator().manual_seed(7000 + tokens + d)
+    scale = channel_scales(d, g)
+    gain = 1.0 + torch.randint(-100, 101, (d,), generator=g).to(torch.float32) / 1024 if weighted else None
     xq, xr, w = [], [], []
     for _ in range(nchunks):
-        x = activations(tokens, d, g)
+        x = activations(tokens, d, g, scale)
         xq.append(x)
         if weighted:  # the reference stream: the quantized one with per-channel gains of ±10 % and some noise
-            if not xr:
-                gain = 1.0 + 0.1 * torch.randn(d, generator=g)
-            xr.append((x.float() * gain + 0.05 * x.float().abs().mean() * torch.randn(tokens, d, generator=g))
-                      .to(torch.bfloat16))
-            w.append(torch.where(torch.rand(tokens, generator=g) < 0.08, 10.0, 1.0).float())
-    W = (0.02 * torch.randn(QEP_ROWS, d, generator=g, dtype=torch.float64)) if weighted else None
+            xr.append((x.float() * gain + 0.0625 * _gauss((tokens, d), g)).to(torch.bfloat16))
+            w.append(torch.where(torch.randint(0, 100, (tokens,), generator=g) < 8, 10.0, 1.0).float())
+    W = (_gauss((QEP_ROWS, d), g).double() * (1.0 / 64)) if weighted else None
     return xq, (xr if weighted else None), (w if weighted else None), W
 
 

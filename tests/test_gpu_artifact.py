@@ -102,7 +102,7 @@ def test_product_matches_dense(golden, nvec):
     y = prod(x).double().cpu().numpy()
     xr = Rotation.from_signs(torch.as_tensor(g["signs"]).double()).rows(x).cpu().numpy()
     ref = xr @ g["decoded"].astype(np.float64).T
-    tol = 1e-2 if nvec >= A.DENSE_PRODUCT_VECTORS else 1e-5  # bf16 dense path vs the fp32 packed product
+    tol = 1e-2 if nvec >= A.GEMM_PRODUCT_VECTORS else 1e-5  # bf16 tensor-core GEMM vs the fp32 packed product
     assert np.abs(y - ref).max() <= tol * np.abs(ref).max()
 
 
