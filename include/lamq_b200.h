@@ -342,8 +342,9 @@ int lamq_trellis_product_groups(const lamq_product_group *groups, int ngroups, i
  * One row group of a trellis-dequant GEMM: `rows` weight rows whose states come either from packed codes
  * (opgraph-packed-1, k-bit symbols, 1 <= k <= 4, L-bit states, codes = rows x lamq_trellis_words_per_row(n, k) words)
  * or from an int16 state matrix (states, rows x lds; codes NULL), the rows' fp32 scales, the 2^L-entry fp32 table, the
- * output row of each (map, or NULL for row r) and the output y (nvec rows of leading dimension ldy, fp32 or bf16).
- * 80 bytes, no padding.
+ * output row of each (map, or NULL for row r), the output y (nvec rows of leading dimension ldy, fp32 or bf16) and
+ * the input the group multiplies: x (nvec x n bf16, leading dimension ldx, the input after the group's input
+ * rotation). 104 bytes, no padding (`reserved` is ignored).
  */
 typedef struct lamq_gemm_group {
     const uint32_t *codes;
@@ -356,19 +357,27 @@ typedef struct lamq_gemm_group {
     const uint32_t *map;
     void *y;
     int64_t ldy;
+    const uint16_t *x;
+    int64_t ldx;
+    int n;
+    int reserved;
 } lamq_gemm_group;
 
 /*
  * The trellis-dequant GEMM for many input vectors (runtime_mlx/fast_q35.py:69-201's product y = S ⊙ (V[state]·x), and
- * compiler_artifact.py:433-442's decode W = S·V[state], fused): y[v][map[r]] = scales[r]·Σ_j bf16(table[state_rj])·
- * x[v][j] with fp32 accumulation on the tensor cores, the weights decoded from the states into shared memory and never
- * written out. x: nvec x n bf16 (the input after the groups' input rotation), 16-byte aligned, ldx a multiple of 8.
- * y_bf16: 0 writes fp32 outputs, 1 bf16. All groups read the same x; they run in one launch per 16 groups. status
- * (device int, 0 on entry) becomes LAMQ_ERR_TIMEOUT if a device wait gives up. `groups` is host memory, read before
- * the call returns.
+ * compiler_artifact.py:433-442's decode W = S·V[state]): y[v][map[r]] = scales[r]·Σ_j bf16(table[state_rj])·x[v][j]
+ * with fp32 accumulation on the tensor cores (pairs of CTAs, 256 rows a tile). Up to 512 vectors the weights are
+ * decoded from the states straight into shared memory, tile by tile, and never written out; from 513 vectors on they
+ * are decoded once into the workspace as bf16 rows and loaded by TMA (the same products, bit for bit). Each group's x
+ * is 16-byte aligned with ldx a multiple of 8; all groups take nvec vectors. Groups may read different inputs (a
+ * layer's stages): one launch takes up to 16 groups over up to 4 inputs, the groups of the longest rows first.
+ * y_bf16: 0 writes fp32 outputs, 1 bf16. workspace: lamq_trellis_gemm_workspace_size(groups, ngroups, nvec) bytes of
+ * device memory, 16-byte aligned (0, and NULL allowed, up to 512 vectors). status (device int, 0 on entry) becomes
+ * LAMQ_ERR_TIMEOUT if a device wait gives up. `groups` is host memory, read before the call returns.
  */
-int lamq_trellis_gemm(const lamq_gemm_group *groups, int ngroups, int n, const uint16_t *x, int64_t ldx,
-                      int64_t nvec, int y_bf16, int *status, lamq_stream_t stream);
+size_t lamq_trellis_gemm_workspace_size(const lamq_gemm_group *groups, int ngroups, int64_t nvec);
+int lamq_trellis_gemm(const lamq_gemm_group *groups, int ngroups, int64_t nvec, int y_bf16, void *workspace,
+                      size_t workspace_bytes, int *status, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -58,7 +58,8 @@ SIGNATURES = {
     "lamq_decode_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _P]),
     "lamq_trellis_product": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P]),
     "lamq_trellis_product_groups": (_I32, [_P, _I32, _I32, _P, _I64, _I32, _P]),
-    "lamq_trellis_gemm": (_I32, [_P, _I32, _I32, _P, _I64, _I64, _I32, _P, _P]),
+    "lamq_trellis_gemm_workspace_size": (_SZ, [_P, _I32, _I64]),
+    "lamq_trellis_gemm": (_I32, [_P, _I32, _I64, _I32, _P, _SZ, _P, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64, _I32]),
     "lamq_ldlq_rowtrellis": (_I32, [_P, _I64, _I64, _I32, _P, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
                                     _P, _P, _P, _SZ, _P]),
@@ -72,9 +73,10 @@ class ProductGroup(_c.Structure):
 
 
 class GemmGroup(_c.Structure):
-    """lamq_gemm_group: one row group of a trellis-dequant GEMM (80 bytes, the header's field order)."""
+    """lamq_gemm_group: one row group of a trellis-dequant GEMM and its input (104 bytes, the header's field order)."""
     _fields_ = [("codes", _P), ("states", _P), ("lds", _I64), ("rows", _I64), ("k", _I32), ("L", _I32),
-                ("scales", _P), ("table", _P), ("map", _P), ("y", _P), ("ldy", _I64)]
+                ("scales", _P), ("table", _P), ("map", _P), ("y", _P), ("ldy", _I64), ("x", _P), ("ldx", _I64),
+                ("n", _I32), ("reserved", _I32)]
 
 
 class LamqError(RuntimeError):

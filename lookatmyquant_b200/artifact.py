@@ -237,31 +237,63 @@ def _bf16_operand(x: torch.Tensor, device) -> torch.Tensor:
     return buf[:, :n]
 
 
-def gemm_groups(groups: list, n: int, x: torch.Tensor, y_bf16: bool = False):
-    """lamq_trellis_gemm over `groups` (lamq_gemm_group structures) that all read x (nvec × n, bf16 operand)."""
-    device = x.device
-    if not groups:
-        return
+def gemm_groups(groups: list, nvec: int, device, y_bf16: bool = False):
+    """lamq_trellis_gemm over `groups` (lamq_gemm_group structures, each with its bf16 input); returns the status
+    word (device int32)."""
     status = torch.zeros(1, dtype=torch.int32, device=device)
+    if not groups:
+        return status
+    lib = _lib.load()
     arr = (_lib.GemmGroup * len(groups))(*groups)
+    need = lib.lamq_trellis_gemm_workspace_size(arr, len(groups), nvec)
+    ws = torch.empty(need, dtype=torch.uint8, device=device) if need else None
     with torch.cuda.device(device):
-        check(_lib.load().lamq_trellis_gemm(arr, len(groups), n, ptr(x), x.stride(0), x.shape[0], 1 if y_bf16 else 0,
-                                            ptr(status), stream_ptr(device)), "lamq_trellis_gemm")
+        check(lib.lamq_trellis_gemm(arr, len(groups), nvec, 1 if y_bf16 else 0, ptr(ws), need, ptr(status),
+                                    stream_ptr(device)), "lamq_trellis_gemm")
     return status
 
 
 def _gemm_product(pairs: list, xr: torch.Tensor):
     """Every row group of the (TrellisProduct, y) pairs times xr (nvec × n) on the tensor cores, one launch."""
-    device, n = pairs[0][0].device, pairs[0][0].n
-    x = _bf16_operand(xr, device)
-    groups = []
-    for prod, y in pairs:
-        for g, codes, rows, scales, table in prod.groups:
-            groups.append(_lib.GemmGroup(ptr(codes), None, 0, rows.numel(), g["bits"], g["state_bits"], ptr(scales),
-                                         ptr(table), ptr(rows), ptr(y), y.stride(0)))
-    status = gemm_groups(groups, n, x)
-    if status is not None and int(status.item()):
-        _lib.check(int(status.item()), "lamq_trellis_gemm")
+    _gemm_layer([(pairs, xr)])
+
+
+def _gemm_layer(stages: list):
+    """[(pairs, xr)]: each stage's (TrellisProduct, y) pairs times its rotated input xr, all in as few launches as
+    lamq_trellis_gemm allows (16 groups and 4 inputs a launch)."""
+    device = stages[0][0][0][0].device
+    nvec = stages[0][1].shape[0]
+    groups, keep = [], []
+    for pairs, xr in stages:
+        x = _bf16_operand(xr, device)
+        keep.append(x)
+        for prod, y in pairs:
+            for g, codes, rows, scales, table in prod.groups:
+                groups.append(_lib.GemmGroup(ptr(codes), None, 0, rows.numel(), g["bits"], g["state_bits"],
+                                             ptr(scales), ptr(table), ptr(rows), ptr(y), y.stride(0), ptr(x),
+                                             x.stride(0), x.shape[1], 0))
+    status = gemm_groups(groups, nvec, device)
+    st = int(status.item())
+    if st:
+        _lib.check(st, "lamq_trellis_gemm")
+
+
+def product_layer(stages: list) -> list:
+    """[product_rotated(products, xr) for (products, xr) in stages] with every row group of every stage in one
+    tensor-core launch per 16 groups (for many vectors; few vectors take the per-stage grouped product). `stages`:
+    [(products, xr)], xr the stage's rotated input (nvec × n), the same nvec for all."""
+    if not stages:
+        return []
+    nvec = stages[0][1].shape[0]
+    if nvec < GEMM_PRODUCT_VECTORS:
+        return [product_rotated(ps, xr) for ps, xr in stages]
+    outs, work = [], []
+    for ps, xr in stages:
+        ys = [torch.empty(nvec, p.m, dtype=torch.float32, device=p.device) for p in ps]
+        outs.append(ys)
+        work.append((list(zip(ps, ys)), xr))
+    _gemm_layer(work)
+    return outs
 
 
 def _grouped_product(pairs: list, xr: torch.Tensor):

@@ -67,6 +67,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *st
     }
 }
 
+// As mbar_wait, with acquire semantics at cluster scope: for barriers that the other CTA of a pair arrives on after
+// writing shared memory the waiting thread's tensor-core operations then read.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *status) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 255u) == 0u) {
+            if (*reinterpret_cast<volatile int *>(status) != 0) return false;
+            if (globaltimer() - t0 > kWaitTimeoutNs) {
+                atomicCAS(status, 0, 4 /* LAMQ_ERR_TIMEOUT */);
+                return false;
+            }
+        }
+    }
+}
+
 // 2-D TMA tile load into shared memory, completing on the mbarrier (transaction bytes).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
     asm volatile(

@@ -156,9 +156,57 @@ class Probe:
         return self.ref.kl(self.hidden(start), self.w)
 
 
+def pieces(layers, n_layers: int) -> list:
+    """The linear pieces of `layers` in the reference's measure order (layer, stage, matrix): (layer, block, stage
+    index, matrix index, name) each."""
+    out = []
+    for i in layers:
+        for si, (block, names) in enumerate(STAGES):
+            for j, name in enumerate(names):
+                out.append((i, block, si, j, name))
+    return out
+
+
+def assign_pieces(items: list, n_layers: int, world: int) -> list:
+    """Pieces per rank for a sweep split across `world` ranks: each piece (all of its options) goes to one rank, the
+    costliest first onto the least loaded rank. A probe of layer i re-runs layers i..n_layers − 1 (the earlier layers'
+    outputs are cached), so its cost is taken as n_layers − i + 1. Every rank computes the same assignment from the
+    same list; no communication is needed. The reference splits the same item space by layer span, one job each
+    (run_batch.py:40-43); pieces balance better than spans because late layers are cheaper to probe."""
+    load = [0.0] * world
+    owned = [[] for _ in range(world)]
+    for k in sorted(range(len(items)), key=lambda k: (-(n_layers - items[k][0] + 1), k)):
+        r = min(range(world), key=lambda q: (load[q], q))
+        load[r] += n_layers - items[k][0] + 1
+        owned[r].append(k)
+    return [sorted(o) for o in owned]
+
+
+def gather_records(res: dict, group, order: list) -> dict:
+    """All ranks' records in the single-rank order (`order`: item names in sweep order), with the job's probe count
+    and the slowest rank's seconds in probes (what the whole job waits for)."""
+    import torch.distributed as dist
+    parts = [None] * dist.get_world_size(group)
+    dist.all_gather_object(parts, {"records": res["records"], "seconds in probes": res["seconds in probes"],
+                                   "probes": res["probes"]}, group=group)
+    rank_of = {name: k for k, name in enumerate(order)}
+    recs = sorted((r for part in parts for r in part["records"]),
+                  key=lambda r: (rank_of[r["item"]], r["option"]))
+    slowest = max(part["seconds in probes"] for part in parts)
+    probes = sum(part["probes"] for part in parts)
+    out = dict(res)
+    out.update({"records": recs, "probes": probes, "seconds in probes": slowest,
+                "probes per hour": 3600.0 * probes / slowest if slowest else None,
+                "seconds in probes per rank": [part["seconds in probes"] for part in parts]})
+    return out
+
+
 def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, windows: int = 8, T: int = 2048,
-        calib: int = 16, chunk: int = 4, kl_batch: int = 2, seed: int = 0, device="cuda", log=print) -> dict:
-    """The measure sweep over the linear pieces of `layers`: returns the records and the timing."""
+        calib: int = 16, chunk: int = 4, kl_batch: int = 2, seed: int = 0, device="cuda", log=print,
+        rank: int = 0, world: int = 1, group=None) -> dict:
+    """The measure sweep over the linear pieces of `layers`: returns the records and the timing. With world > 1 this
+    rank probes only its share of the pieces (assign_pieces) on its own model replica, and with a process group the
+    ranks' records are gathered (every rank returns the whole sweep)."""
     dev = torch.device(device)
     t_all = time.time()
     model = build_model(n_layers, seed, dev)
@@ -177,45 +225,56 @@ def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, wind
     trellis = {}
     recs, t_probe, n_probe = [], 0.0, 0
     layers = list(layers)
+    items = pieces(layers, n_layers)
+    mine = set(assign_pieces(items, n_layers, world)[rank]) if world > 1 else set(range(len(items)))
+    mine_layers = sorted({items[k][0] for k in mine})
     groups = [layers[k:k + 4] for k in range(0, len(layers), 4)]
-    for group in groups:
-        H = capture(model, group, chunks)
-        for i in group:
+    for grp in groups:
+        if not any(i in mine_layers for i in grp):
+            continue
+        H = capture(model, grp, chunks)
+        for k, (i, block, si, j, name) in enumerate(items):
+            if i not in grp or k not in mine:
+                continue
             L = model.model.layers[i]
-            for block, names in STAGES:
-                Hs = H[(i, names[0])]
-                for j, name in enumerate(names):
-                    mod = L.get_submodule(name)
-                    orig = mod.weight.data.clone()
-                    W = orig.double()
-                    m, n = W.shape
-                    Tm = T_tr if m % T_tr == 0 else next(t for t in (320, 256, 128, 64) if m % t == 0)
-                    seed_ = 1000 * i + 100 * BLOCK_SEED[block] + j
-                    for o in options:
-                        k = int(o[2:])
-                        if (k, Tm) not in trellis:
-                            trellis[(k, Tm)] = codes.TrellisCode(12, k, T=Tm)
-                        ts = time.time()
-                        word = codes.ldlq_words([W], Hs, trellis[(k, Tm)], [seed_])[0]
-                        mod.weight.data = word.matrix().to(torch.bfloat16)
-                        d = probe.kl(start=i) - floor
-                        mod.weight.data = orig
-                        dt = time.time() - ts
-                        t_probe += dt
-                        n_probe += 1
-                        recs.append({"item": f"{i}.{name}", "layer": i, "role": name, "shape": [m, n], "T": Tm,
-                                     "option": o, "bits": word.rate_bits(), "dkl": d, "seconds": round(dt, 4)})
-                    log(f"  layer {i} {name}: " + ", ".join(f"{r['option']} {r['dkl']:.3e}" for r in recs[-len(options):]))
-    return {"records": recs, "kl floor": floor, "probes": n_probe, "seconds in probes": t_probe,
-            "probes per hour": 3600.0 * n_probe / t_probe if t_probe else None, "seconds per kl": t_kl,
-            "seconds for the reference distribution": t_ref, "seconds": time.time() - t_all,
-            "held windows": [windows, T], "calibration": [calib, T]}
+            Hs = H[(i, STAGES[si][1][0])]
+            mod = L.get_submodule(name)
+            orig = mod.weight.data.clone()
+            W = orig.double()
+            m, n = W.shape
+            Tm = T_tr if m % T_tr == 0 else next(t for t in (320, 256, 128, 64) if m % t == 0)
+            seed_ = 1000 * i + 100 * BLOCK_SEED[block] + j
+            for o in options:
+                kbits = int(o[2:])
+                if (kbits, Tm) not in trellis:
+                    trellis[(kbits, Tm)] = codes.TrellisCode(12, kbits, T=Tm)
+                ts = time.time()
+                word = codes.ldlq_words([W], Hs, trellis[(kbits, Tm)], [seed_])[0]
+                mod.weight.data = word.matrix().to(torch.bfloat16)
+                d = probe.kl(start=i) - floor
+                mod.weight.data = orig
+                dt = time.time() - ts
+                t_probe += dt
+                n_probe += 1
+                recs.append({"item": f"{i}.{name}", "layer": i, "role": name, "shape": [m, n], "T": Tm,
+                             "option": o, "bits": word.rate_bits(), "dkl": d, "seconds": round(dt, 4)})
+            log(f"  layer {i} {name}: " + ", ".join(f"{r['option']} {r['dkl']:.3e}" for r in recs[-len(options):]))
+    res = {"records": recs, "kl floor": floor, "probes": n_probe, "seconds in probes": t_probe,
+           "probes per hour": 3600.0 * n_probe / t_probe if t_probe else None, "seconds per kl": t_kl,
+           "seconds for the reference distribution": t_ref, "seconds": time.time() - t_all,
+           "held windows": [windows, T], "calibration": [calib, T], "rank": rank, "world": world}
+    if group is not None and world > 1:
+        res = gather_records(res, group, [f"{i}.{name}" for i, _, _, _, name in items])
+    return res
 
 
 def main():
     """`python -m lookatmyquant_b200.measure [--layers A:B] [--windows 8] [--T 2048]`: the config-4 KL probes over the
-    linear pieces of the chosen layers of a random SmolLM2-360M-architecture model; prints one JSON summary."""
+    linear pieces of the chosen layers of a random SmolLM2-360M-architecture model; prints one JSON summary. Under
+    torch.distributed.run each rank takes its share of the pieces on its own GPU and rank 0 prints the whole sweep."""
     import argparse
+    import datetime
+    import os
     ap = argparse.ArgumentParser(description=main.__doc__)
     ap.add_argument("--layers", default="0:1")
     ap.add_argument("--model-layers", type=int, default=32)
@@ -226,12 +285,27 @@ def main():
     ap.add_argument("--out", default=None)
     a = ap.parse_args()
     lo, hi = (int(x) for x in a.layers.split(":"))
-    res = run(range(lo, hi), a.options, a.model_layers, a.windows, a.T, a.calib)
-    summary = {k: v for k, v in res.items() if k != "records"}
-    print(json.dumps(summary), flush=True)
-    if a.out:
-        with open(a.out, "w") as f:
-            json.dump(res, f, indent=1)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, group = int(os.environ.get("RANK", "0")), None
+    device = "cuda"
+    if world > 1:
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        device = f"cuda:{local}"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        group = dist.group.WORLD
+    res = run(range(lo, hi), a.options, a.model_layers, a.windows, a.T, a.calib, device=device,
+              log=print if rank == 0 else (lambda s: None), rank=rank, world=world, group=group)
+    if rank == 0:
+        summary = {k: v for k, v in res.items() if k != "records"}
+        print(json.dumps(summary), flush=True)
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(res, f, indent=1)
+    if group is not None:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -245,15 +245,15 @@ def run(device="cuda", log=print, only=None) -> list:
 
             def product():
                 xr = {st: layer[nm][0].rotate(xs[st]) for st, nm in first.items()}
-                return [y for st, ps in stages.items() for y in artifact.product_rotated(ps, xr[st])]
+                return artifact.product_layer([(ps, xr[st]) for st, ps in stages.items()])
             if batch >= artifact.GEMM_PRODUCT_VECTORS:
                 ms = timer(product)
                 add(_record("a14", "input rotation per stage + trellis_gemm_kernel (decode fused into tcgen05 GEMM)",
                             f"layer, batch {batch}", ms, 2.0 * batch * weights, "TFLOP/s", bf16,
                             "weights decoded from the packed states into shared memory, never written", "tensor"))
                 xr = {st: layer[nm][0].rotate(xs[st]) for st, nm in first.items()}
-                ms = timer(lambda: [artifact.product_rotated(ps, xr[st]) for st, ps in stages.items()])
-                add(_record("a14", "trellis_gemm_kernel alone (rotated inputs given, one launch per stage)",
+                ms = timer(lambda: artifact.product_layer([(ps, xr[st]) for st, ps in stages.items()]))
+                add(_record("a14", "trellis_gemm_kernel alone (rotated inputs given, the layer's groups in 2 launches)",
                             f"layer, batch {batch}", ms, 2.0 * batch * weights, "TFLOP/s", bf16,
                             f"codes {code_bytes / 1e6:.1f} MB per pass", "tensor"))
                 continue

@@ -88,9 +88,8 @@ INVALID = [
     ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, -1, N, 4, N), b"bad vector shape"),
     ("lamq_trellis_product_groups", (N, 1, 0, N, 32, 1, N), b"bad shape"),
     ("lamq_trellis_product_groups", (N, 1, 32, N, 32, 1, N), b"null pointer"),
-    ("lamq_trellis_gemm", (N, 1, 0, N, 32, 64, 0, N, N), b"bad shape"),
-    ("lamq_trellis_gemm", (N, 1, 32, N, 32, 64, 0, N, N), b"null pointer"),
-    ("lamq_trellis_gemm", (P, 1, 32, P + 8, 32, 64, 0, P, N), b"16-byte aligned"),
+    ("lamq_trellis_gemm", (N, 1, -1, 0, N, 0, N, N), b"bad shape"),
+    ("lamq_trellis_gemm", (N, 1, 64, 0, N, 0, N, N), b"null pointer"),
 ]
 
 # Empty inputs are a successful no-op, as the reference's loops over no rows are.
@@ -114,8 +113,8 @@ EMPTY = [
     ("lamq_decode_trellis", (N, 0, 32, 2, 12, N, N, N, N, 32, N)),
     ("lamq_trellis_product", (N, 4, 32, 2, 12, N, N, N, N, 32, 0, N, 4, N)),
     ("lamq_trellis_product_groups", (N, 0, 32, N, 32, 1, N)),
-    ("lamq_trellis_gemm", (N, 0, 32, N, 32, 64, 0, N, N)),
-    ("lamq_trellis_gemm", (P, 1, 32, P, 32, 0, 0, P, N)),
+    ("lamq_trellis_gemm", (N, 0, 64, 0, N, 0, N, N)),
+    ("lamq_trellis_gemm", (P, 1, 0, 0, N, 0, P, N)),
 ]
 
 
@@ -159,19 +158,31 @@ def test_product_group_layout_matches_the_header(lib):
 
 
 def test_gemm_group_layout_matches_the_header(lib):
-    """The ctypes lamq_gemm_group reaches the library field for field: the checks quote rows, k and L back."""
-    assert ctypes.sizeof(_lib.GemmGroup) == 80
-    x = (ctypes.c_uint16 * 64)()
-    xp = (ctypes.addressof(x) + 15) // 16 * 16
+    """The ctypes lamq_gemm_group reaches the library field for field: the checks quote rows, n, k and L back."""
+    assert ctypes.sizeof(_lib.GemmGroup) == 104
     st = ctypes.c_int(0)
-    one = [_lib.GemmGroup(None, None, 0, 0, 1, 12, None, None, None, None, 0),
-           _lib.GemmGroup(None, None, 0, -3, 1, 12, None, None, None, None, 0)]
-    arr = (_lib.GemmGroup * 2)(*one)
-    assert lib.lamq_trellis_gemm(arr, 2, 16, xp, 16, 1, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+
+    def grp(codes, states, lds, rows, k, L, x=P + 16, ldx=16, n=16):
+        return _lib.GemmGroup(codes, states, lds, rows, k, L, P, P, None, P, max(rows, 4), x, ldx, n, 0)
+    arr = (_lib.GemmGroup * 2)(grp(None, None, 0, 0, 1, 12), grp(None, None, 0, -3, 1, 12))
+    assert lib.lamq_trellis_gemm(arr, 2, 1, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
     assert b"group 1 has -3 rows" in lib.lamq_last_error()
-    arr[1] = _lib.GemmGroup(P, None, 0, 4, 5, 12, P, P, None, P, 4)
-    assert lib.lamq_trellis_gemm(arr, 2, 16, xp, 16, 1, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+    arr[1] = grp(P, None, 0, 4, 5, 12)
+    assert lib.lamq_trellis_gemm(arr, 2, 1, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
     assert b"group 1: packed widths" in lib.lamq_last_error() and b"(k 5, L 12)" in lib.lamq_last_error()
-    arr[1] = _lib.GemmGroup(P, P, 16, 4, 2, 12, P, P, None, P, 4)
-    assert lib.lamq_trellis_gemm(arr, 2, 16, xp, 16, 1, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+    arr[1] = grp(P, P, 16, 4, 2, 12)
+    assert lib.lamq_trellis_gemm(arr, 2, 1, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
     assert b"not both" in lib.lamq_last_error()
+    arr[1] = grp(P, None, 0, 4, 2, 12, x=P + 8)
+    assert lib.lamq_trellis_gemm(arr, 2, 1, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+    assert b"16-byte aligned" in lib.lamq_last_error()
+    arr[1] = grp(P, None, 0, 4, 2, 12, ldx=8, n=16)
+    assert lib.lamq_trellis_gemm(arr, 2, 1, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+    assert b"bad input shape (n 16, ldx 8)" in lib.lamq_last_error()
+    # from 513 vectors the weights are decoded once into a workspace of rows x ceil(n / 8)·8 bf16
+    arr[0] = grp(P, None, 0, 300, 2, 12, n=100, ldx=104)
+    arr[1] = grp(P, None, 0, 0, 2, 12)
+    assert lib.lamq_trellis_gemm_workspace_size(arr, 2, 512) == 0
+    assert lib.lamq_trellis_gemm_workspace_size(arr, 2, 513) == 300 * 104 * 2
+    assert lib.lamq_trellis_gemm(arr, 2, 513, 0, None, 0, ctypes.addressof(st), None) == _lib.LAMQ_ERR_INVALID
+    assert b"workspace of 62400 bytes" in lib.lamq_last_error()

@@ -47,3 +47,17 @@ def test_probe_from_a_cached_layer_input_equals_the_full_forward():
     assert torch.equal(probe.hidden(start=1), probe.hidden())
     assert probe.kl(start=1) == probe.kl() and probe.kl() > 0
     mod.weight.data = orig
+
+
+def test_sweep_split_by_piece_equals_the_whole_sweep():
+    """Two ranks' shares of the sweep (run one after the other on this GPU, each with its own model replica) hold
+    every piece once, and each record's KL equals the single-rank sweep's exactly."""
+    from lookatmyquant_b200 import measure
+    kw = dict(layers=range(2), options=("tr2",), n_layers=2, windows=2, T=128, calib=2, chunk=2, log=lambda s: None)
+    whole = measure.run(**kw)
+    parts = [measure.run(**kw, rank=r, world=2) for r in range(2)]
+    assert sum(p["probes"] for p in parts) == whole["probes"] == 14
+    got = {(r["item"], r["option"]): r["dkl"] for p in parts for r in p["records"]}
+    want = {(r["item"], r["option"]): r["dkl"] for r in whole["records"]}
+    assert got == want
+    assert {r["item"] for r in parts[0]["records"]}.isdisjoint({r["item"] for r in parts[1]["records"]})

@@ -46,8 +46,8 @@ def _run(groups, n, x, m, y_bf16=False):
                    dtype=torch.bfloat16 if y_bf16 else torch.float32)
     descs = [_lib.GemmGroup(ptr(g["codes"]), None if g["codes"] is not None else ptr(g["states"]),
                             g["states"].stride(0), g["rows"].numel(), g["k"], 12, ptr(g["scales"]), ptr(g["table"]),
-                            ptr(g["rows"]), ptr(y), y.stride(0)) for g in groups]
-    status = A.gemm_groups(descs, n, x, y_bf16)
+                            ptr(g["rows"]), ptr(y), y.stride(0), ptr(x), x.stride(0), n, 0) for g in groups]
+    status = A.gemm_groups(descs, x.shape[0], x.device, y_bf16)
     assert int(status.item()) == 0
     return y
 
@@ -100,6 +100,30 @@ def test_gemm_is_deterministic_and_many_groups():
     assert (y1.double() - ref).abs().max() <= 1e-5 * ref.abs().max()
 
 
+def test_layer_in_one_launch_equals_stage_by_stage():
+    """Groups over different inputs (a layer's stages: three inputs of 2560, 4096 and 9728 columns, 17 groups, so
+    two launches) give every output exactly what each stage's own launch gives."""
+    from lookatmyquant_b200 import _lib, artifact as A
+    from lookatmyquant_b200._lib import ptr
+    nvec = 300
+    specs = [(640, 2560, [1, 2, 3, 4, 2, 3]), (384, 4096, [2, 3, 4, 1, 2]), (300, 9728, [3, 1, 4, 2, 2, 3])]
+    stages = []
+    for m, n, widths in specs:
+        groups = _groups(m, n, widths, m + n)
+        x = torch.randn(nvec, n, generator=torch.Generator().manual_seed(n)).to(torch.bfloat16).cuda()
+        stages.append((m, n, groups, x))
+    alone = [_run(groups, n, x, m) for m, n, groups, x in stages]
+    ys = [torch.full((nvec, m), float("nan"), device="cuda") for m, _, _, _ in stages]
+    descs = [_lib.GemmGroup(ptr(g["codes"]), None, 0, g["rows"].numel(), g["k"], 12, ptr(g["scales"]),
+                            ptr(g["table"]), ptr(g["rows"]), ptr(y), y.stride(0), ptr(x), x.stride(0), n, 0)
+             for (m, n, groups, x), y in zip(stages, ys) for g in groups]
+    assert len(descs) == 17
+    st = A.gemm_groups(descs, nvec, torch.device("cuda"))
+    assert int(st.item()) == 0
+    for y, ref in zip(ys, alone):
+        assert torch.equal(y, ref)
+
+
 def test_trellis_product_uses_the_gemm_from_64_vectors(golden):
     """TrellisProduct on the reference's packed entry (artifact.npz): from 64 vectors the tensor-core GEMM, within
     the config-5 bar of the fp64 product of the reference's decoded weights."""
@@ -124,3 +148,18 @@ def test_trellis_product_uses_the_gemm_from_64_vectors(golden):
     xr = Rotation.from_signs(torch.as_tensor(g["signs"]).double()).rows(x).cpu().numpy()
     ref = xr @ g["decoded"].astype(np.float64).T
     assert np.abs(y - ref).max() <= 1e-2 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("nvec", [513, 1000, 2048])
+def test_decode_once_mode_equals_the_fused_decode(nvec):
+    """From 513 vectors the weights are decoded once into the workspace and fed by TMA: the same products as the
+    fused decode of the same groups, block of 512 vectors by block, bit for bit (packed and int16 sources, ragged n)."""
+    m, n = 700, 2504
+    for states_source in (False, True):
+        groups = _groups(m, n, [4, 1, 3, 2], 3 * nvec, states_source=states_source)
+        x = torch.randn(nvec, n, generator=torch.Generator().manual_seed(nvec)).to(torch.bfloat16).cuda()
+        y = _run(groups, n, x, m)
+        parts = [_run(groups, n, x[v:v + 512], m) for v in range(0, nvec, 512)]
+        assert torch.equal(y, torch.cat(parts))
+        ref = _reference(groups, x, m)
+        assert (y.double() - ref).abs().max() <= 1e-5 * ref.abs().max()

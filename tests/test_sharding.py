@@ -136,3 +136,53 @@ def test_four_gloo_ranks_share_factors_from_their_owners():
         p.join(60)
         assert p.exitcode == 0
     assert all(ok for _, ok in out), out
+
+
+def test_measure_pieces_are_assigned_once_and_balanced():
+    from lookatmyquant_b200.measure import assign_pieces, pieces
+    items = pieces(range(32), 32)
+    assert len(items) == 224  # the config-4 sweep: 7 linear pieces a layer
+    for world in (1, 2, 3, 4, 8):
+        owned = assign_pieces(items, 32, world)
+        flat = sorted(k for o in owned for k in o)
+        assert flat == list(range(len(items)))
+        assert assign_pieces(items, 32, world) == owned  # every rank computes the same split
+        cost = [sum(32 - items[k][0] + 1 for k in o) for o in owned]
+        assert max(cost) - min(cost) <= 33  # within one piece's cost
+
+
+def _gather_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from lookatmyquant_b200.measure import assign_pieces, gather_records, pieces
+        items = pieces(range(3), 3)
+        order = [f"{i}.{name}" for i, _, _, _, name in items]
+        mine = assign_pieces(items, 3, world)[rank]
+        recs = [{"item": order[k], "option": o, "dkl": float(k)} for k in mine for o in ("tr2", "tr3")]
+        res = gather_records({"records": recs, "seconds in probes": 1.0 + rank, "probes": len(recs)},
+                             dist.group.WORLD, order)
+        q.put((rank, [r["item"] for r in res["records"]], res["probes"], res["seconds in probes"]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_measure_records_gather_in_sweep_order(world):
+    """The ranks' records come back on every rank in the single-rank sweep order, with the job's probe count and
+    the slowest rank's time."""
+    from lookatmyquant_b200.measure import pieces
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    items = pieces(range(3), 3)
+    want = [f"{i}.{name}" for i, _, _, _, name in items for _ in ("tr2", "tr3")]
+    for rank, got, probes, slowest in out:
+        assert got == want and probes == len(want) and slowest == float(world)
