@@ -332,3 +332,45 @@ def product_rotated(products: list, xr: torch.Tensor) -> list:
     else:
         _grouped_product(list(zip(products, ys)), xr.to(device, torch.float32).contiguous())
     return ys
+
+
+class TrellisLinear(torch.nn.Module):
+    """A linear layer whose weight is a trellis word (codes.TrellisWord: W = R_outᵀ·diag(S)·V[states]·R_in), applied
+    without forming W: y = R_outᵀ·(S ⊙ (V[states]·(R_in x))). The input rotation runs through the Kronecker factors
+    (fp64), the product on the tensor cores straight from the int16 states (lamq_trellis_gemm: bf16 operands, fp32
+    accumulation), the output rotation through the factors again; the result is cast to the input's dtype. This is
+    how the measure sweep's probe runs its quantized piece (the reference writes the dense word into the model,
+    compiler.py:220-229 with quantize.py:332-347)."""
+
+    def __init__(self, word, device=None):
+        super().__init__()
+        dev = torch.device(device or word.states.device)
+        self.word = word
+        self.out_features, self.in_features = word.states.shape
+        st = word.states.to(dev, torch.int16)
+        if st.stride(-1) != 1 or st.stride(0) % 8 or st.data_ptr() % 16 or self.in_features % 8:
+            ld = (self.in_features + 7) // 8 * 8
+            buf = torch.zeros(self.out_features, ld, dtype=torch.int16, device=dev)
+            buf[:, :self.in_features] = st
+            st = buf
+        self.states = st
+        self.scales = word.scales.to(dev, torch.float32).contiguous()
+        self.table = torch.as_tensor(word.values).to(dev, torch.float32).contiguous()
+        self.L = int(word.L)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        xf = x.reshape(-1, self.in_features)
+        xr = self.word.R_in.rows(xf.to(torch.float64).contiguous()) if self.word.R_in is not None else xf
+        xb = _bf16_operand(xr, self.states.device)
+        nvec = xb.shape[0]
+        z = torch.empty(nvec, self.out_features, dtype=torch.float32, device=self.states.device)
+        g = _lib.GemmGroup(None, ptr(self.states), self.states.stride(0), self.out_features, 0, self.L,
+                           ptr(self.scales), ptr(self.table), None, ptr(z), z.stride(0), ptr(xb), xb.stride(0),
+                           self.in_features, 0)
+        status = gemm_groups([g], nvec, z.device)
+        if self.word.R_out is not None:
+            z = self.word.R_out.rows_t(z.to(torch.float64))
+        if int(status.item()):
+            _lib.check(int(status.item()), "lamq_trellis_gemm")
+        return z.to(x.dtype).reshape(*shape[:-1], self.out_features)

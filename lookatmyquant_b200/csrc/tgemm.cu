@@ -522,7 +522,8 @@ struct DecodeParams {
     int ng;
 };
 
-constexpr int kDecodeThreads = 256, kDecodeItems = 64;  // 8-column chunks per thread
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeBlocksPerSm = 8;  // resident decode blocks per SM (8 KB of table each): the grid is one wave
 
 // bf16(table[state]) for every (row, column) of every group: a thread per 8 consecutive columns of a row (one
 // 16-byte store), the states cut from three stream words (or read as eight int16), the group's table in shared
@@ -542,6 +543,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_rows_kernel(const __gri
     const uint32_t lmask = (1u << g.L) - 1u;
     const int N = (g.n + 31) / 32 * 32;
     const int wpr = N / 32 * g.k;
+#pragma unroll 2
     for (int64_t it = (blockIdx.x - g.first_block) * kDecodeThreads + threadIdx.x; it < items;
          it += nblocks * kDecodeThreads) {
         const int64_t r = it / nch;
@@ -728,6 +730,9 @@ int run_gemm(const lamq_gemm_group *const *groups, int ngroups, int64_t nvec, in
             if (st) return st;
         }
         DecodeParams dp{};
+        int64_t total = 0;
+        for (int i = 0; i < ng; ++i) total += p.g[i].rows * (decoded_ld(p.n[p.g[i].input]) / 8);
+        const int64_t budget = (int64_t)num_sms() * kDecodeBlocksPerSm;
         int64_t blocks = 0;
         for (int i = 0; i < ng; ++i) {
             const GemmGroup &g = p.g[i];
@@ -744,8 +749,9 @@ int run_gemm(const lamq_gemm_group *const *groups, int ngroups, int64_t nvec, in
             d.ld = decoded_ld(n);
             d.out = scratch + base[g.input] + g.arow * d.ld;
             d.first_block = blocks;
-            const int64_t items = g.rows * (d.ld / 8);
-            blocks += std::max<int64_t>(1, (items + kDecodeThreads * kDecodeItems - 1) / (kDecodeThreads * kDecodeItems));
+            const int64_t items = g.rows * (d.ld / 8);  // one wave of blocks, split by each group's share of chunks
+            blocks += std::max<int64_t>(1, std::min<int64_t>((items + kDecodeThreads - 1) / kDecodeThreads,
+                                                             budget * items / std::max<int64_t>(total, 1)));
         }
         dp.ng = ng;
         LAMQ_REQUIRE(blocks <= INT_MAX, "lamq_trellis_gemm: decode grid too large");

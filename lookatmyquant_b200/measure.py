@@ -8,8 +8,10 @@ and option `word(option, W, H, seed, trellis)` (quantize.py:332-347: the column 
 
 Here: H from the tcgen05 statistics kernel (bf16 activations, as the reference's fp32 Xᵀ·X of the bf16 stream), the
 word from the column-trellis sweep kernel, the forward through the model's own bf16 layers — from the quantized
-piece's layer on, the earlier layers' outputs being kept from the reference pass (Probe) — and the KL from the fused
-LM-head/log-softmax/KL kernel (kl.KLReference) on the final hidden states — no logits are formed. The model is a
+piece's layer on, the earlier layers' outputs being kept from the reference pass (Probe) — with the quantized piece
+running as a TrellisLinear (the trellis-dequant tensor-core GEMM straight from the word's states and rotations, no
+dense weight), and the KL from the fused LM-head/log-softmax/KL kernel (kl.KLReference) on the final hidden states —
+no logits are formed. `dense_piece=True` writes the dense word into the model instead, as the reference does. The model is a
 random-initialised SmolLM2-360M-architecture Llama (weights N(0, 0.02²), bf16) and the windows are seeded Zipf tokens.
 """
 
@@ -21,6 +23,7 @@ import time
 import torch
 
 from . import codes
+from .artifact import TrellisLinear
 from .hessian import Statistics
 from .kl import KLReference
 
@@ -203,7 +206,7 @@ def gather_records(res: dict, group, order: list) -> dict:
 
 def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, windows: int = 8, T: int = 2048,
         calib: int = 16, chunk: int = 4, kl_batch: int = 2, seed: int = 0, device="cuda", log=print,
-        rank: int = 0, world: int = 1, group=None) -> dict:
+        rank: int = 0, world: int = 1, group=None, dense_piece: bool = False) -> dict:
     """The measure sweep over the linear pieces of `layers`: returns the records and the timing. With world > 1 this
     rank probes only its share of the pieces (assign_pieces) on its own model replica, and with a process group the
     ranks' records are gathered (every rank returns the whole sweep)."""
@@ -250,9 +253,17 @@ def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, wind
                     trellis[(kbits, Tm)] = codes.TrellisCode(12, kbits, T=Tm)
                 ts = time.time()
                 word = codes.ldlq_words([W], Hs, trellis[(kbits, Tm)], [seed_])[0]
-                mod.weight.data = word.matrix().to(torch.bfloat16)
-                d = probe.kl(start=i) - floor
-                mod.weight.data = orig
+                if dense_piece:
+                    mod.weight.data = word.matrix().to(torch.bfloat16)
+                    d = probe.kl(start=i) - floor
+                    mod.weight.data = orig
+                else:
+                    parent, leaf = L.get_submodule(name.rsplit(".", 1)[0]), name.rsplit(".", 1)[1]
+                    setattr(parent, leaf, TrellisLinear(word))
+                    try:
+                        d = probe.kl(start=i) - floor
+                    finally:
+                        setattr(parent, leaf, mod)
                 dt = time.time() - ts
                 t_probe += dt
                 n_probe += 1

@@ -61,3 +61,59 @@ def test_sweep_split_by_piece_equals_the_whole_sweep():
     want = {(r["item"], r["option"]): r["dkl"] for r in whole["records"]}
     assert got == want
     assert {r["item"] for r in parts[0]["records"]}.isdisjoint({r["item"] for r in parts[1]["records"]})
+
+
+def test_trellis_linear_matches_the_dense_word():
+    """The probe's quantized piece as a TrellisLinear (rotations through the factors, the tensor-core GEMM from the
+    int16 states) against x·Wᵀ with the dense word W = word.matrix(), within the bf16-operand bar (1e-2)."""
+    from lookatmyquant_b200 import codes
+    from lookatmyquant_b200.artifact import TrellisLinear
+    g = torch.Generator().manual_seed(3)
+    W = (0.02 * torch.randn(640, 960, generator=g, dtype=torch.float64)).cuda()
+    A = torch.randn(4096, 960, generator=g, dtype=torch.float64).cuda()
+    H = A.T @ A / 4096
+    word = codes.ldlq_words([W], H, codes.TrellisCode(12, 2, T=320), [7])[0]
+    x = torch.randn(2, 700, 960, generator=g).to(torch.bfloat16).cuda()
+    y = TrellisLinear(word)(x)
+    assert y.shape == (2, 700, 640) and y.dtype == torch.bfloat16
+    ref = x.double().reshape(-1, 960) @ word.matrix().T
+    assert (y.reshape(-1, 640).double() - ref).abs().max() <= 1e-2 * ref.abs().max()
+
+
+def test_trellis_linear_launches_no_library_gemm():
+    """The quantized piece's forward runs this library's kernels and torch's elementwise casts only: no cuBLAS or
+    other library GEMM."""
+    from torch.profiler import ProfilerActivity, profile
+    from lookatmyquant_b200 import codes
+    from lookatmyquant_b200.artifact import TrellisLinear
+    g = torch.Generator().manual_seed(4)
+    W = (0.02 * torch.randn(320, 960, generator=g, dtype=torch.float64)).cuda()
+    word = codes.ldlq_words([W], None, codes.TrellisCode(12, 3, T=320), [9])[0]
+    lin = TrellisLinear(word)
+    x = torch.randn(1024, 960, generator=g).to(torch.bfloat16).cuda()
+    lin(x)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        lin(x)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("trellis_gemm_kernel" in nm for nm in names)
+    assert any("rht_rows" in nm for nm in names)
+    library = [nm for nm in names if ("gemm" in nm.lower() or "cutlass" in nm.lower() or "xmma" in nm.lower())
+               and "lamq" not in nm]
+    assert not library, library
+
+
+def test_probe_kl_through_trellis_linear_matches_the_dense_piece():
+    """The sweep with each quantized piece as a TrellisLinear gives every record's KL within 1e-4 nats of the sweep
+    that writes the dense bf16 word into the model (the reference's way)."""
+    from lookatmyquant_b200 import measure
+    kw = dict(layers=range(2), options=("tr2", "tr4"), n_layers=2, windows=2, T=256, calib=2, chunk=2,
+              log=lambda s: None)
+    fused = measure.run(**kw)
+    dense = measure.run(**kw, dense_piece=True)
+    a = {(r["item"], r["option"]): r["dkl"] for r in fused["records"]}
+    b = {(r["item"], r["option"]): r["dkl"] for r in dense["records"]}
+    assert a.keys() == b.keys() and len(a) == 28
+    assert max(abs(a[k] - b[k]) for k in a) <= 1e-4
+    assert max(b.values()) > 1e-4  # the pieces do move the KL
