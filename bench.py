@@ -274,6 +274,7 @@ class Config3:
         tables = stacked_tables(12, 256, self.device)
         h_ms = sw_ms = 0.0
         h_flop = 0.0
+        self.h_accum = {}
         edges = 0
         sweep_bytes = 0
         for s in self.stages:
@@ -290,6 +291,9 @@ class Config3:
             # executed flops: H's triangle d(d+1)/2 and D's d^2 entries, 2 flops per token each, plus the weighted
             # tokens' own pass (one weight value here: each weighted token once more)
             h_flop += 2.0 * (ntok + nw) * (s.d * (s.d + 1) / 2 + s.d * s.d)
+            # BASELINE config 2's count: 2·N·d² for H (and as much again for D), N this rank's tokens
+            self.h_accum[s.name] = {"d": s.d, "tokens": ntok, "ms": a.elapsed_time(b),
+                                    "tflops_2Nd2": 2.0 * 2.0 * ntok * s.d * s.d / (a.elapsed_time(b) * 1e-3) / 1e12}
             H, D = st.finalize(self.tokens)
             rot = Rotation(s.d, 301, self.device)
             env = Environment(rot.conj(H))
@@ -386,50 +390,118 @@ def config1_cpu_sample(threads, W, H, in_seed, values):
                          f"{per_row * 1e3:.1f} ms per row ({t_w:.0f} s)")
 
 
-def config3_cpu_sample(threads, tokens=384 * 2048, stages=None):
-    """The reference's CPU path (the oracle port) on a bounded sample, extrapolated to one layer:
-    - the fp32 Hessian/QEP GEMMs on 8192 tokens at d = 2560, scaled by tokens and by d² over every stage's H and D;
-    - the work per stage that does not depend on its rows (R·H·Rᵀ, the environment, the QEP solve) at n = 2560,
-      scaled by n³ per stage, once per stage (the reference repeats it for every row group: a lower bound);
-    - the word work per width: seconds per call and per row fitted on 16 and 128 rows (words_fit), then
-      GROUPS_PER_MATRIX calls per matrix plus the stage's rows. The sweep's cost does not depend on U's values, so an
-      identity U stands in for the stage's.
-    The dense rotations are formed once per width, outside the timed work."""
-    from lookatmyquant_b200.layer import qwen3_4b_stages
+_FIXED_CACHE = {}
+
+
+def _ldlq_call_fixed_seconds(n):
+    """Seconds of the work the reference's ldlq_words repeats on every call at input width n, whatever the call's
+    rows (codes.py:425-439 with GPU_SWEEP off, torch on the CPU as the reference runs it): the dense rht(n), the
+    rotated statistics R·H·Rᵀ and the Environment's three factorizations (frame.py:515-522)."""
+    rng = np.random.default_rng(n)
+    A = torch.from_numpy(rng.standard_normal((n + 64, n)))
+    H = A.T @ A / (n + 64)
+    t0 = time.perf_counter()
+    R = torch.from_numpy(_dense_rotation(n, 301))  # formed by the reference per call (torch.kron), here from cache
+    Hr = R @ H @ R.T
+    Hr += 0.01 * torch.mean(torch.diag(Hr)) * torch.eye(n, dtype=Hr.dtype)
+    U = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(Hr)), upper=True)
+    del U
+    return time.perf_counter() - t0
+
+
+def _qep_seconds(n, rows):
+    """The QEP target of one stage (quantize.py:1330-1335, :1503): the ridge solve for M and W·M, torch fp64 on the
+    CPU."""
+    rng = np.random.default_rng(n + 1)
+    A = torch.from_numpy(rng.standard_normal((n + 64, n)))
+    H = A.T @ A / (n + 64)
+    D = 0.01 * H
+    W = torch.from_numpy(0.02 * rng.standard_normal((rows, n)))
+    t0 = time.perf_counter()
+    eye = torch.eye(n, dtype=H.dtype)
+    M = eye + 0.5 * torch.linalg.solve(H + 0.1 * torch.diag(H).mean() * eye, D.T).T
+    W @ M
+    return time.perf_counter() - t0
+
+
+CPU_SAMPLE_TOKENS = {2560: 16384, 4096: 8192, 9728: 2048}  # statistics sample per width (all tokens: ×48, ×96, ×384)
+
+
+def _h_seconds_per_token(d):
+    """The statistics GEMMs of one calibration token at width d: fp32 X_refᵀ(w⊙X) and Xᵀ(w⊙X) (quantize.py:1457-1470,
+    torch on the CPU as the reference runs them), timed on CPU_SAMPLE_TOKENS[d] tokens."""
     from lookatmyquant_b200.workloads import stage_activations, token_weights
+    nt = CPU_SAMPLE_TOKENS.get(d, 4096)
+    x, xr = (t.float() for t in stage_activations(nt, d, seed=3000 + d, device="cpu"))
+    w = token_weights(nt, seed=7, device="cpu").float()
+    t0 = time.perf_counter()
+    xw = x * w.reshape(-1, 1)
+    xr.T @ xw
+    x.T @ xw
+    return (time.perf_counter() - t0) / nt
+
+
+def _words_fit_at(d):
+    from lookatmyquant_b200.layer import qwen3_4b_stages  # noqa: F401  (the widths come from the layer)
+    values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
+    _warm_oracle(values)
+    W = 0.02 * np.random.default_rng(d).standard_normal((128, d))
+    return words_fit(W, _dense_rotation(d), np.eye(d), np.zeros(d, dtype=bool), values)
+
+
+def config3_components(stages=None):
+    """The pieces of the reference's CPU path for one config-3 layer that the CPU baseline times, each a bounded
+    sample: (key, function returning its measurement). A step of the reference arm times two of them."""
+    from lookatmyquant_b200.layer import qwen3_4b_stages
+    stages = stages or qwen3_4b_stages()
+    widths = sorted({s.d for s in stages})
+    comps = [(("h", d), (lambda d=d: _h_seconds_per_token(d))) for d in widths]
+    comps += [(("fixed", d), (lambda d=d: _ldlq_call_fixed_seconds(d))) for d in widths]
+    comps += [(("qep", s.name), (lambda s=s: _qep_seconds(s.d, sum(r for _, r in s.matrices)))) for s in stages]
+    comps += [(("words", d), (lambda d=d: _words_fit_at(d))) for d in widths]
+    return comps
+
+
+def config3_total(meas: dict, tokens=384 * 2048, stages=None):
+    """One layer's seconds from the components' measurements (each a list; the median is used), with every
+    extrapolation factor stated:
+    - statistics: seconds per token at each stage's width × the layer's tokens;
+    - per ldlq_words call, the work it repeats whatever its rows (R·H·Rᵀ, the Environment) at the stage's width ×
+      the calls (one per width group of every matrix, quantize.py:530-565);
+    - the QEP target per stage (solve and W·M) at full size;
+    - the word work (rotation, row scales, Viterbi sweep, dequantization) on the oracle port: a line fitted on 16 and
+      128 rows per width, its per-call part × the calls and its per-row part × the layer's rows."""
+    from lookatmyquant_b200.layer import qwen3_4b_stages
+    stages = stages or qwen3_4b_stages()
+    med = {k: (statistics.median(v) if not isinstance(v[0], tuple) else
+               tuple(statistics.median(x[i] for x in v) for i in range(2))) for k, v in meas.items()}
+    calls = {s.name: GROUPS_PER_MATRIX * len(s.matrices) for s in stages}
+    h = sum(med[("h", s.d)] * tokens for s in stages)
+    f = sum(calls[s.name] * med[("fixed", s.d)] for s in stages)
+    q = sum(med[("qep", s.name)] for s in stages)
+    w = sum(calls[s.name] * med[("words", s.d)][0] + sum(r for _, r in s.matrices) * med[("words", s.d)][1]
+            for s in stages)
+    widths = sorted({s.d for s in stages})
+    desc = [f"H/D fp32 GEMMs {h:.0f} s (" + ", ".join(f"d={d}: {CPU_SAMPLE_TOKENS.get(d, 4096)} of {tokens} tokens, "
+                                                      f"x{tokens / CPU_SAMPLE_TOKENS.get(d, 4096):.0f}" for d in widths) + ")",
+            "R·H·Rᵀ + Environment per ldlq_words call at full width (" +
+            ", ".join(f"{d}: {med[('fixed', d)]:.2f} s" for d in widths) + f") x{sum(calls.values())} calls: {f:.0f} s",
+            f"QEP solve + W·M per stage at full size: {q:.0f} s",
+            "row-trellis words fitted on 16 and 128 rows per width (" +
+            ", ".join(f"d={d}: {med[('words', d)][0]:.2f} s/call + {med[('words', d)][1] * 1e3:.1f} ms/row"
+                      for d in widths) + f") over the layer's {sum(r for s in stages for _, r in s.matrices)} rows: "
+            f"{w:.0f} s"]
+    return h + f + q + w, desc
+
+
+def config3_cpu_sample(threads, tokens=384 * 2048, stages=None):
+    """Every component timed once on this process's host threads (the repo arm's cpu_baseline leg)."""
     from oracle import core as O
     O.set_threads(threads)
     torch.set_num_threads(threads)
-    values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
-    _warm_oracle(values)
-    stages = stages or qwen3_4b_stages()
-    x, xr = (t.float().numpy() for t in stage_activations(8192, 2560, seed=3000, device="cpu"))
-    w = token_weights(8192, seed=7, device="cpu").numpy()
-    t0 = time.perf_counter()
-    O.hessian_accumulate([x], [w], [xr])
-    t_h = time.perf_counter() - t0
-    h_total = t_h * (tokens / 8192) * sum((s.d / 2560) ** 2 for s in stages)
-    rng = np.random.default_rng(0)
-    A = rng.standard_normal((4096, 2560))
-    Hs = A.T @ A / 4096
-    R = _dense_rotation(2560)
-    t0 = time.perf_counter()
-    O.environment(R @ Hs @ R.T)
-    O.cross_target(Hs, 0.01 * Hs, 0.5)
-    t_e = time.perf_counter() - t0
-    e_total = t_e * sum((s.d / 2560) ** 3 for s in stages)
-    fits = {}
-    for d in sorted({s.d for s in stages}):
-        W = 0.02 * rng.standard_normal((128, d))
-        fits[d] = words_fit(W, _dense_rotation(d), np.eye(d), np.zeros(d, dtype=bool), values)
-    t_w = sum(GROUPS_PER_MATRIX * len(s.matrices) * fits[s.d][0] + sum(r for _, r in s.matrices) * fits[s.d][1]
-              for s in stages)
-    per_row = ", ".join(f"d={d}: {a:.2f} s/call + {b * 1e3:.1f} ms/row" for d, (a, b) in fits.items())
-    v = h_total + e_total + t_w
-    return v, (f"oracle on {threads} host threads, extrapolated to one layer: H/D fp32 GEMMs on 8192 of {tokens} "
-               f"tokens ({h_total:.0f} s), R·H·Rᵀ + environment + QEP solve at n=2560 scaled by n^3 per stage "
-               f"({e_total:.0f} s), row-trellis words fitted on 16 and 128 rows per width ({per_row}) over "
-               f"{GROUPS_PER_MATRIX} calls per matrix and the layer's rows ({t_w:.0f} s)")
+    meas = {k: [fn()] for k, fn in config3_components(stages)}
+    v, desc = config3_total(meas, tokens, stages)
+    return v, f"oracle port and torch on {threads} host threads, one layer extrapolated: " + "; ".join(desc)
 
 
 WORKLOADS = {"config1": Config1, "config3": Config3}
@@ -472,34 +544,82 @@ def sweep_roofline(kms, algo_bytes, edges, pk):
                     "frac": fp32_achieved / fp32_peak, "note": "3 fp32 ops per trellis edge; the binding roofline"}}
 
 
+PROBE_LAYERS = (0, 16, 31)  # the config-4 sample: every linear piece of a first, a middle and the last layer
+
+
+def probe_sample(dev, rank, world, group):
+    """BASELINE config 4 on a bounded sample: the KL probes (tr2, tr3, tr4) of every linear piece of PROBE_LAYERS of
+    the 32-layer SmolLM2-360M-architecture model over 8 × 2048 held tokens, pieces split across the ranks; probes per
+    hour = the sample's probes / the slowest rank's seconds in probes (a probe's cost falls with its layer, so the
+    first, middle and last layers stand for the sweep's average)."""
+    from lookatmyquant_b200 import measure
+    torch.cuda.synchronize()
+    res = measure.run(layers=PROBE_LAYERS, n_layers=32, windows=8, T=2048, device=dev, log=lambda s: None,
+                      rank=rank, world=world, group=group)
+    return {"probes_per_hour": res["probes per hour"], "probes": res["probes"],
+            "seconds_in_probes": res["seconds in probes"], "layers": list(PROBE_LAYERS),
+            "held_tokens": 8 * 2048, "options": ["tr2", "tr3", "tr4"], "kl_floor": res["kl floor"],
+            "sweep": "224 pieces x 3 options = 672 probes", "piece": "TrellisLinear (trellis-dequant tensor-core GEMM)"}
+
+
 def run_reference(args):
-    """The reference arm: the CPU oracle port of the reference's path on all host threads, a bounded sample per step
-    extrapolated to the workload's unit. Rank 0 only."""
+    """The reference arm: the reference's CPU path (its torch arithmetic, and the oracle port of its sweep) on all
+    host threads. config3: every step times two of the layer's components (config3_components, in turn, each a
+    bounded sample), and the value is one layer extrapolated from the median of each component's timed measurements
+    (config3_total; the warm-up steps time every component once and are not used). config1: every step times the
+    whole sample and the value is the median. ms_per_step is a step's wall time. Rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    times, sample = [], ""
-    for i in range(args.warmup + args.steps):
-        if args.workload == "config3":
-            v, sample = config3_cpu_sample(threads)
-        else:
+    from oracle import core as O
+    O.set_threads(threads)
+    torch.set_num_threads(threads)
+    walls, sample = [], ""
+    if args.workload == "config3":
+        comps = config3_components()
+        warm = {}
+        for k, fn in comps:  # warm-up: every component once (not used)
+            warm[k] = [fn()]
+        meas = {}
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            for j in (2 * i, 2 * i + 1):
+                k, fn = comps[j % len(comps)]
+                meas.setdefault(k, []).append(fn())
+            walls.append(time.perf_counter() - t0)
+        for k in warm:  # a component no timed step reached keeps its warm-up measurement
+            meas.setdefault(k, warm[k])
+        v, desc = config3_total(meas)
+        counts = sorted({len(x) for x in meas.values()})
+        sample = (f"oracle port and torch on {threads} host threads, one layer extrapolated from the median of "
+                  f"{counts} timed samples per component: " + "; ".join(desc))
+        spread = None
+    else:
+        times = []
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
             from lookatmyquant_b200.workloads import config1
             W, H, seed, in_seed = config1()
             values = np.fromfile(ROOT / "lookatmyquant_b200" / "tables" / "trellis_L12_k2_T256_s0_ema.f64", "<f8")
-            v, sample = config1_cpu_sample(threads, W.numpy(), H.numpy(), in_seed, values)
-        if i >= args.warmup:
-            times.append(v)
-    v = statistics.mean(times)
+            x, sample = config1_cpu_sample(threads, W.numpy(), H.numpy(), in_seed, values)
+            if i >= args.warmup:
+                times.append(x)
+                walls.append(time.perf_counter() - t0)
+        v = statistics.median(times)
+        spread = (max(times) - min(times)) / v if v else 0.0
     metric = Config3.metric if args.workload == "config3" else Config1.metric
     cfg = {"workload": args.workload}
-    print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "s", "n_gpus": args.gpus,
-                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1e3, "higher_is_better": False,
-                      "scaling": "strong" if args.workload == "config3" else "weak", "vs_baseline": None,
-                      "dtype": "f64+f32", "data": "synthetic (seeded)", "config": cfg,
-                      "cpu_baseline": {"value": v, "unit": "s", "cores": threads, "kind": "port", "sample": sample},
-                      "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
-          flush=True)
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": "s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(walls) * 1e3,
+            "higher_is_better": False, "scaling": "strong" if args.workload == "config3" else "weak",
+            "vs_baseline": None, "dtype": "f64+f32", "data": "synthetic (seeded)", "config": cfg,
+            "value_is": "one layer (build) extrapolated from bounded CPU samples; ms_per_step is a step's wall time",
+            "cpu_baseline": {"value": v, "unit": "s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if spread is not None:
+        line["step_spread"] = spread
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -510,6 +630,7 @@ def main():
     ap.add_argument("--workload", default="config3", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-probes", action="store_true", help="skip the config-4 KL-probe sample")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -576,6 +697,13 @@ def main():
         "e2e": {"value": e2e / 1e3, "unit": "s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
     }
+    if getattr(wl, "h_accum", None):
+        # the metric's "H-accum TFLOP/s": config 2 is this statistics pass (786,432 weighted tokens; d = 2560 is the
+        # q/k/v and gate/up stages' input, d = 9728 the down_proj stage's), H and D, on each rank's token shard
+        line["h_accum_tflops"] = {k: {"d": v["d"], "tokens_per_rank": v["tokens"], "ms": round(v["ms"], 2),
+                                      "tflops": round(v["tflops_2Nd2"] * world, 1)} for k, v in wl.h_accum.items()}
+    if args.workload == "config3" and not args.no_probes:
+        line["config4"] = probe_sample(dev, rank, world, group)
     if getattr(wl, "stage_ms", None):
         # per-stage device time of the timed steps (this rank's; the step's all-gather of states is outside them)
         line["stage_ms"] = {k: round(statistics.mean(a.elapsed_time(b) for a, b in v), 2)
