@@ -28,6 +28,8 @@
  *   lamq_trellis_product_groups                       the same for all row groups that read one input, one launch
  *   lamq_trellis_gemm      fast_q35.py:69-201 with    many input vectors: the decode fused into a tcgen05 GEMM
  *                          compiler_artifact.py:433-442
+ *   lamq_square_sums       row_importance.py:57-93,   per-channel E[y²], E[g²] (row importance) and per-token Σ g²
+ *                          quantize.py:853-894        (GuidedQuant token weights)
  *   lamq_kl_reference,     compiler.py:176-187        the KL probe: ref_lp once, then per probe the KL of the held
  *   lamq_kl_head                                      positions' log_softmax(lm_head(h)) to it
  */
@@ -378,6 +380,21 @@ typedef struct lamq_gemm_group {
 size_t lamq_trellis_gemm_workspace_size(const lamq_gemm_group *groups, int ngroups, int64_t nvec);
 int lamq_trellis_gemm(const lamq_gemm_group *groups, int ngroups, int64_t nvec, int y_bf16, void *workspace,
                       size_t workspace_bytes, int *status, lamq_stream_t stream);
+
+/* Element types of lamq_square_sums. */
+#define LAMQ_F32 0
+#define LAMQ_BF16 1
+
+/*
+ * Sums of squares of x (rows x cols, leading dimension ld, fp32 or bf16) in fp64: col_acc[j] += Σ_r x[r][j]² (the
+ * per-output-channel E[y²] and E[g²] of row importance, row_importance.py:57-93, summed over windows by accumulating)
+ * and row_out[r] = Σ_j x[r][j]² (the per-token Σ of squared output gradients of GuidedQuant's token weights,
+ * quantize.py:853-894). Either output may be NULL. Deterministic (fixed summation order). Workspace (column sums
+ * only): lamq_square_sums_workspace_size(rows, cols) bytes.
+ */
+size_t lamq_square_sums_workspace_size(int64_t rows, int cols);
+int lamq_square_sums(const void *x, int dtype, int64_t rows, int cols, int64_t ld, double *col_acc, double *row_out,
+                     void *workspace, size_t workspace_bytes, lamq_stream_t stream);
 
 #ifdef __cplusplus
 }

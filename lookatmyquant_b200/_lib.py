@@ -16,6 +16,7 @@ _lib = None
 _lock = threading.Lock()
 
 LAMQ_OK, LAMQ_ERR_INVALID, LAMQ_ERR_CUDA, LAMQ_ERR_NOT_PD, LAMQ_ERR_TIMEOUT, LAMQ_ERR_NOT_PATH = range(6)
+LAMQ_F32, LAMQ_BF16 = 0, 1
 
 _c = ctypes
 _P, _I64, _I32, _SZ, _D = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_size_t, _c.c_double
@@ -58,6 +59,8 @@ SIGNATURES = {
     "lamq_decode_trellis": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _P]),
     "lamq_trellis_product": (_I32, [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P]),
     "lamq_trellis_product_groups": (_I32, [_P, _I32, _I32, _P, _I64, _I32, _P]),
+    "lamq_square_sums_workspace_size": (_SZ, [_I64, _I32]),
+    "lamq_square_sums": (_I32, [_P, _I32, _I64, _I32, _I64, _P, _P, _P, _SZ, _P]),
     "lamq_trellis_gemm_workspace_size": (_SZ, [_P, _I32, _I64]),
     "lamq_trellis_gemm": (_I32, [_P, _I32, _I64, _I32, _P, _SZ, _P, _P]),
     "lamq_ldlq_rowtrellis_workspace_size": (_SZ, [_I64, _I32]),

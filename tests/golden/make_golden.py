@@ -68,7 +68,8 @@ def calib_H(n, tokens, seed, dead=()):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word"],
+    ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word",
+                                       "embedding", "importance"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -98,6 +99,12 @@ def main():
         return
     if args.only == "best_word":
         write_best_word_fixture(C, Q, torch, args.reference.resolve())
+        return
+    if args.only == "embedding":
+        write_embedding_fixture(Q, torch)
+        return
+    if args.only == "importance":
+        write_importance_fixture(Q, torch, args.reference.resolve())
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -221,6 +228,8 @@ def main():
     write_statistics_fixture(torch, args.reference.resolve())
     write_kl_fixture(torch, Q)
     write_best_word_fixture(C, Q, torch, args.reference.resolve())
+    write_embedding_fixture(Q, torch)
+    write_importance_fixture(Q, torch, args.reference.resolve())
     print("golden vectors written to", HERE)
 
 
@@ -365,6 +374,98 @@ def write_best_word_fixture(C, Q, torch, ref: Path):
     np.savez_compressed(HERE / "best_word.npz", W=W.float().numpy(), H=H.float().numpy(),
                         meta=np.array([m, n, k, seed, nseeds]), errs=np.array(errs), chosen=np.array(chosen[0]),
                         states=Q.trellis_states(best.cores["W"].data, trellis[k].values).numpy())
+
+
+def write_embedding_fixture(Q, torch):
+    """14. Embedding buckets (quantize.py:350-465) by the reference's own embed_word: a column trellis over runs of
+    256 rows after a hidden-dimension rotation, with and without H (a lookup table pads 300 rows to 512), a centred
+    bucket, the prng bucket; embedding_buckets and frequency_order."""
+    out = {}
+    cases = [("a", 512, 64, "tr2", 7001, True, False), ("b", 300, 64, "tr3", 7002, False, False),
+             ("c", 256, 64, "tr2", 7003, True, True), ("d", 100, 64, "prng", 7004, False, False),
+             ("e", 256, 128, "tr4", 7005, True, False)]
+    for name, rows, n, prog, seed, with_h, center in cases:
+        W = (0.02 * torch.randn(rows, n, generator=torch.Generator().manual_seed(seed), dtype=torch.float64)).float().double()
+        H = calib_H(n, 1024, seed + 1) if with_h else None
+        net = Q.embed_word(W, H, prog, seed, center=center)
+        out[f"{name}_W"] = W.float().numpy()
+        if H is not None:
+            out[f"{name}_H"] = H.float().numpy()
+        out[f"{name}_meta"] = np.array([rows, n, seed, int(with_h), int(center)])
+        out[f"{name}_prog"] = np.array(prog)
+        out[f"{name}_Q"] = net.matrix(dtype=torch.float64).numpy()
+        out[f"{name}_bits"] = np.array(float(net.rate_bits()))
+    out["buckets_49152"] = np.array(Q.embedding_buckets(49152))
+    out["buckets_1000"] = np.array(Q.embedding_buckets(1000))
+    ids = torch.randint(0, 500, (4000,), generator=torch.Generator().manual_seed(9))
+    out["freq_ids"] = ids.numpy()
+    out["freq_order"] = Q.frequency_order(ids, 600).numpy()
+    np.savez_compressed(HERE / "embedding.npz", **out)
+
+
+def write_importance_fixture(Q, torch, ref: Path):
+    """15. Row importance (row_importance.py:57-93) and GuidedQuant token weights (quantize.py:853-894) on a tiny
+    random-init fp32 Llama (statgen.tiny_llama; its weights are stored): the importances E[g²]·E[y²] accumulated by
+    the reference's own hooks (the `keep` closure of row_importance.main, run from its source) over three windows
+    whose sampled tokens are recorded, and the reference's guided_weights itself (its draws recorded too)."""
+    import torch.nn.functional as F
+    sys.path.insert(0, str(HERE))
+    import statgen
+    model = statgen.tiny_llama()
+    for p in model.parameters():
+        p.requires_grad_(False)
+    layers = model.model.layers
+    mods = {f"{l}.{n}": m for l, L in enumerate(layers) for n, m in L.named_modules() if isinstance(m, torch.nn.Linear)}
+    g = torch.Generator().manual_seed(42)
+    windows = torch.randint(0, 1000, (3, 32), generator=g)
+    weight = (torch.rand(3, 32, generator=g) < 0.5).float()  # the positions that count (the reference's digits)
+    keep_code = _reference_code(ref / "row_importance.py", "main",
+                                lambda n, t: isinstance(n, ast_def()) and n.name == "keep")[0][2]
+    gg = {k: torch.zeros(m.out_features, dtype=torch.float64) for k, m in mods.items()}
+    yy = {k: torch.zeros(m.out_features, dtype=torch.float64) for k, m in mods.items()}
+    ns = {"gg": gg, "yy": yy, "torch": torch}
+    exec(keep_code, ns)
+    hooks = [m.register_forward_hook(ns["keep"](k)) for k, m in mods.items()]
+    gen = torch.Generator().manual_seed(0)
+    sampled = []
+    for i in range(len(windows)):  # the window loop of row_importance.py:66-80 (digit mask given as `weight`)
+        x = windows[i:i + 1]
+        emb = model.get_input_embeddings()(x).detach().requires_grad_(True)
+        lg = model(inputs_embeds=emb, use_cache=False).logits.float()
+        with torch.no_grad():
+            y = torch.multinomial(F.softmax(lg[0], -1), 1, generator=gen)[:, 0]
+        sampled.append(y)
+        lp = F.log_softmax(lg[0], -1).gather(1, y[:, None])[:, 0]
+        (lp * weight[i]).sum().backward()
+    for h in hooks:
+        h.remove()
+    out = {"windows": windows.numpy(), "weight": weight.numpy(), "sampled": torch.stack(sampled).numpy()}
+    for k in mods:
+        out[f"imp_{k}"] = (gg[k] * yy[k]).clamp_min(1e-30).numpy()
+    out["mods"] = np.array(list(mods))
+    # GuidedQuant: the reference's function; its draws recorded by wrapping torch.multinomial for the call
+    chunks = [windows[:2], windows[2:]]
+    base = [torch.ones(2, 32), torch.ones(1, 32) * 2.0]
+    stages_of = {i: [{"kind": "linear", "names": [n for n, m in L.named_modules() if isinstance(m, torch.nn.Linear)]}]
+                 for i, L in enumerate(layers)}
+    draws, real = [], torch.multinomial
+
+    def recording(*a, **k):
+        r = real(*a, **k)
+        draws.append(r.clone())
+        return r
+    torch.multinomial = recording
+    try:
+        gw = Q.guided_weights(model, chunks, stages_of, layers, base, 0.1)
+    finally:
+        torch.multinomial = real
+    out["guided_draws"] = torch.stack([d[:, 0] for d in draws]).numpy()
+    for k, v in gw.items():
+        out[f"guided_{k}"] = torch.cat(v).numpy()
+    out["state"] = np.array(list(model.state_dict().keys()))
+    for i, (k, v) in enumerate(model.state_dict().items()):
+        out[f"p{i}"] = v.to(torch.bfloat16).view(torch.int16).numpy()
+    np.savez_compressed(HERE / "importance.npz", **out)
 
 
 def ast_def():

@@ -87,3 +87,22 @@ def digest(tensors) -> str:
         h.update(t.contiguous().view(torch.uint8).numpy().tobytes() if t.dtype == torch.bfloat16
                  else t.contiguous().numpy().tobytes())
     return h.hexdigest()
+
+
+def tiny_llama(dtype=None, state=None):
+    """A 2-layer Llama of hidden 64 (vocab 1000, weights N(0, 0.3²) rounded to bf16 values), fp32 unless `dtype`;
+    `state` loads given weights (the fixture's) instead of the seeded initialisation."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, vocab_size=1000, rms_norm_eps=1e-5, rope_theta=1e4,
+                      tie_word_embeddings=True, max_position_embeddings=256, initializer_range=0.3)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(41)
+    model = LlamaForCausalLM(cfg).eval()
+    if state is not None:
+        model.load_state_dict(state)
+    else:
+        with torch.no_grad():
+            for p in model.parameters():
+                p.copy_(p.to(torch.bfloat16).float())
+    return model.to(dtype or torch.float32)

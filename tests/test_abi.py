@@ -76,6 +76,9 @@ INVALID = [
     ("lamq_env_factor", (N, 4, 4, 0.01, N, 4, N, N, 0, N, N), b"null or aliased"),
     ("lamq_ridge", (N, 2, N, 4, 4, 0.1, N), b"bad shape"),
     ("lamq_proxy_loss", (N, 2, N, 4, 4, 4, N, 4, N, N, N, 0, N), b"bad shape"),
+    ("lamq_square_sums", (N, 0, 4, 8, 4, N, N, N, 0, N), b"bad shape"),
+    ("lamq_square_sums", (N, 2, 4, 8, 8, N, N, N, 0, N), b"dtype"),
+    ("lamq_square_sums", (P, 0, 4, 8, 8, P, N, N, 0, N), b"workspace"),
     ("lamq_proxy_loss", (N, 4, N, 4, 4, 4, N, 4, N, P, N, 0, N), b"null pointer"),
     ("lamq_cross_apply", (N, 4, 6, 4, N, 4, N, 4, 0.5, N, 4, N, 0, N), b"needs rows == n"),
     ("lamq_kl_reference", (N, 8, 0, 8, N, 8, 16, N, 16, N, N, N, N, 0, N, N), b"lamq_kl_reference: bad shape"),
@@ -107,6 +110,7 @@ EMPTY = [
     ("lamq_env_factor", (N, 0, 0, 0.01, N, 0, N, N, 0, N, N)),
     ("lamq_ridge", (N, 0, N, 0, 0, 0.1, N)),
     ("lamq_proxy_loss", (N, 4, N, 4, 4, 0, N, 4, N, P, N, 0, N)),
+    ("lamq_square_sums", (N, 1, 0, 8, 8, N, N, N, 0, N)),
     ("lamq_cross_apply", (N, 4, 0, 0, N, 4, N, 4, 0.5, N, 4, N, 0, N)),
     ("lamq_pack_trellis", (N, 32, 0, 32, 2, 12, N, N, N)),
     ("lamq_unpack_trellis", (N, 0, 32, 2, 12, N, 32, N)),

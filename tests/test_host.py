@@ -194,3 +194,13 @@ def test_cpu_baseline_fit_separates_call_and_row_costs(monkeypatch):
     assert abs(per_call - 1.0) < 1e-9 and abs(per_row - 0.01) < 1e-12
     times[128] = 0.9  # noise: the larger sample ran faster
     assert bench.words_fit(np.zeros((128, 8)), None, None, None, None) == (0.0, 0.9 / 128)
+
+
+def test_embedding_buckets_and_frequency_order_match_reference(golden):
+    """quantize.py:350-364 by the reference (embedding.npz): bucket sizes and the frequency order (ties by id)."""
+    import torch
+    from lookatmyquant_b200.embedding import embedding_buckets, frequency_order
+    g = golden("embedding")
+    assert embedding_buckets(49152) == list(g["buckets_49152"])
+    assert embedding_buckets(1000) == list(g["buckets_1000"])
+    assert torch.equal(frequency_order(torch.as_tensor(g["freq_ids"]), 600), torch.as_tensor(g["freq_order"]))
