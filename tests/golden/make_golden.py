@@ -69,7 +69,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word",
-                                       "embedding", "importance"],
+                                       "embedding", "importance", "finetune"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -105,6 +105,9 @@ def main():
         return
     if args.only == "importance":
         write_importance_fixture(Q, torch, args.reference.resolve())
+        return
+    if args.only == "finetune":
+        write_finetune_fixture(C, torch)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -230,6 +233,7 @@ def main():
     write_best_word_fixture(C, Q, torch, args.reference.resolve())
     write_embedding_fixture(Q, torch)
     write_importance_fixture(Q, torch, args.reference.resolve())
+    write_finetune_fixture(C, torch)
     print("golden vectors written to", HERE)
 
 
@@ -466,6 +470,45 @@ def write_importance_fixture(Q, torch, ref: Path):
     for i, (k, v) in enumerate(model.state_dict().items()):
         out[f"p{i}"] = v.to(torch.bfloat16).view(torch.int16).numpy()
     np.savez_compressed(HERE / "importance.npz", **out)
+
+
+def write_finetune_fixture(C, torch):
+    """16. The fine-tuning's trellis parts by the reference itself (finetune_lib.py): `rounded` — a 96 x 256 W in three
+    row groups (k = 1, 2, 3, the shipped tables) under the rotated statistics of a calibration H, scales refitted — and
+    TrellisCoded.nearest / repick of a stored entry after a seeded summed gradient."""
+    import finetune_lib as FL
+    from opgraph.frame import Environment
+    m, n, in_seed = 96, 256, 5101
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(5100), dtype=torch.float64)).float()
+    H = calib_H(n, 2048, 5102)
+    R = FL.FastRHT(n, in_seed)
+    env = Environment(FL.rotated_moment(H, R))
+    perm = torch.randperm(m, generator=torch.Generator().manual_seed(5103))
+    groups = [(perm[32 * i:32 * (i + 1)], k, FL.RowPath(C.trellis_values(12, k, 256), k)) for i, k in enumerate((1, 2, 3))]
+    scale0 = R.back(W).double().pow(2).mean(1).sqrt().float()
+    scale = scale0.clone()
+    P, states = FL.rounded(W, R, groups, scale, env)
+    out = {"W": W.numpy(), "H": H.float().numpy(), "in_seed": np.array(in_seed), "perm": perm.numpy(),
+           "scale0": scale0.numpy(), "P": P.numpy(), "states": states.numpy(), "scale": scale.numpy()}
+    # rows given: the second group's first 10 rows and the third's last 6, in that order
+    rows = torch.cat([perm[32:42], perm[90:96]])
+    scale2 = scale0.clone()
+    P2, states2 = FL.rounded(W, R, groups, scale2, env, rows=rows)
+    out.update({"rows2": rows.numpy(), "P2": P2.numpy(), "states2": states2.numpy(), "scale2": scale2.numpy()})
+    # a stored entry (the k = 2 group as a matrix of its own) and one proximal re-pick step
+    g2 = groups[1][0]
+    entry = {"states": states[g2].long().clone(), "scales": scale[g2].clone(),
+             "table": C.trellis_values(12, 2, 256).float(), "in_seed": in_seed}
+    entry_states = entry["states"].numpy().copy()  # TrellisCoded keeps (and repick overwrites) the tensor itself
+    tc = FL.TrellisCoded(entry, {}, move=True)
+    acc = 0.8 * torch.randn(tc.states.shape, generator=torch.Generator().manual_seed(5104))
+    tc.acc.copy_(acc)
+    out.update({"entry_states": entry_states, "entry_scales": entry["scales"].numpy().copy(),
+                "acc": acc.numpy(), "eta": np.array(0.7), "nearest": tc.nearest(0.7, 1 << 28).numpy().copy()})
+    changed = tc.repick(0.7, 1 << 28)
+    out["changed"] = np.array(changed)
+    out["k"] = np.array(tc.k)
+    np.savez_compressed(HERE / "finetune.npz", **out)
 
 
 def ast_def():
