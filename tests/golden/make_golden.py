@@ -69,7 +69,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word",
-                                       "embedding", "importance", "finetune"],
+                                       "embedding", "importance", "finetune", "dropin"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -108,6 +108,9 @@ def main():
         return
     if args.only == "finetune":
         write_finetune_fixture(C, torch)
+        return
+    if args.only == "dropin":
+        write_dropin_fixture(C, Q, torch)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -234,6 +237,7 @@ def main():
     write_embedding_fixture(Q, torch)
     write_importance_fixture(Q, torch, args.reference.resolve())
     write_finetune_fixture(C, torch)
+    write_dropin_fixture(C, Q, torch)
     print("golden vectors written to", HERE)
 
 
@@ -509,6 +513,57 @@ def write_finetune_fixture(C, torch):
     out["changed"] = np.array(changed)
     out["k"] = np.array(tc.k)
     np.savez_compressed(HERE / "finetune.npz", **out)
+
+
+def write_dropin_fixture(C, Q, torch):
+    """17. The reference's own call sites, recorded: quantize_row_groups (quantize.py:530-565) over a 192 x 256 matrix
+    in three width groups, each through the reference's `word` (quantize.py:332-347), with every call it makes to
+    opgraph.codes.ldlq_words and opgraph.codes.viterbi recorded (arguments and results). A test replays each call into
+    this package's function of the same name: equal results at every call site mean the patched reference would
+    follow the same path, call for call."""
+    m, n = 192, 256
+    W = (0.02 * torch.randn(m, n, generator=torch.Generator().manual_seed(6001), dtype=torch.float64)).float().double()
+    H = calib_H(n, 2048, 6002)
+    perm = torch.randperm(m, generator=torch.Generator().manual_seed(6003))
+    groups = [{"rows": perm[:64], "bits": 2}, {"rows": perm[64:128], "bits": 3}, {"rows": perm[128:], "bits": 1}]
+    trellis = {b: C.RowTrellisCode(12, b, T=256, width=16, look=8) for b in (1, 2, 3, 4)}
+    in_seed = 6101
+    vit_calls, words_calls = [], []
+    real_v, real_w = C.viterbi, C.ldlq_words
+
+    def spy_viterbi(X, values, L, k, chunk=None, start=None):
+        out = real_v(X, values, L, k, chunk=chunk, start=start)
+        vit_calls.append((X.clone(), k, None if start is None else start.clone(), out.clone()))
+        return out
+
+    def spy_words(Ws, H_, code, seeds, incoherent=True, in_seed=None, out_rot=True):
+        nets = real_w(Ws, H_, code, seeds, incoherent=incoherent, in_seed=in_seed, out_rot=out_rot)
+        words_calls.append((torch.stack(list(Ws)) if len(Ws) == 1 else torch.cat(list(Ws)), code.k, list(seeds),
+                            incoherent, in_seed, out_rot,
+                            [Q.trellis_states(net.cores["W"].data, code.values) for net in nets]))
+        return nets
+
+    C.viterbi, C.ldlq_words = spy_viterbi, spy_words
+    try:
+        def round_group(rows, bits):
+            return Q.word(f"tr{bits}x", W[rows], H, 6100, trellis, in_seed, False)
+        Wq, rate, entry = Q.quantize_row_groups(W, groups, round_group, in_seed, True)
+    finally:
+        C.viterbi, C.ldlq_words = real_v, real_w
+    out = {"W": W.float().numpy(), "H": H.float().numpy(), "perm": perm.numpy(), "in_seed": np.array(in_seed),
+           "Wq": Wq.float().numpy(), "states": entry["states"].numpy()}
+    out["vit_k"] = np.array([c[1] for c in vit_calls])
+    out["vit_rows"] = np.array([c[0].shape[0] for c in vit_calls])
+    out["vit_T"] = np.array([c[0].shape[1] for c in vit_calls])
+    out["vit_X"] = np.concatenate([c[0].reshape(-1).numpy() for c in vit_calls])
+    out["vit_start"] = np.concatenate([c[2].numpy() for c in vit_calls])
+    out["vit_out"] = np.concatenate([c[3].reshape(-1).numpy() for c in vit_calls])
+    for i, (Ws, k, seeds, inc, ins, orot, sts) in enumerate(words_calls):
+        out[f"w{i}_W"] = Ws.reshape(-1, Ws.shape[-1]).float().numpy()
+        out[f"w{i}_meta"] = np.array([k, seeds[0], int(inc), -1 if ins is None else ins, int(orot)])
+        out[f"w{i}_states"] = sts[0].numpy()
+    out["words_calls"] = np.array(len(words_calls))
+    np.savez_compressed(HERE / "dropin.npz", **out)
 
 
 def ast_def():
