@@ -381,9 +381,20 @@ size_t lamq_trellis_gemm_workspace_size(const lamq_gemm_group *groups, int ngrou
 int lamq_trellis_gemm(const lamq_gemm_group *groups, int ngroups, int64_t nvec, int y_bf16, void *workspace,
                       size_t workspace_bytes, int *status, lamq_stream_t stream);
 
-/* Element types of lamq_square_sums. */
+/* Element types of lamq_square_sums and lamq_rht_rows_act. */
 #define LAMQ_F32 0
 #define LAMQ_BF16 1
+#define LAMQ_F64 2
+
+/*
+ * lamq_rht_rows for activations: the same y = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)) per row, summed in fp32, reading
+ * bf16, fp32 or fp64 rows (in_dtype) and writing bf16 or fp32 (out_dtype) — the input rotation of a product whose
+ * operand is bf16 (the trellis GEMM, a probed piece), R_in x (codes.py:430's rotation applied to activations).
+ * n = a·b up to 25,600; in and out must not alias.
+ */
+int lamq_rht_rows_act(const void *in, int in_dtype, int64_t ldi, void *out, int out_dtype, int64_t ldo, int64_t rows,
+                      int a, int b, const uint32_t *abits, const uint32_t *bbits, const double *pre,
+                      const double *post, double scale, lamq_stream_t stream);
 
 /*
  * Sums of squares of x (rows x cols, leading dimension ld, fp32 or bf16) in fp64: col_acc[j] += Σ_r x[r][j]² (the

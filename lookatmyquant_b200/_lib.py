@@ -16,7 +16,7 @@ _lib = None
 _lock = threading.Lock()
 
 LAMQ_OK, LAMQ_ERR_INVALID, LAMQ_ERR_CUDA, LAMQ_ERR_NOT_PD, LAMQ_ERR_TIMEOUT, LAMQ_ERR_NOT_PATH = range(6)
-LAMQ_F32, LAMQ_BF16 = 0, 1
+LAMQ_F32, LAMQ_BF16, LAMQ_F64 = 0, 1, 2
 
 _c = ctypes
 _P, _I64, _I32, _SZ, _D = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_size_t, _c.c_double
@@ -38,6 +38,7 @@ SIGNATURES = {
     "lamq_hessian_finalize": (_I32, [_P, _P, _I32, _I64, _D, _P, _P, _P]),
     "lamq_rht_rows": (_I32, [_P, _I64, _P, _I64, _I64, _I32, _I32, _P, _P, _P, _P, _D, _P]),
     "lamq_transpose_f64": (_I32, [_P, _I64, _P, _I64, _I32, _I32, _P]),
+    "lamq_rht_rows_act": (_I32, [_P, _I32, _I64, _P, _I32, _I64, _I64, _I32, _I32, _P, _P, _P, _P, _D, _P]),
     "lamq_dgemm": (_I32, [_I32, _I32, _I32, _I32, _D, _P, _I64, _P, _I64, _D, _P, _I64, _P]),
     "lamq_factor_workspace_size": (_SZ, [_I32]),
     "lamq_cholesky_inverse_lower": (_I32, [_P, _I64, _I32, _P, _SZ, _P, _P]),

@@ -189,8 +189,12 @@ class TrellisProduct:
         self._dense = None
 
     def rotate(self, x: torch.Tensor) -> torch.Tensor:
-        """R_in x for each row of x (nvec x n), fp32."""
-        return self.rot.rows(x.to(self.device, torch.float64).contiguous()).to(torch.float32)
+        """R_in x for each row of x (nvec x n): fp64 through the factors, then fp32, for the CUDA-core product of few
+        vectors; from GEMM_PRODUCT_VECTORS vectors on summed in fp32 and rounded to the GEMM's bf16 operand."""
+        x = x.reshape(-1, self.n).to(self.device)
+        if x.shape[0] >= GEMM_PRODUCT_VECTORS:
+            return self.rot.rows_act(x, torch.bfloat16)
+        return self.rot.rows(x.to(torch.float64).contiguous()).to(torch.float32)
 
     def dense_rotated(self) -> torch.Tensor:
         """decode_rotated as bf16 (cached): V[state]·S before the input transform (a check, not the product path)."""
@@ -336,8 +340,8 @@ def product_rotated(products: list, xr: torch.Tensor) -> list:
 
 class TrellisLinear(torch.nn.Module):
     """A linear layer whose weight is a trellis word (codes.TrellisWord: W = R_outᵀ·diag(S)·V[states]·R_in), applied
-    without forming W: y = R_outᵀ·(S ⊙ (V[states]·(R_in x))). The input rotation runs through the Kronecker factors
-    (fp64), the product on the tensor cores straight from the int16 states (lamq_trellis_gemm: bf16 operands, fp32
+    without forming W: y = R_outᵀ·(S ⊙ (V[states]·(R_in x))). The input rotation runs through the Kronecker factors,
+    the product on the tensor cores straight from the int16 states (lamq_trellis_gemm: bf16 operands, fp32
     accumulation), the output rotation through the factors again; the result is cast to the input's dtype. This is
     how the measure sweep's probe runs its quantized piece (the reference writes the dense word into the model,
     compiler.py:220-229 with quantize.py:332-347)."""
@@ -361,7 +365,7 @@ class TrellisLinear(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
         xf = x.reshape(-1, self.in_features)
-        xr = self.word.R_in.rows(xf.to(torch.float64).contiguous()) if self.word.R_in is not None else xf
+        xr = self.word.R_in.rows_act(xf, torch.bfloat16) if self.word.R_in is not None else xf
         xb = _bf16_operand(xr, self.states.device)
         nvec = xb.shape[0]
         z = torch.empty(nvec, self.out_features, dtype=torch.float32, device=self.states.device)
@@ -370,7 +374,7 @@ class TrellisLinear(torch.nn.Module):
                            self.in_features, 0)
         status = gemm_groups([g], nvec, z.device)
         if self.word.R_out is not None:
-            z = self.word.R_out.rows_t(z.to(torch.float64))
+            z = self.word.R_out.rows_t_act(z, torch.float32)
         if int(status.item()):
             _lib.check(int(status.item()), "lamq_trellis_gemm")
         return z.to(x.dtype).reshape(*shape[:-1], self.out_features)

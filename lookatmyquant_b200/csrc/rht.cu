@@ -11,6 +11,8 @@
 // Fewer than kSplitRows rows (a decode step's few input vectors) are spread over many CTAs instead (the split form).
 // The general form computed is y = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)), so R (Ae = A, Be = B, pre = s) and Rᵀ
 // (Ae = Aᵀ, Be = Bᵀ, post = s) are both one pass.
+#include <cuda_bf16.h>
+
 #include "lamq_common.cuh"
 
 namespace lamq {
@@ -213,6 +215,150 @@ __global__ void __launch_bounds__(kSplitWarps * 32) rht_split_cols_kernel(RhtPar
     }
 }
 
+// ---- activations: the same transform in fp32 for many rows, reading bf16/fp32/fp64 and writing bf16 or fp32
+//
+// The product's inputs and the probed piece's activations go to a bf16 tensor-core operand, so fp32 sums (at most
+// a + b = 216 terms of ±1·x) are more than enough; fp32 values take half the shared memory (more rows in flight per
+// SM) and the fp32 pipe adds twice as fast as the fp64 one.
+
+template <int NC>
+__device__ __forceinline__ void signed_sums_f32(const float *__restrict__ src, int stride, int len,
+                                                const uint32_t (&bits)[NC][8], float (&acc)[NC]) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        if (32 * w >= len) break;
+        uint32_t bw[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) bw[c] = bits[c][w];
+        const int lim = min(32, len - 32 * w);
+        if (lim == 32) {
+#pragma unroll
+            for (int bit = 0; bit < 32; ++bit) {
+                const uint32_t v = __float_as_uint(src[(32 * w + bit) * stride]);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) acc[c] += __uint_as_float(v ^ (((bw[c] >> bit) & 1u) << 31));
+            }
+        } else {
+            for (int bit = 0; bit < lim; ++bit) {
+                const uint32_t v = __float_as_uint(src[(32 * w + bit) * stride]);
+#pragma unroll
+                for (int c = 0; c < NC; ++c) acc[c] += __uint_as_float(v ^ (((bw[c] >> bit) & 1u) << 31));
+            }
+        }
+    }
+}
+
+struct RhtActParams {
+    const void *in;
+    int in_dtype;
+    int64_t ldi;
+    void *out;
+    int out_dtype;
+    int64_t ldo;
+    int64_t rows;
+    int a, b;
+    const uint32_t *abits, *bbits;
+    int wa, wb;
+    const double *pre, *post;  // n signs (±1) or null
+    float scale;
+};
+
+__device__ __forceinline__ float load_act(const void *p, int dtype, int64_t e) {
+    if (dtype == LAMQ_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[e]);
+    if (dtype == LAMQ_F32) return reinterpret_cast<const float *>(p)[e];
+    return (float)reinterpret_cast<const double *>(p)[e];
+}
+
+template <int NA, int NB>
+__global__ void __launch_bounds__(kRhtThreads, 2) rht_rows_act_kernel(RhtActParams p) {
+    extern __shared__ __align__(16) float svf[];
+    const int n = p.a * p.b;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRhtThreads / 32;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t base = row * p.ldi;
+#pragma unroll 8
+        for (int e = threadIdx.x; e < n; e += kRhtThreads) {
+            const float v = load_act(p.in, p.in_dtype, base + e);
+            svf[e] = p.pre ? (p.pre[e] < 0 ? -v : v) : v;
+        }
+        __syncthreads();
+        {  // the sign words are loaded per phase (cached): both phases' in registers would halve the resident CTAs
+        uint32_t bbits[NB][8];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) {
+            const int q = lane + 32 * c;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) bbits[c][w] = (q < p.b && w < p.wb) ? __ldg(p.bbits + q * p.wb + w) : 0u;
+        }
+        for (int pr = warp; pr < p.a; pr += nwarps) {  // Z[pr][q] = Σ_q' Be[q][q']·V[pr][q']
+            float acc[NB];
+#pragma unroll
+            for (int c = 0; c < NB; ++c) acc[c] = 0.f;
+            signed_sums_f32<NB>(svf + pr * p.b, 1, p.b, bbits, acc);
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < NB; ++c) {
+                const int q = lane + 32 * c;
+                if (q < p.b) svf[pr * p.b + q] = acc[c];
+            }
+            __syncwarp();
+        }
+        }
+        __syncthreads();
+        {
+        uint32_t abits[NA][8];
+#pragma unroll
+        for (int c = 0; c < NA; ++c) {
+            const int pr = lane + 32 * c;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) abits[c][w] = (pr < p.a && w < p.wa) ? __ldg(p.abits + pr * p.wa + w) : 0u;
+        }
+        for (int q = warp; q < p.b; q += nwarps) {  // Y[pr][q] = Σ_p' Ae[pr][p']·Z[p'][q]
+            float acc[NA];
+#pragma unroll
+            for (int c = 0; c < NA; ++c) acc[c] = 0.f;
+            signed_sums_f32<NA>(svf + q, p.b, p.a, abits, acc);
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < NA; ++c) {
+                const int pr = lane + 32 * c;
+                if (pr < p.a) svf[pr * p.b + q] = acc[c];
+            }
+            __syncwarp();
+        }
+        }
+        __syncthreads();
+        const int64_t obase = row * p.ldo;
+#pragma unroll 8
+        for (int e = threadIdx.x; e < n; e += kRhtThreads) {
+            float y = svf[e] * p.scale;
+            if (p.post && p.post[e] < 0) y = -y;
+            if (p.out_dtype == LAMQ_BF16)
+                reinterpret_cast<__nv_bfloat16 *>(p.out)[obase + e] = __float2bfloat16_rn(y);
+            else
+                reinterpret_cast<float *>(p.out)[obase + e] = y;
+        }
+        __syncthreads();
+    }
+}
+
+template <int NA, int NB>
+int launch_rht_act(const RhtActParams &p, cudaStream_t stream) {
+    const size_t smem = (size_t)p.a * p.b * sizeof(float);
+    const cudaError_t e = smem_limit_once((const void *)rht_rows_act_kernel<NA, NB>, 100 * 1024);
+    if (e != cudaSuccess) {
+        set_error("lamq_rht_rows_act: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t grid = p.rows < (int64_t)sms * 8 ? p.rows : (int64_t)sms * 8;
+    rht_rows_act_kernel<NA, NB><<<(unsigned)grid, kRhtThreads, smem, stream>>>(p);
+    LAMQ_CHECK_LAUNCH("lamq_rht_rows_act");
+    return LAMQ_OK;
+}
+
 constexpr int kTile = 32;
 
 __global__ void transpose_kernel(const double *__restrict__ in, int64_t ldi, double *__restrict__ out, int64_t ldo,
@@ -302,4 +448,35 @@ extern "C" int lamq_transpose_f64(const double *in, int64_t ldi, double *out, in
     transpose_kernel<<<grid, block, 0, (cudaStream_t)stream>>>(in, ldi, out, ldo, rows, cols);
     LAMQ_CHECK_LAUNCH("lamq_transpose_f64");
     return LAMQ_OK;
+}
+
+extern "C" int lamq_rht_rows_act(const void *in, int in_dtype, int64_t ldi, void *out, int out_dtype, int64_t ldo,
+                                 int64_t rows, int a, int b, const uint32_t *abits, const uint32_t *bbits,
+                                 const double *pre, const double *post, double scale, lamq_stream_t stream) {
+    LAMQ_REQUIRE(rows >= 0 && a >= 1 && b >= 1 && a <= kMaxFactor && b <= kMaxFactor,
+                 "lamq_rht_rows_act: factor orders must be 1..%d", kMaxFactor);
+    LAMQ_REQUIRE(in_dtype == LAMQ_F32 || in_dtype == LAMQ_BF16 || in_dtype == LAMQ_F64,
+                 "lamq_rht_rows_act: input dtype must be LAMQ_F32, LAMQ_BF16 or LAMQ_F64");
+    LAMQ_REQUIRE(out_dtype == LAMQ_F32 || out_dtype == LAMQ_BF16,
+                 "lamq_rht_rows_act: output dtype must be LAMQ_F32 or LAMQ_BF16");
+    if (rows == 0) return LAMQ_OK;
+    LAMQ_REQUIRE(in && out && abits && bbits, "lamq_rht_rows_act: null pointer");
+    LAMQ_REQUIRE(ldi >= (int64_t)a * b && ldo >= (int64_t)a * b, "lamq_rht_rows_act: leading dimension below n");
+    LAMQ_REQUIRE(in != out, "lamq_rht_rows_act: in and out must not alias");
+    LAMQ_REQUIRE((size_t)a * b * sizeof(float) <= 100 * 1024, "lamq_rht_rows_act: n = %d too large for one CTA", a * b);
+    RhtActParams p{in, in_dtype, ldi, out, out_dtype, ldo, rows, a, b, abits, bbits, (a + 31) / 32, (b + 31) / 32,
+                   pre, post, (float)scale};
+    const int na = p.wa <= 1 ? 1 : p.wa <= 2 ? 2 : p.wa <= 4 ? 4 : 8;
+    const int nb = p.wb;
+    cudaStream_t s = (cudaStream_t)stream;
+#define LAMQ_RHT_ACT_CASE(NA_, NB_) \
+    if (na == NA_ && nb == NB_) return launch_rht_act<NA_, NB_>(p, s);
+#define LAMQ_RHT_ACT_ROW(NA_) \
+    LAMQ_RHT_ACT_CASE(NA_, 1) LAMQ_RHT_ACT_CASE(NA_, 2) LAMQ_RHT_ACT_CASE(NA_, 3) LAMQ_RHT_ACT_CASE(NA_, 4) \
+    LAMQ_RHT_ACT_CASE(NA_, 5) LAMQ_RHT_ACT_CASE(NA_, 6) LAMQ_RHT_ACT_CASE(NA_, 7) LAMQ_RHT_ACT_CASE(NA_, 8)
+    LAMQ_RHT_ACT_ROW(1) LAMQ_RHT_ACT_ROW(2) LAMQ_RHT_ACT_ROW(4) LAMQ_RHT_ACT_ROW(8)
+#undef LAMQ_RHT_ACT_ROW
+#undef LAMQ_RHT_ACT_CASE
+    set_error("lamq_rht_rows_act: unsupported factor orders %d x %d", a, b);
+    return LAMQ_ERR_INVALID;
 }

@@ -65,6 +65,38 @@ class Rotation:
                                             stream_ptr(self.device)), "lamq_rht_rows")
         return out
 
+    def _act(self, X, transpose: bool, out_dtype):
+        """lamq_rht_rows_act: the rotation of activation rows (bf16/fp32/fp64 in, fp32 sums, bf16/fp32 out)."""
+        if not X.is_cuda:
+            raise TypeError("rotations run on CUDA tensors")
+        dt = {torch.bfloat16: _lib.LAMQ_BF16, torch.float32: _lib.LAMQ_F32, torch.float64: _lib.LAMQ_F64}
+        if X.dtype not in dt or out_dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"activation rotation: {X.dtype} in, {out_dtype} out not supported")
+        X = X.reshape(-1, X.shape[-1])
+        X = X if X.stride(-1) == 1 else X.contiguous()
+        if X.shape[1] != self.n:
+            raise ValueError(f"rows of length {X.shape[1]}, rotation of order {self.n}")
+        rows = X.shape[0]
+        ld = (self.n + 7) // 8 * 8  # 16-byte rows: the bf16 output is a TMA operand
+        out = torch.empty(rows, ld, dtype=out_dtype, device=X.device)[:, :self.n]
+        ab, bb = (self.Atbits, self.Btbits) if transpose else (self.Abits, self.Bbits)
+        pre, post = (None, self.signs) if transpose else (self.signs, None)
+        with torch.cuda.device(self.device):
+            check(_lib.load().lamq_rht_rows_act(ptr(X), dt[X.dtype], X.stride(0), ptr(out), dt[out_dtype],
+                                                out.stride(0), rows, self.a, self.b, ptr(ab), ptr(bb), ptr(pre),
+                                                ptr(post), self.scale, stream_ptr(self.device)),
+                  "lamq_rht_rows_act")
+        return out
+
+    def rows_act(self, X: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+        """X·Rᵀ for activation rows (R applied to each row), summed in fp32, as bf16 (a tensor-core operand with
+        16-byte rows) or fp32."""
+        return self._act(X, False, out_dtype)
+
+    def rows_t_act(self, X: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+        """X·R for activation rows (Rᵀ applied to each row), summed in fp32."""
+        return self._act(X, True, out_dtype)
+
     def rows(self, M: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """M·Rᵀ: X = W·R_inᵀ (codes.py:430)."""
         return self._run(M, out, False)

@@ -70,6 +70,9 @@ INVALID = [
     ("lamq_hessian_finalize", (N, N, 4, 4, 1.0, N, N, N), b"null pointer"),
     ("lamq_rht_rows", (N, 4, N, 4, 2, 0, 4, N, N, N, N, 1.0, N), b"factor orders"),
     ("lamq_transpose_f64", (N, 4, N, 4, -1, 4, N), b"negative shape"),
+    ("lamq_rht_rows_act", (N, 1, 4, N, 1, 4, 2, 0, 4, N, N, N, N, 1.0, N), b"factor orders"),
+    ("lamq_rht_rows_act", (N, 5, 4, N, 1, 4, 2, 2, 2, N, N, N, N, 1.0, N), b"input dtype"),
+    ("lamq_rht_rows_act", (P, 1, 4, P, 1, 4, 2, 2, 2, P, P, N, N, 1.0, N), b"must not alias"),
     ("lamq_dgemm", (0, -1, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N), b"negative shape"),
     ("lamq_dgemm", (0, 4, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N), b"null pointer"),
     ("lamq_cholesky_inverse_lower", (N, 2, 4, N, 0, N, N), b"bad shape"),
@@ -105,6 +108,7 @@ EMPTY = [
     ("lamq_weighted_split", (N, 8, N, 8, N, N, 0, 8, N, N, N)),
     ("lamq_rht_rows", (N, 4, N, 4, 0, 2, 2, N, N, N, N, 1.0, N)),
     ("lamq_transpose_f64", (N, 4, N, 4, 0, 4, N)),
+    ("lamq_rht_rows_act", (N, 1, 4, N, 1, 4, 0, 2, 2, N, N, N, N, 1.0, N)),
     ("lamq_dgemm", (0, 0, 4, 4, 1.0, N, 4, N, 4, 0.0, N, 4, N)),
     ("lamq_cholesky_inverse_lower", (N, 0, 0, N, 0, N, N)),
     ("lamq_env_factor", (N, 0, 0, 0.01, N, 0, N, N, 0, N, N)),

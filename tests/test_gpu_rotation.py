@@ -49,3 +49,21 @@ def test_few_rows_equal_the_one_row_per_cta_form(n):
             inplace = M[:k].clone()
             run(inplace, out=inplace)
             assert torch.equal(inplace, whole[:k])
+
+
+@pytest.mark.parametrize("n", [960, 2560, 4096, 9728, 200])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_activation_rotation_matches_fp64(n, dtype):
+    """lamq_rht_rows_act (fp32 sums, bf16/fp32 in and out) against the fp64 rotation: R x and Rᵀ x to fp32 (or bf16)
+    rounding."""
+    from lookatmyquant_b200.rotation import Rotation
+    R = Rotation(n, 301)
+    x = torch.randn(300, n, generator=torch.Generator().manual_seed(n)).to(dtype).cuda()
+    want = R.rows(x.double())
+    for out_dtype, tol in ((torch.float32, 1e-5), (torch.bfloat16, 1e-2)):
+        got = R.rows_act(x, out_dtype)
+        assert got.dtype == out_dtype and got.shape == (300, n)
+        assert (got.double() - want).abs().max() <= tol * want.abs().max()
+    want_t = R.rows_t(x.double())
+    got_t = R.rows_t_act(x, torch.float32)
+    assert (got_t.double() - want_t).abs().max() <= 1e-5 * want_t.abs().max()
