@@ -525,6 +525,62 @@ struct DecodeParams {
 constexpr int kDecodeThreads = 256;
 constexpr int kDecodeBlocksPerSm = 8;  // resident decode blocks per SM (8 KB of table each): the grid is one wave
 
+// The rows of one decode group from this block's share of its 8-column chunks (K = 0: int16 states; else packed
+// k-bit symbols, the per-column bit offsets constants).
+template <int K>
+__device__ __forceinline__ void decode_items(const DecodeGroup &g, const uint16_t *tab, int64_t first, int64_t step) {
+    const int nch = (int)(g.ld / 8);
+    const int64_t items = g.rows * nch;
+    const uint32_t lmask = (1u << g.L) - 1u;
+    const int N = (g.n + 31) / 32 * 32;
+    const int wpr = N / 32 * (K > 0 ? K : 1);
+#pragma unroll 2
+    for (int64_t it = first; it < items; it += step) {
+        const int64_t r = it / nch;
+        const int j0 = (int)(it % nch) * 8;
+        uint32_t st[8];
+        if constexpr (K == 0) {
+            const uint4 v = j0 < g.n ? __ldg(reinterpret_cast<const uint4 *>(g.states + r * g.lds + j0))
+                                     : make_uint4(0, 0, 0, 0);
+            const uint32_t raw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                st[2 * h] = raw[h] & lmask;
+                st[2 * h + 1] = (raw[h] >> 16) & lmask;
+            }
+        } else {
+            // state of column j0 + i: the L bits at (N − 1 − j0 − i)·K = b0 + (7 − i)·K, b0 = (N − 8 − j0)·K; with
+            // j0 a multiple of 8, b0 mod 32 is one of 32 / gcd(32, 8K) values and the 8 states span < 3 words
+            const uint32_t *row = g.codes + r * (int64_t)wpr;
+            const int64_t b0 = (int64_t)(N - 8 - j0) * K;
+            const int w0 = (int)(b0 >> 5), sh = (int)(b0 & 31);
+            uint32_t w[3];
+#pragma unroll
+            for (int q = 0; q < 3; ++q) w[q] = (w0 + q >= 0 && w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
+            const uint64_t lo = (uint64_t)w[1] << 32 | w[0];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int off = (7 - i) * K;  // a constant
+                if (7 * K + 12 <= 32) {       // all eight states inside the first 64 bits whatever sh is
+                    st[i] = (uint32_t)(lo >> (sh + off)) & lmask;
+                } else {
+                    const int pos = sh + off;
+                    st[i] = (pos < 32 ? __funnelshift_r(w[0], w[1], pos) : __funnelshift_r(w[1], w[2], pos - 32)) &
+                            lmask;
+                }
+            }
+        }
+        uint32_t pk[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const uint32_t a = j0 + 2 * h < g.n ? tab[st[2 * h]] : 0u;
+            const uint32_t b = j0 + 2 * h + 1 < g.n ? tab[st[2 * h + 1]] : 0u;
+            pk[h] = a | (b << 16);
+        }
+        *reinterpret_cast<uint4 *>(g.out + r * g.ld + j0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+}
+
 // bf16(table[state]) for every (row, column) of every group: a thread per 8 consecutive columns of a row (one
 // 16-byte store), the states cut from three stream words (or read as eight int16), the group's table in shared
 // memory as bf16. Columns from n to the row's end (ld) are written as zeros.
@@ -537,51 +593,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_rows_kernel(const __gri
     for (int i = threadIdx.x; i < kTableEntries; i += kDecodeThreads)
         tab[i] = __bfloat16_as_ushort(__float2bfloat16_rn(i < nt ? __ldg(g.table + i) : 0.f));
     __syncthreads();
-    const int nch = (int)(g.ld / 8);
-    const int64_t items = g.rows * nch;
     const int64_t nblocks = (gi + 1 < p.ng ? p.g[gi + 1].first_block : gridDim.x) - g.first_block;
-    const uint32_t lmask = (1u << g.L) - 1u;
-    const int N = (g.n + 31) / 32 * 32;
-    const int wpr = N / 32 * g.k;
-#pragma unroll 2
-    for (int64_t it = (blockIdx.x - g.first_block) * kDecodeThreads + threadIdx.x; it < items;
-         it += nblocks * kDecodeThreads) {
-        const int64_t r = it / nch;
-        const int j0 = (int)(it % nch) * 8;
-        uint32_t st[8];
-        if (g.states) {
-            const uint4 v = j0 < g.n ? __ldg(reinterpret_cast<const uint4 *>(g.states + r * g.lds + j0))
-                                     : make_uint4(0, 0, 0, 0);
-            const uint32_t raw[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                st[2 * h] = raw[h] & lmask;
-                st[2 * h + 1] = (raw[h] >> 16) & lmask;
-            }
-        } else {
-            // state of column j0 + i: the L bits at (N − 1 − j0 − i)·k = b0 + (7 − i)·k, b0 = (N − 8 − j0)·k
-            const uint32_t *row = g.codes + r * (int64_t)wpr;
-            const int64_t b0 = (int64_t)(N - 8 - j0) * g.k;
-            const int w0 = (int)(b0 >> 5), sh = (int)(b0 & 31);
-            uint32_t w[3];
-#pragma unroll
-            for (int q = 0; q < 3; ++q) w[q] = (w0 + q >= 0 && w0 + q < wpr) ? __ldg(row + w0 + q) : 0u;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int pos = sh + (7 - i) * g.k;
-                const int q = pos >> 5;
-                const uint32_t lo = q == 0 ? w[0] : w[1], hi = q == 0 ? w[1] : w[2];
-                st[i] = __funnelshift_r(lo, hi, pos & 31) & lmask;
-            }
-        }
-        uint32_t pk[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const uint32_t a = j0 + 2 * h < g.n ? tab[st[2 * h]] : 0u;
-            const uint32_t b = j0 + 2 * h + 1 < g.n ? tab[st[2 * h + 1]] : 0u;
-            pk[h] = a | (b << 16);
-        }
-        *reinterpret_cast<uint4 *>(g.out + r * g.ld + j0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    const int64_t first = (blockIdx.x - g.first_block) * kDecodeThreads + threadIdx.x;
+    const int64_t step = nblocks * kDecodeThreads;
+    switch (g.states ? 0 : g.k) {
+        case 0: decode_items<0>(g, tab, first, step); break;
+        case 1: decode_items<1>(g, tab, first, step); break;
+        case 2: decode_items<2>(g, tab, first, step); break;
+        case 3: decode_items<3>(g, tab, first, step); break;
+        default: decode_items<4>(g, tab, first, step); break;
     }
 }
 

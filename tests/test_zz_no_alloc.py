@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import table
+from conftest import GOLDEN, table
 from lookatmyquant_b200 import _lib
 
 
@@ -59,3 +59,7 @@ def test_noalloc_matches_workspace_entry_point_twice(k):
     X = torch.as_tensor(rng.standard_normal((1000, 24)), dtype=torch.float32).cuda()
     start = torch.as_tensor(rng.integers(0, 4096, 1000)).cuda()
     assert torch.equal(_viterbi_noalloc(lib, X, V, start, k), _viterbi_ws(lib, X, V, start, k))
+    # and the reference's own paths (tests/golden/viterbi.npz: free-start sequences of 256 entries)
+    g = np.load(GOLDEN / "viterbi.npz")
+    X = torch.as_tensor(g[f"k{k}_Xfree"], dtype=torch.float32).cuda()
+    assert np.array_equal(_viterbi_noalloc(lib, X, V, None, k).cpu().numpy(), g[f"k{k}_states_free"])
