@@ -199,9 +199,9 @@ class RowTrellisCode:
     """Each row as one trellis path along its columns, from state 0 (codes.py:386-410). Block LDLQ settles `width`
     columns at a time; each block's Viterbi also looks `look` columns ahead."""
 
-    def __init__(self, L: int, k: int, T: int = 256, width: int = 16, look: int = 8, seed: int = 0):
+    def __init__(self, L: int, k: int, T: int = 256, width: int = 16, look: int = 8, seed: int = 0, values=None):
         self.L, self.k, self.T, self.width, self.look, self.seed = L, k, T, width, look, seed
-        self.values = trellis_values(L, k, T, seed)
+        self.values = trellis_values(L, k, T, seed) if values is None else torch.as_tensor(values).double().cpu()
         self.state = None
 
     def step(self, j, X, ahead):
@@ -217,9 +217,9 @@ class RowTrellisCode:
 class TrellisCode:
     """Sequences of T consecutive outputs (one column) onto trellis paths (codes.py:363-383)."""
 
-    def __init__(self, L: int, k: int, T: int = 320, width: int = 16, seed: int = 0):
+    def __init__(self, L: int, k: int, T: int = 320, width: int = 16, seed: int = 0, values=None):
         self.L, self.k, self.T, self.width, self.seed = L, k, T, width, seed
-        self.values = trellis_values(L, k, T, seed)
+        self.values = trellis_values(L, k, T, seed) if values is None else torch.as_tensor(values).double().cpu()
 
     def _seqs(self, X):
         o, w = X.shape
@@ -331,6 +331,73 @@ def _col_trellis_sweep(X, S, env, code, settled_out=True):
     return T, states, settled
 
 
+def generic_trellis_sweep(X, S, env, code):
+    """The sweep of ldlq_words (codes.py:442-450) for trellises the fused kernels do not take (L < 12): the generic
+    block sweep (syntax.sweep, the reference's order, the run product on the fp64 tensor cores) with the code's
+    projection — RowTrellisCode.step (each row's path continued from its last state over the block and `look` columns
+    ahead) or TrellisCode.project (runs of T rows down each column) — through lamq_viterbi's kernel for fewer states.
+    X (rows × n fp64, device). Returns (states int16, settled values in units of S, fp64)."""
+    from .syntax import sweep
+    rows, n = X.shape
+    dev = X.device
+    settled = torch.empty_like(X)
+    states = torch.empty(rows, n, dtype=torch.int16, device=dev)
+    values = code.values.to(dev, torch.float64)
+    last = [torch.zeros(rows, dtype=torch.long, device=dev)]
+
+    def project(j, x, T):
+        xs = x[:, None] if code.width == 1 else x
+        w = xs.shape[1]
+        if isinstance(code, RowTrellisCode):
+            win = torch.cat([xs / S[:, None], T[:, j + w:j + w + code.look] / S[:, None]], 1)
+            path = viterbi(win, code.values, code.L, code.k, start=last[0])[:, :w]
+            last[0] = path[:, -1]
+        else:
+            o = xs.shape[0]
+            seqs = (xs / S[:, None]).reshape(o // code.T, code.T, w).permute(0, 2, 1).reshape(-1, code.T)
+            path = viterbi(seqs, code.values, code.L, code.k)
+            path = path.reshape(o // code.T, w, code.T).permute(0, 2, 1).reshape(o, w)
+        q = values[path]
+        settled[:, j:j + w] = q
+        states[:, j:j + w] = path.to(torch.int16)
+        q = q * S[:, None]
+        return q[:, 0] if code.width == 1 else q
+
+    sweep(X, env, project, width=code.width)
+    return states, settled
+
+
+def _gaussian_centroids(bounds: torch.Tensor) -> torch.Tensor:
+    """The mean of a unit Gaussian on each cell [bounds[j], bounds[j+1]] (nested.py:44-48)."""
+    phi = lambda x: torch.exp(-0.5 * x * x) / math.sqrt(2 * math.pi)
+    Phi = lambda x: 0.5 * (1 + torch.erf(x / math.sqrt(2)))
+    a, b = bounds[:-1], bounds[1:]
+    pa = torch.where(torch.isinf(a), torch.zeros_like(a), phi(a))
+    pb = torch.where(torch.isinf(b), torch.zeros_like(b), phi(b))
+    return (pa - pb) / (Phi(b) - Phi(a))
+
+
+def lloyd_max_levels(n: int, iters: int = 500) -> torch.Tensor:
+    """The best n levels for a unit Gaussian (nested.py:75-82): fp64 on the CPU."""
+    lv = _gaussian_centroids(torch.special.ndtri(torch.arange(n + 1, dtype=torch.float64) / n) * math.sqrt(3))
+    for _ in range(iters):
+        mid = (lv[1:] + lv[:-1]) / 2
+        bounds = torch.cat([torch.tensor([-math.inf], dtype=lv.dtype), mid, torch.tensor([math.inf], dtype=lv.dtype)])
+        lv = _gaussian_centroids(bounds)
+    return lv
+
+
+def synthetic_codebook(bits: int, seed: int = 0) -> tuple[int, torch.Tensor]:
+    """BASELINE config 3's codebook for a width: a Lloyd-Max fit to N(0, 1) with 2^(bits+4) entries rounded to fp16,
+    placed in state order as trellis_values orders its quantiles (codes.py:202-204: state s takes the level of rank
+    randperm(2^L)[s], torch's CPU generator seeded `seed`). Returns (L, values fp64)."""
+    L = bits + 4
+    S = 1 << L
+    levels = lloyd_max_levels(S).to(torch.float16).double()
+    perm = torch.randperm(S, generator=torch.Generator().manual_seed(seed))
+    return L, levels[perm]
+
+
 def _round_to_nearest(X, S, code):
     """The code applied directly, without H (codes.py:460-461 with `settled` None): each row from state 0 (row trellis,
     codes.py:406-409) or each run of T outputs down a column (column trellis, codes.py:371-378)."""
@@ -372,8 +439,11 @@ def ldlq_words(Ws: list[torch.Tensor], H: torch.Tensor | None, code, seeds: list
     else:
         Hd = H.to(dev, torch.float64)
         env = Environment(R_in.conj(Hd) if incoherent else Hd)
-        sweep = _row_trellis_sweep if isinstance(code, RowTrellisCode) else _col_trellis_sweep
-        _, states, settled = sweep(X, S, env, code)
+        if code.L != 12:  # fewer states than the fused kernels take: the generic sweep with the small Viterbi
+            states, settled = generic_trellis_sweep(X, S, env, code)
+        else:
+            sweep = _row_trellis_sweep if isinstance(code, RowTrellisCode) else _col_trellis_sweep
+            _, states, settled = sweep(X, S, env, code)
         env.check()
     fixed, T = (True, None) if isinstance(code, RowTrellisCode) else (False, code.T)
     out, r0 = [], 0

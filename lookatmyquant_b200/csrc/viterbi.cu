@@ -184,6 +184,97 @@ using namespace lamq;
 namespace lamq {
 namespace {
 
+// ----------------------------------------------------------------------------- trellises of fewer states
+//
+// L < 12 (BASELINE config 3's synthetic codebooks have 2^(bits+4) states: L = 5..8; L up to 11 is served): one warp
+// per sequence, the 2^L costs of the step before and the 2^(L−k) best values in shared memory, lane l handling states
+// l, l + 32, … . Each step takes best_t[r] = min_h cost_{t−1}[h·R + r] (the smallest h on ties, as torch.min) with its
+// h stored as a byte per r in the workspace (T x R bytes per sequence), then cost_t[s] = best_t[s >> k] + (x_t − C[s])²
+// with the subtraction, the square and the sum each rounded by itself in fp32, as the reference's tensor ops; the
+// final state is the first minimum (torch.argmin), and the path is read back from the stored choices.
+
+constexpr int kSmallWarps = 4;
+
+__global__ void __launch_bounds__(kSmallWarps * 32) viterbi_small_kernel(const float *__restrict__ X, int64_t rows,
+                                                                           int T, const float *__restrict__ values,
+                                                                           int L, int k, const int64_t *start,
+                                                                           int64_t *states, uint8_t *back) {
+    extern __shared__ __align__(16) float sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = 1 << L, R = 1 << (L - k), NB = 1 << k;
+    float *C = sm;                                   // S table values (shared by the CTA)
+    float *cost = sm + S + warp * (S + R);           // this warp's S costs
+    float *best = cost + S;                          // and R best values
+    for (int i = threadIdx.x; i < S; i += blockDim.x) C[i] = values[i];
+    __syncthreads();
+    const int64_t row = (int64_t)blockIdx.x * kSmallWarps + warp;
+    if (row >= rows) return;
+    const float *x = X + row * (int64_t)T;
+    uint8_t *bk = back + row * (int64_t)T * R;
+    const float inf = __int_as_float(0x7f800000);
+    const float x0 = __ldg(x);
+    const bool has_start = start != nullptr;
+    const int st0 = has_start ? (int)(start[row] & (S - 1)) : 0;
+    for (int s = lane; s < S; s += 32) {
+        const float d = __fsub_rn(x0, C[s]);
+        const float c = __fmul_rn(d, d);
+        // with a start state, only its successors ((start << k) | b) & mask are reachable at the first entry
+        cost[s] = (!has_start || (s >> k) == (st0 & (R - 1))) ? c : inf;
+    }
+    __syncwarp();
+    for (int t = 1; t < T; ++t) {
+        const float xt = __ldg(x + t);
+        for (int r = lane; r < R; r += 32) {
+            float m = cost[r];
+            int hb = 0;
+            for (int h = 1; h < NB; ++h) {
+                const float v = cost[h * R + r];
+                if (v < m) {
+                    m = v;
+                    hb = h;
+                }
+            }
+            best[r] = m;
+            bk[(int64_t)t * R + r] = (uint8_t)hb;
+        }
+        __syncwarp();
+        for (int s = lane; s < S; s += 32) {
+            const float d = __fsub_rn(xt, C[s]);
+            cost[s] = __fadd_rn(best[s >> k], __fmul_rn(d, d));
+        }
+        __syncwarp();
+    }
+    // the first state of minimum final cost (states visited in increasing order per lane, then the lanes merged)
+    float m = inf;
+    int ms = 0x7fffffff;
+    for (int s = lane; s < S; s += 32) {
+        const float v = cost[s];
+        if (v < m) {
+            m = v;
+            ms = s;
+        }
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, off);
+        const int os = __shfl_xor_sync(0xffffffffu, ms, off);
+        if (om < m || (om == m && os < ms)) {
+            m = om;
+            ms = os;
+        }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        int64_t *out = states + row * (int64_t)T;
+        int sc = ms;
+        out[T - 1] = sc;
+        for (int t = T - 1; t > 0; --t) {
+            const int r = sc >> k;
+            sc = (int)bk[(int64_t)t * R + r] * R + r;
+            out[t - 1] = sc;
+        }
+    }
+}
+
 // Back-pointer bytes of the one-warp kernel for sequences longer than kShortT (32 words of 8 bytes per entry), or
 // SIZE_MAX when rows x T x 256 does not fit a size_t.
 size_t backptr_bytes(int64_t rows, int T) {
@@ -225,7 +316,11 @@ int launch_viterbi_warp(const VitParams &p, int k, cudaStream_t stream, const ch
 }  // namespace lamq
 
 extern "C" size_t lamq_viterbi_workspace_size(int64_t rows, int T, int L, int k) {
-    (void)L;
+    if (L >= 2 && L < kL && k >= 1 && k < L) {  // fewer states: a byte per r per step
+        if (rows <= 0 || T <= 0) return 0;
+        const size_t per = (size_t)T << (L - k);
+        return (size_t)rows > SIZE_MAX / per ? SIZE_MAX : (size_t)rows * per;
+    }
     if (rows <= 0 || T <= kShortT) return 0;
     if (k >= 1 && k <= 4 && pair_long_fits(T, k)) return 0;  // the pair decoder keeps its back-pointers on chip
     return backptr_bytes(rows, T);
@@ -234,11 +329,30 @@ extern "C" size_t lamq_viterbi_workspace_size(int64_t rows, int T, int L, int k)
 extern "C" int lamq_viterbi(const float *X, int64_t rows, int T, const float *values, int L, int k,
                             const int64_t *start, int64_t *states, void *workspace, size_t workspace_bytes,
                             lamq_stream_t stream) {
-    LAMQ_REQUIRE(L == kL, "lamq_viterbi: only L = 12 is supported (got %d)", L);
-    LAMQ_REQUIRE(k >= 1 && k <= 4, "lamq_viterbi: k must be 1..4 (got %d)", k);
+    LAMQ_REQUIRE(L >= 2 && L <= kL, "lamq_viterbi: L must be 2..12 (got %d)", L);
+    LAMQ_REQUIRE(k >= 1 && k <= 4 && k < L, "lamq_viterbi: k must be 1..4 and below L (got %d)", k);
     LAMQ_REQUIRE(rows >= 0 && T >= 0, "lamq_viterbi: negative shape");
     if (rows == 0 || T == 0) return LAMQ_OK;
     LAMQ_REQUIRE(X && values && states, "lamq_viterbi: null pointer");
+    if (L < kL) {
+        const size_t need = lamq_viterbi_workspace_size(rows, T, L, k);
+        LAMQ_REQUIRE(need != SIZE_MAX && workspace_bytes >= need && workspace != nullptr,
+                     "lamq_viterbi: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+        const int64_t grid = (rows + kSmallWarps - 1) / kSmallWarps;
+        LAMQ_REQUIRE(grid <= INT_MAX, "lamq_viterbi: %lld sequences exceed the launch grid", (long long)rows);
+        const size_t smem = ((size_t)1 << L) * sizeof(float) +
+                            (size_t)kSmallWarps * (((size_t)1 << L) + ((size_t)1 << (L - k))) * sizeof(float);
+        const cudaError_t e = smem_limit_once((const void *)viterbi_small_kernel,
+                                              (int)((1 << 11) * 4 + kSmallWarps * ((1 << 11) + (1 << 10)) * 4));
+        if (e != cudaSuccess) {
+            set_error("lamq_viterbi: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        viterbi_small_kernel<<<(unsigned)grid, kSmallWarps * 32, smem, (cudaStream_t)stream>>>(
+            X, rows, T, values, L, k, start, states, reinterpret_cast<uint8_t *>(workspace));
+        LAMQ_CHECK_LAUNCH("lamq_viterbi (fewer states)");
+        return LAMQ_OK;
+    }
     if (T > kShortT && pair_long_fits(T, k)) {
         LAMQ_REQUIRE((rows + 1) / 2 <= INT_MAX, "lamq_viterbi: %lld sequences exceed the launch grid", (long long)rows);
         VitParams p{X, rows, T, values, start, states, nullptr};

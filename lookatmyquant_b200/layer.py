@@ -336,7 +336,21 @@ def build_layer_from_host(stages, weights, acts, w, bits, layer: int = 0, group=
 
 
 def sweep_rows(X, S, env, row_bits, tables=None):
-    """The fused row-trellis LDLQ sweep (lamq_ldlq_rowtrellis) with per-row widths; returns (states, settled)."""
+    """The fused row-trellis LDLQ sweep (lamq_ldlq_rowtrellis) with per-row widths; returns (states, settled).
+    `tables` may instead be {width: (L, values)} codebooks with L < 12 (BASELINE config 3's synthetic codebooks):
+    then each width's rows take the generic sweep with the small-state Viterbi (codes.generic_trellis_sweep)."""
+    if isinstance(tables, dict):
+        dev = X.device
+        states = torch.empty(X.shape, dtype=torch.int16, device=dev)
+        settled = torch.empty_like(X)
+        for k, (L, values) in tables.items():
+            idx = torch.nonzero(row_bits.to(dev) == k).flatten()
+            if idx.numel() == 0:
+                continue
+            code = codes.RowTrellisCode(L, k, T=256, width=codes.WIDTH, look=codes.LOOK, values=values)
+            st, se = codes.generic_trellis_sweep(X[idx].contiguous(), S[idx].contiguous(), env, code)
+            states[idx], settled[idx] = st, se
+        return states, settled
     from . import _lib
     from ._lib import check, ptr, stream_ptr
     dev = X.device
@@ -374,10 +388,14 @@ def main():
     ap = argparse.ArgumentParser(description=main.__doc__)
     ap.add_argument("--tokens", type=int, default=384 * 2048)
     ap.add_argument("--repeat", type=int, default=1)
+    ap.add_argument("--codebooks", choices=["reference", "synthetic"], default="reference",
+                    help="the reference's 4096-state L = 12 tables for every width, or BASELINE config 3's "
+                         "2^(bits+4)-entry Lloyd-Max codebooks (L = bits + 4, the generic sweep)")
     a = ap.parse_args()
     dev = torch.device("cuda")
     stages, weights, acts, w, bits = config3(a.tokens, device=dev)
-    tables = stacked_tables(12, 256, dev)
+    tables = stacked_tables(12, 256, dev) if a.codebooks == "reference" else \
+        {b: codes.synthetic_codebook(b) for b in (1, 2, 3, 4)}
     for _ in range(a.repeat):
         times = {}
         for s in stages:
@@ -386,7 +404,8 @@ def main():
             build_stage(s, weights, *acts[s.name], w, bits, 0, None, True, tables)
             torch.cuda.synchronize()
             times[s.name] = round((time.perf_counter() - t0) * 1e3, 2)
-        print(json.dumps({"stage_ms": times, "total_ms": round(sum(times.values()), 2)}), flush=True)
+        print(json.dumps({"codebooks": a.codebooks, "stage_ms": times, "total_ms": round(sum(times.values()), 2)}),
+              flush=True)
 
 
 if __name__ == "__main__":

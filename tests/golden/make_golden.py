@@ -69,7 +69,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--only", choices=["artifact", "fit", "neartie", "ldlq_gpu", "statistics", "kl", "best_word",
-                                       "embedding", "importance", "finetune", "dropin"],
+                                       "embedding", "importance", "finetune", "dropin", "small_l"],
                     help="write only this fixture (the others stay as committed)")
     ap.add_argument("--case", type=Path, help="for --only neartie: an .npz with X (1 x T), values (4096) and k")
     args = ap.parse_args()
@@ -111,6 +111,9 @@ def main():
         return
     if args.only == "dropin":
         write_dropin_fixture(C, Q, torch)
+        return
+    if args.only == "small_l":
+        write_small_l_fixture(C, torch)
         return
     # the reference's fitted L=12 tables, as raw fp64
     TABLES.mkdir(parents=True, exist_ok=True)
@@ -238,6 +241,7 @@ def main():
     write_importance_fixture(Q, torch, args.reference.resolve())
     write_finetune_fixture(C, torch)
     write_dropin_fixture(C, Q, torch)
+    write_small_l_fixture(C, torch)
     print("golden vectors written to", HERE)
 
 
@@ -564,6 +568,57 @@ def write_dropin_fixture(C, Q, torch):
         out[f"w{i}_states"] = sts[0].numpy()
     out["words_calls"] = np.array(len(words_calls))
     np.savez_compressed(HERE / "dropin.npz", **out)
+
+
+def write_small_l_fixture(C, torch):
+    """18. Trellises of fewer states (BASELINE config 3's synthetic codebooks: a Lloyd-Max fit to N(0, 1) with
+    2^(bits+4) entries, fp16, in the state order trellis_values gives its quantiles): the reference's
+    nested.lloyd_max_levels, its viterbi at L = 5..11 (with and without start states), and its ldlq_words with a row
+    trellis (L = 6, k = 2) and a column trellis (L = 7, k = 3, T = 64) on those codebooks."""
+    from opgraph import nested as NS
+    out = {}
+    g = torch.Generator().manual_seed(7100)
+
+    def codebook(bits):
+        L = bits + 4
+        levels = NS.lloyd_max_levels(1 << L).to(torch.float16).double()
+        return L, levels[torch.randperm(1 << L, generator=torch.Generator().manual_seed(0))]
+    for bits in (1, 2, 3, 4):
+        L, v = codebook(bits)
+        out[f"codebook_{bits}"] = v.numpy()
+    out["lloyd_max_levels_64"] = NS.lloyd_max_levels(64).numpy()
+    cases = [("a", 6, 2, 64, 24, True), ("b", 5, 1, 32, 256, False), ("c", 8, 4, 48, 24, True), ("d", 11, 3, 8, 40, False),
+             ("e", 7, 3, 40, 320, True)]
+    for name, L, k, rows, T, with_start in cases:
+        v = torch.randn(1 << L, generator=g, dtype=torch.float64).float().double()
+        X = torch.randn(rows, T, generator=g, dtype=torch.float64).float().double()
+        start = torch.randint(0, 1 << L, (rows,), generator=g) if with_start else None
+        out[f"v{name}_meta"] = np.array([L, k, int(with_start)])
+        out[f"v{name}_values"], out[f"v{name}_X"] = v.numpy(), X.numpy()
+        if with_start:
+            out[f"v{name}_start"] = start.numpy()
+        out[f"v{name}_states"] = C.viterbi(X, v, L, k, start=start).numpy()
+    real = C.trellis_values
+    try:
+        L, v = codebook(2)
+        C.trellis_values = lambda *a, **kw: v
+        code = C.RowTrellisCode(L, 2, T=256, width=16, look=8)
+        W = (0.02 * torch.randn(64, 256, generator=g, dtype=torch.float64)).float().double()
+        H = calib_H(256, 2048, 7101)
+        net = C.ldlq_words([W], H, code, [7102], in_seed=7103, out_rot=False)[0]
+        out.update({"row_W": W.float().numpy(), "row_H": H.float().numpy(), "row_Wq": net.matrix(dtype=torch.float64).numpy(),
+                    "row_settled": net.cores["W"].data.numpy()})
+        L, v = codebook(3)
+        C.trellis_values = lambda *a, **kw: v
+        code = C.TrellisCode(L, 3, T=64)
+        W = (0.02 * torch.randn(128, 64, generator=g, dtype=torch.float64)).float().double()
+        H = calib_H(64, 1024, 7104)
+        net = C.ldlq_words([W], H, code, [7105])[0]
+        out.update({"col_W": W.float().numpy(), "col_H": H.float().numpy(), "col_Wq": net.matrix(dtype=torch.float64).numpy(),
+                    "col_settled": net.cores["W"].data.numpy().reshape(128, 64)})
+    finally:
+        C.trellis_values = real
+    np.savez_compressed(HERE / "small_l.npz", **out)
 
 
 def ast_def():

@@ -35,9 +35,9 @@ def test_every_declared_symbol_is_exported(lib):
 def test_abi_version_and_errors_without_gpu(lib):
     assert lib.lamq_abi_version() >= 1
     # argument validation happens before any CUDA call
-    st = lib.lamq_viterbi(None, 4, 8, None, 11, 2, None, None, None, 0, None)
+    st = lib.lamq_viterbi(None, 4, 8, None, 13, 2, None, None, None, 0, None)
     assert st == _lib.LAMQ_ERR_INVALID
-    assert b"L = 12" in lib.lamq_last_error()
+    assert b"L must be 2..12" in lib.lamq_last_error()
     st = lib.lamq_ldlq_rowtrellis(None, 16, 4, 16, None, 16, None, None, None, None, 2, 12, 16, 20, 128,
                                   None, None, None, 0, None)
     assert st == _lib.LAMQ_ERR_INVALID

@@ -204,3 +204,15 @@ def test_embedding_buckets_and_frequency_order_match_reference(golden):
     assert embedding_buckets(49152) == list(g["buckets_49152"])
     assert embedding_buckets(1000) == list(g["buckets_1000"])
     assert torch.equal(frequency_order(torch.as_tensor(g["freq_ids"]), 600), torch.as_tensor(g["freq_order"]))
+
+
+def test_synthetic_codebooks_match_reference(golden):
+    """BASELINE config 3's codebooks: nested.lloyd_max_levels restated (fp64, to 1e-12), and the fp16 levels in
+    the state order trellis_values gives its quantiles, exactly (small_l.npz, by the reference)."""
+    import torch
+    from lookatmyquant_b200.codes import lloyd_max_levels, synthetic_codebook
+    g = golden("small_l")
+    assert np.abs(lloyd_max_levels(64).numpy() - g["lloyd_max_levels_64"]).max() <= 1e-12
+    for bits in (1, 2, 3, 4):
+        L, v = synthetic_codebook(bits)
+        assert L == bits + 4 and torch.equal(v, torch.as_tensor(g[f"codebook_{bits}"]))

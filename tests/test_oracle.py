@@ -211,3 +211,12 @@ def test_kl_fixture_formula(golden):
     g = golden("kl")
     assert abs(float(g["kl_pos"].astype(np.float64).mean()) - float(g["kl"])) <= 1e-6
     assert float(g["kl"]) > 0.1
+
+
+def test_oracle_viterbi_on_fewer_states(golden):
+    """The C restatement at L = 5..11 against the reference's viterbi (small_l.npz)."""
+    g = golden("small_l")
+    for c in "abcde":
+        L, k, with_start = (int(v) for v in g[f"v{c}_meta"])
+        out = O.viterbi(g[f"v{c}_X"], g[f"v{c}_values"], L, k, start=g[f"v{c}_start"] if with_start else None)
+        assert np.array_equal(out, g[f"v{c}_states"]), c
