@@ -24,6 +24,14 @@
 // From d = 512 on, xtx_pair_kernel (below) computes 256 × 256 tiles on pairs of CTAs (cta_group::2 MMAs): half the
 // operand bytes per CTA per flop, a 6-stage ring.
 //
+// Flush order: a tile's chunks are added into the accumulator in chunk order, whichever CTAs computed them. Each
+// launch has one ticket per (tile, CTA of the pair) counting the drain threads that have added their part of a chunk;
+// a drain thread adds chunk c only once the ticket reaches 256·c (the units of a tile's chunks are issued in chunk
+// order, so the wait is on earlier units and ends), then counts itself. Every element's fp32 sum therefore runs in the same order on every
+// run: the statistics, and the layer built from them, are bit-reproducible for a given call sequence. Inside a full
+// window a tile's chunks fall to one CTA and the ticket is always ready; a wait longer than kGateTimeoutNs (CTAs not
+// co-resident) adds unordered rather than stall.
+//
 // Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
 // (A = X, B = X: exact products), and the weighted tokens add Σ_t (w_t − 1)·x_t x_tᵀ in a second pass over only
 // those tokens, with (w − 1)·x split into a bf16 pair hi + lo (hi = bf16(y), lo = bf16(y − hi)), which carries y to
@@ -63,6 +71,8 @@ constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;
 // error) switches the gate off for the rest of the launch.
 constexpr unsigned long long kGateTimeoutNs = 20000000ull;
 constexpr int kGateSlots = 64;
+constexpr int kTicketSlots = 16;
+constexpr int kMaxTickets = 2 * 128 * 128;  // tickets of the largest ordered launch: d <= 32768 (128 x 128 pair tiles)
 
 struct GemmParams {
     float *acc;
@@ -81,10 +91,13 @@ struct GemmParams {
     int64_t units;
     int *status;
     unsigned int *gate;     // units whose loads have all been issued (the wave gate), zeroed before the launch
+    unsigned int *tickets;  // per tile and CTA of the pair: chunks added so far (zeroed), or null: unordered adds
 };
 
 struct Unit {
     int ti, tj, kb0, nkb;
+    int64_t tile;  // index in the band raster
+    int chunk;
 };
 
 // Tiles of column tj inside the band of row tiles [b0, b1). Symmetric C: row tile ti (rows 128·ti..) and column tile
@@ -127,6 +140,8 @@ __device__ bool unit_at(int64_t u, const GemmParams &p, Unit &out) {
         idx = full * p.win + rem % last;
     }
     tile_at(idx, p, out.ti, out.tj);
+    out.tile = idx;
+    out.chunk = chunk;
     out.kb0 = chunk * p.kblocks_per_chunk;
     out.nkb = min(p.kblocks_per_chunk, p.kblocks - out.kb0);
     return true;
@@ -136,6 +151,31 @@ __device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int *p) {
     unsigned int v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int *p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Before a unit's tile is added: wait until every drain thread has added the tile's earlier chunks (see "Flush order"
+// above; each drain thread waits for itself, so no barrier is shared with a thread that may have stopped on an error).
+__device__ __forceinline__ void flush_wait(const unsigned int *ticket, int chunk) {
+    if (ticket == nullptr || chunk == 0) return;
+    const unsigned int target = (unsigned int)chunk * (kEpiWarps * 32);
+    const unsigned long long t0 = globaltimer();
+    while (ld_acquire_u32(ticket) < target) {
+        if (globaltimer() - t0 > kGateTimeoutNs) break;  // not co-resident: add unordered rather than stall
+        __nanosleep(64);
+    }
+}
+
+// After a drain thread's adds: they are performed before its count reaches the ticket.
+__device__ __forceinline__ void flush_done(unsigned int *ticket) {
+    if (ticket == nullptr) return;
+    __threadfence();
+    atomicAdd(ticket, 1u);
 }
 
 // 32 lanes x 32 bits, 32 consecutive columns: thread t of the warp gets lane (base lane + t).
@@ -320,6 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc ^= 1;
             }
             if (!ok) break;
+            unsigned int *ticket = p.tickets ? p.tickets + 2 * U.tile : nullptr;
+            flush_wait(ticket, U.chunk);
             const int i = U.ti * BM + 32 * q + lane;
             if (i < p.d) {
 #pragma unroll
@@ -328,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
                 }
             }
+            flush_done(ticket);
         }
     }
     tc_fence_before();
@@ -512,6 +555,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc ^= 1;
             }
             if (!ok) break;
+            unsigned int *ticket = p.tickets ? p.tickets + 2 * U.tile + rank : nullptr;
+            flush_wait(ticket, U.chunk);
             const int i = U.ti * 256 + 128 * (int)rank + 32 * q + lane;
             if (i < p.d) {
 #pragma unroll
@@ -520,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
                 }
             }
+            flush_done(ticket);
         }
     }
     tc_fence_before();
@@ -616,6 +662,44 @@ int make_map(CUtensorMap *m, const void *base, int64_t tokens, int d, int64_t ld
 
 constexpr int kMaxDevices = 64;
 __device__ unsigned int g_gate[kGateSlots];  // one array per device (module globals are per device)
+__device__ unsigned int g_tickets[kTicketSlots][kMaxTickets];
+
+// The flush tickets of one launch on the current device (`n` of them, zeroed on the launch's stream), or null when
+// the launch has more tiles than a slot holds (its adds are then unordered). Slots go round robin like the gate's.
+int ticket_slot(cudaStream_t stream, int64_t n, unsigned int **out) {
+    static std::mutex mu;
+    static unsigned int *base[kMaxDevices] = {};
+    static unsigned int next[kMaxDevices] = {};
+    *out = nullptr;
+    if (n > kMaxTickets) return LAMQ_OK;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("lamq_xtx_accumulate: no usable current device");
+        return LAMQ_ERR_CUDA;
+    }
+    unsigned int *slot;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (base[dev] == nullptr) {
+            void *sym = nullptr;
+            e = cudaGetSymbolAddress(&sym, g_tickets);
+            if (e != cudaSuccess || sym == nullptr) {
+                set_error("lamq_xtx_accumulate: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+                return LAMQ_ERR_CUDA;
+            }
+            base[dev] = reinterpret_cast<unsigned int *>(sym);
+        }
+        slot = base[dev] + (size_t)(next[dev]++ % kTicketSlots) * kMaxTickets;
+    }
+    e = cudaMemsetAsync(slot, 0, (size_t)n * sizeof(unsigned int), stream);
+    if (e != cudaSuccess) {
+        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    *out = slot;
+    return LAMQ_OK;
+}
 
 // A wave-gate counter for one launch on the current device: slots are handed out round robin (launches in flight at
 // once take different slots) and zeroed on the launch's stream.
@@ -723,6 +807,11 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
     p.ntiles = tiles;
     st = gate_counter((cudaStream_t)stream, &p.gate);
     if (st != LAMQ_OK) return st;
+    // one chunk per tile needs no order
+    if (p.nchunk > 1) {
+        st = ticket_slot((cudaStream_t)stream, 2 * tiles, &p.tickets);
+        if (st != LAMQ_OK) return st;
+    }
     cudaError_t e;
     if (p.pair) {
         const int64_t clusters = std::min<int64_t>(p.units, num_sms() / 2);

@@ -169,6 +169,16 @@ def run(device="cuda", log=print, only=None) -> list:
                     "fp64 tensor"))
         del D, qep
 
+    if want("dgemm"):  # the recursion's top-level product size at n = 9728 (the 128 x 128 CTA tile)
+        from .linalg import gemm
+        m = n // 2
+        A = torch.randn(m, m, dtype=torch.float64, device=dev, generator=g)
+        B = torch.randn(m, m, dtype=torch.float64, device=dev, generator=g)
+        ms = timer(lambda: gemm(A, B), reps=3)
+        add(_record("a5", "dgemm_kernel (128 x 128 tiles, mma.sync f64)", f"{m}^3", ms, 2.0 * m ** 3, "TFLOP/s",
+                    FP64_TENSOR_TF, "the factorizations' largest products", "fp64 tensor"))
+        del A, B
+
     if want("a3"):  # the randomized Hadamard transform of a stage's targets (9728 x 2560) and of H (9728²)
         for n_, rows_ in ((2560, 9728), (9728, 2560)):
             rot = Rotation(n_, 301, dev)
@@ -301,7 +311,7 @@ def table(recs) -> str:
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--out", default=None, help="write the records as JSON")
-    ap.add_argument("--only", nargs="+", default=None, help="rows to measure (a1 a2 a3 a5 a6 a7 a8 a13 a14 a15)")
+    ap.add_argument("--only", nargs="+", default=None, help="rows to measure (a1 a2 a3 a5 dgemm a6 a7 a8 a13 a14 a15)")
     a = ap.parse_args()
     recs = run(only=set(a.only) if a.only else None)
     print(table(recs), flush=True)

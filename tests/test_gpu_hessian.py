@@ -148,3 +148,24 @@ def test_config2_d9728_token_subset_against_oracle():
     H, _ = hessian(X, w)
     ref, _ = O.hessian_accumulate([X.float().cpu().numpy()], [w.cpu().numpy()])
     assert rel(H.cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.parametrize("tokens,d,chunk", [(100000, 256, 4096), (131072, 2560, 8192), (32768, 9728, 4096)])
+def test_statistics_are_bit_reproducible(tokens, d, chunk):
+    """Each tile's chunks are added into the fp32 accumulators in chunk order, whichever CTAs computed them: three runs
+    give the same bits. The shapes take every schedule: all units in one wave with a tile's chunks side by side
+    (d = 256), tiles fewer than CTA pairs (d = 2560), and full windows plus a partial last one (d = 9728)."""
+    from lookatmyquant_b200.hessian import Statistics
+    X, Xr = acts(tokens, d, 11).cuda(), acts(tokens, d, 12).cuda()
+    w = weights(tokens, 13).cuda()
+    runs = []
+    for _ in range(3):
+        st = Statistics(d, cross=True, device="cuda", chunk_tokens=chunk)
+        st.add(X, w, Xr)
+        torch.cuda.synchronize()
+        st.check_status()
+        runs.append((st.accH.clone(), st.accD.clone()))
+        del st
+    for H, D in runs[1:]:
+        assert torch.equal(H, runs[0][0])
+        assert torch.equal(D, runs[0][1])

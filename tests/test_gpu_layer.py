@@ -68,6 +68,29 @@ def test_build_from_host_equals_the_device_build():
             assert ((sa - sb).abs() <= 1e-6 * sb.abs()).all()
 
 
+def test_layer_build_is_bit_reproducible():
+    """Two builds of the same layer from the same inputs give identical states and scales (the statistics are summed
+    chunk by chunk in a fixed order, and every later step is deterministic): 100,000 tokens make four chunks per
+    statistics launch."""
+    from lookatmyquant_b200.layer import StageSpec, build_layer, build_layer_from_host
+    from lookatmyquant_b200.workloads import config3
+    stages = [StageSpec("attn_in", 256, [("self_attn.q_proj", 256), ("self_attn.k_proj", 128)], "self_attn"),
+              StageSpec("down_in", 320, [("mlp.down_proj", 192)], "mlp")]
+    stages, weights, acts, w, bits = config3(100000, stages=stages)
+    a = build_layer(stages, weights, acts, w, bits, dequantize=False)
+    b = build_layer(stages, weights, acts, w, bits, dequantize=False)
+    host_acts = {k: (x.cpu().pin_memory(), y.cpu().pin_memory()) for k, (x, y) in acts.items()}
+    host_w = {k: v.cpu().pin_memory() for k, v in weights.items()}
+    c = build_layer_from_host(stages, host_w, host_acts, w.cpu().pin_memory(), bits, chunk_tokens=65536)
+    d = build_layer_from_host(stages, host_w, host_acts, w.cpu().pin_memory(), bits, chunk_tokens=65536)
+    for s in stages:
+        for nm, _ in s.matrices:
+            assert torch.equal(a[s.name].states[nm], b[s.name].states[nm])
+            assert torch.equal(a[s.name].scales[nm], b[s.name].scales[nm])
+            assert torch.equal(c[s.name].states[nm], d[s.name].states[nm])
+            assert torch.equal(c[s.name].scales[nm], d[s.name].scales[nm])
+
+
 def test_full_config3_layer_row_subsets_match_oracle():
     """BASELINE config 3 at full size: one Qwen3-4B-class layer (all four stages, 786,432 weighted calibration
     tokens, d up to 9728, the 1-4-bit row plan) built on the device; per stage the oracle forms the QEP target, the
