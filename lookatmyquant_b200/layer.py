@@ -110,7 +110,8 @@ def _reduce_finalize(st: Statistics, group, n_tok_total):
         torch.distributed.all_reduce(st.accH, group=group)
         torch.distributed.all_reduce(st.accD, group=group)
         if n_tok_total is None:  # ranks may hold unequal shares (token_shard splits whole chunks): sum them
-            cnt = torch.tensor([float(n_tok)], dtype=torch.float64, device=st.accH.device)
+            # a fill on the device, not a copy from host memory (which would queue behind a host build's bulk copies)
+            cnt = torch.full((1,), float(n_tok), dtype=torch.float64, device=st.accH.device)
             torch.distributed.all_reduce(cnt, group=group)
             n_tok_total = int(cnt.item())
         n_tok = n_tok_total
@@ -119,10 +120,10 @@ def _reduce_finalize(st: Statistics, group, n_tok_total):
 
 def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, bits: dict, layer: int = 0, group=None,
                                 dequantize: bool = True, tables=None, n_tok_total: int | None = None, HD=None,
-                                factors=None) -> StageResult:
+                                factors=None, rot=None) -> StageResult:
     """The stage after its statistics have been accumulated (all of this rank's tokens added to `st`). `HD` (H, D)
     and `factors` (env, Linv, qep_status) skip the reduction and the factorizations when they were done already
-    (build_stages_sharded)."""
+    (build_stages_sharded); `rot` is the stage's input rotation when the caller made it already."""
     dev = st.device if st is not None else HD[0].device
     world = group.size() if group is not None else 1
     rank = group.rank() if group is not None else 0
@@ -136,7 +137,7 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     # factorization of R·H·Rᵀ), are independent: the first runs on a side stream while the second runs on the main one
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev)
-    rot = Rotation(spec.d, in_seed, dev)
+    rot = Rotation(spec.d, in_seed, dev) if rot is None else rot
     if factors is None and world >= 2:
         # two ranks factor at once, one matrix each, and broadcast the factors (NVLink): the QEP's inverse Cholesky
         # factor from rank 1, the environment's U from rank 0
@@ -282,17 +283,36 @@ def _copy_stream(dev) -> torch.cuda.Stream:
     return _COPY[dev]
 
 
+def tail_order(stages, world: int = 1) -> list:
+    """The stages ordered by the work that follows their statistics, largest first: the two factorizations (∝ d³)
+    and the sweep of this rank's rows (∝ rows·d / world). A host build copies the stages in this order, so the stage
+    whose factor-and-sweep tail is shortest arrives last and little compute is left once the last byte is resident.
+    The coefficients are B200 timings (d = 9728: ~130 ms of factorizations and QEP map; 2560 x 9728 rows swept in
+    ~74 ms); only the order matters."""
+    def tail(s):
+        rows = sum(r for _, r in s.matrices)
+        return 1.4e-13 * float(s.d) ** 3 + 2.5e-9 * rows * s.d / max(1, world)
+    return sorted(stages, key=lambda s: -tail(s))
+
+
 def build_layer_from_host(stages, weights, acts, w, bits, layer: int = 0, group=None, n_tok_total: int | None = None,
                           chunk_tokens: int = 65536, device=None):
     """The layer build from host memory: `weights[name]` and `acts[stage] = (x, x_ref)` are pinned CPU tensors (this
     rank's token shard), `w` the pinned per-token weights. Every copy is queued at once on a copy stream, chunk by
     chunk and stage by stage, so the statistics kernel consumes each chunk as soon as it is resident and the later
     stages' activations arrive while the earlier stages factor and sweep: the build takes about the longer of the
-    host→device transfer and the compute instead of their sum. The weighted tokens of each chunk are found on the
-    host. Returns {stage: StageResult} with states and scales in pinned host memory (the call synchronizes)."""
+    host→device transfer and the compute instead of their sum. The stages go in `tail_order` (each stage's inputs are
+    given, so the order changes no result): the stage with the least work after its statistics comes last. The
+    weighted tokens of each chunk are found on the host. Everything small the stages need from the host (the row
+    widths, the rotations' signs and factors) goes to the device before the bulk copies are queued: a copy from
+    pageable memory queued behind them would wait for all of them. Returns {stage: StageResult} with states and
+    scales in pinned host memory (the call synchronizes)."""
     dev = torch.device(device or "cuda")
     copy, main = _copy_stream(dev), torch.cuda.current_stream(dev)
     tables = stacked_tables(12, 256, dev)
+    stages = tail_order(stages, group.size() if group is not None else 1)
+    bits = {nm: bits[nm].to(dev) for s in stages for nm, _ in s.matrices}
+    rots = {s.name: Rotation(s.d, _in_seed(s, layer), dev) for s in stages}
     copy.wait_stream(main)
     staged = []
     with torch.cuda.stream(copy):
@@ -326,7 +346,8 @@ def build_layer_from_host(stages, weights, acts, w, bits, layer: int = 0, group=
             main.wait_event(ev)
             st.add(x_d[c0:c1], w_d[c0:c1], xr_d[c0:c1], weighted=idx)
         del x_d, xr_d, chunks
-        res = build_stage_from_statistics(s, wts, st, bits, layer, group, False, tables, n_tok_total)
+        res = build_stage_from_statistics(s, wts, st, bits, layer, group, False, tables, n_tok_total,
+                                          rot=rots[s.name])
         for nm in list(res.states):
             res.states[nm] = res.states[nm].to("cpu", non_blocking=True)
             res.scales[nm] = res.scales[nm].to("cpu", non_blocking=True)
