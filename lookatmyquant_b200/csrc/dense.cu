@@ -278,46 +278,120 @@ __device__ __forceinline__ void chol_inv16(double *S, int ld, double *Xd, int *b
 // Factors the nb x nb diagonal block at A[k0][k0] in place (lower Cholesky; the block's strict upper part set to zero)
 // and writes its inverse to X[k0][k0] (lower, strict upper zero). A non-positive pivot sets *status = LAMQ_ERR_NOT_PD.
 // Blocked by 16-column panels on the fp64 tensor cores, 8 warps, warp w owning rows [16w, 16w + 16); the block is
-// padded to a multiple of 16 with the identity and kept in shared memory (row stride ≡ 4 mod 16 doubles).
-//   Cholesky, panel p: warp p factors and inverts its diagonal 16 x 16 block (L_pp, X_pp = L_pp⁻¹); | barrier |
-//     every later warp forms its rows of the panel, L21 = A21·X_ppᵀ, with two m16n8k16 MMAs; | barrier | and updates
-//     its trailing tiles up to its own diagonal block, A22 −= L21·L21ᵀ. The next panel's diagonal block belongs to the
-//     warp that just updated it, so no barrier is needed before it is factored.
-//   Inverse, by row panels with R = I in registers (warp w: its rows, 16 column tiles of 16 x 8): panel q forms
-//     X[q] = X_qq·R[q] (its rows of L⁻¹) in shared memory; | barrier | later warps update R[w] −= L[w][q]·X[q]; | barrier |.
+// padded to a multiple of 16 with the identity and kept in shared memory (row stride ≡ 4 mod 16 doubles). The rows of
+// the inverse, R (warp w: its rows, 16 column tiles of 16 x 8 in registers, starting at I), are formed in the same
+// panel loop: X[q] = X_qq·R[q] once R[q] has taken every R[q] −= L[q][j]·X[j], j < q. Panel p:
+//   (a) warp p factors and inverts its diagonal 16 x 16 block (L_pp, X_pp = L_pp⁻¹);                     | barrier |
+//   (b) every later warp forms its rows of the panel, L21 = A21·X_ppᵀ (two m16n8k16 MMAs), and stores them; warp p + 1
+//       then updates its diagonal block (the next panel's) from its own rows; warp p stores L_pp;         | barrier |
+//   (c) warps w > p + 1 update their trailing tiles up to their own diagonal block, A22 −= L21·L21ᵀ, and take
+//       R[w] −= L[w][p−1]·X[p−1]; warp p takes its last two updates (with X[p−2] and X[p−1]) and forms X[p] = X_pp·R[p]
+//       into one of two row-panel buffers (and global memory); warp p + 1 goes on to factor.
+// The chain that sets the leaf's time is (a) → (b) → (a) of the next panel: every product of (c), the inverse's
+// included, runs beside the next factor step, and warp p + 1 defers its update with X[p − 1] to the panel it factors.
 constexpr int kLeafThreads = 256;
 constexpr int kLeafLd = NB + 4;
-constexpr size_t kLeafSmem = (size_t)(NB * kLeafLd + 8 * 16 * kLeafLdd + 16 * kLeafLd) * sizeof(double);
+constexpr size_t kLeafSmem = (size_t)(NB * kLeafLd + 8 * 16 * kLeafLdd + 2 * 16 * kLeafLd) * sizeof(double);
+
+// R[w] −= L[w][q]·X[q] over the column tiles ct < 2q + 2 (the only non-zero ones of X[q]): Lq = this warp's band at
+// column 16q, Xq = the row panel of X[q].
+__device__ __forceinline__ void leaf_inverse_update(double (&R)[16][4], const double *Lq, const double *Xq, int q,
+                                                    int g, int tq) {
+    double af[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) af[e] = -Lq[(g + 8 * (e & 1)) * kLeafLd + tq + 4 * (e >> 1)];
+#pragma unroll
+    for (int ct = 0; ct < 16; ++ct) {
+        if (ct >= 2 * q + 2) continue;  // warp-uniform
+        double bf[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bf[e] = Xq[(tq + 4 * e) * kLeafLd + 8 * ct + g];
+        dmma16816(R[ct], af, bf);
+    }
+}
+
+// This warp's band −= L21·L21ᵀ over its column tiles ct0 .. ct1 (L21: the band's and the tiles' rows at column j0).
+__device__ __forceinline__ void leaf_trailing(double *band, const double *Ls, int j0, int ct0, int ct1, int g,
+                                              int tq) {
+    double af[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) af[e] = -band[(g + 8 * (e & 1)) * kLeafLd + j0 + tq + 4 * (e >> 1)];
+#pragma unroll
+    for (int ct = 2; ct < 16; ++ct) {  // unrolled so the independent tiles' MMAs overlap
+        if (ct < ct0 || ct > ct1) continue;  // warp-uniform
+        double bf[4], cf[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) bf[e] = Ls[(8 * ct + g) * kLeafLd + j0 + tq + 4 * e];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const double2 v = *reinterpret_cast<const double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq);
+            cf[2 * h] = v.x;
+            cf[2 * h + 1] = v.y;
+        }
+        dmma16816(cf, af, bf);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            *reinterpret_cast<double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq) =
+                make_double2(cf[2 * h], cf[2 * h + 1]);
+    }
+}
 
 __global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, int64_t lda, int k0, int nb,
                                                                      double *X, int64_t ldx, int *status) {
     extern __shared__ __align__(16) double lsm[];
     double *Ls = lsm;                         // the padded block, row-major; L on the way out
     double *Xd = Ls + NB * kLeafLd;           // the diagonal blocks' inverses, 16 x kLeafLdd each
-    double *Xp = Xd + 8 * 16 * kLeafLdd;      // one row panel of L⁻¹ (inverse phase)
+    double *Xp0 = Xd + 8 * 16 * kLeafLdd;     // two row panels of L⁻¹: X[q] in Xp0 + (q & 1)·16·kLeafLd
     __shared__ int bad;
     const int t = threadIdx.x, w = t >> 5, lane = t & 31, g = lane >> 2, tq = lane & 3;
     const int P = (nb + 15) >> 4, nbp = 16 * P;
-    // staging: thread t covers column t % 128 of rows t / 128, t / 128 + 2, ... (16 independent loads in flight)
+    double *Ab = A + (int64_t)k0 * lda + k0;
+    // staging: thread t covers columns 2(t % 64), 2(t % 64) + 1 of rows t / 64, t / 64 + 4, …: 32 loads in flight
+    // (16-byte loads when the rows allow them); the strict upper part is not read and is zeroed in global memory here
     {
-        const int c = t & (NB - 1);
-        const double *src = A + (int64_t)k0 * lda + k0 + c;
-#pragma unroll 16
-        for (int i = t >> 7; i < nbp; i += kLeafThreads / NB) {
-            double v = (i == c) ? 1.0 : 0.0;
-            if (i < nb && c < nb) v = (c <= i) ? __ldg(src + (int64_t)i * lda) : 0.0;
-            if (c < nbp) Ls[i * kLeafLd + c] = v;
+        const int c = 2 * (t & 63), i0 = t >> 6;
+        const bool vec = (lda & 1) == 0 && (reinterpret_cast<uintptr_t>(Ab) & 15) == 0;
+        double v0[32], v1[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+            const int i = i0 + 4 * u;
+            const double *src = Ab + (int64_t)i * lda + c;
+            if (vec && i < nb && c + 1 < nb && c + 1 <= i) {
+                const double2 v = __ldg(reinterpret_cast<const double2 *>(src));
+                v0[u] = v.x;
+                v1[u] = v.y;
+            } else {
+                v0[u] = (i < nb && c < nb && c <= i) ? __ldg(src) : 0.0;
+                v1[u] = (i < nb && c + 1 < nb && c + 1 <= i) ? __ldg(src + 1) : 0.0;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+            const int i = i0 + 4 * u;
+            if (i < nbp && c < nbp)
+                *reinterpret_cast<double2 *>(Ls + i * kLeafLd + c) =
+                    make_double2((i < nb && c < nb) ? v0[u] : (i == c ? 1.0 : 0.0),
+                                 (i < nb && c + 1 < nb) ? v1[u] : (i == c + 1 ? 1.0 : 0.0));
+            if (i < nb && c < nb && c > i) Ab[(int64_t)i * lda + c] = 0.0;
+            if (i < nb && c + 1 < nb && c + 1 > i) Ab[(int64_t)i * lda + c + 1] = 0.0;
         }
     }
     if (t == 0) bad = 0;
+    double R[16][4];
+#pragma unroll
+    for (int ct = 0; ct < 16; ++ct)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) R[ct][e] = (16 * w + g + 8 * (e >> 1) == 8 * ct + 2 * tq + (e & 1)) ? 1.0 : 0.0;
     __syncthreads();
+    double *band = Ls + (16 * w) * kLeafLd;
     for (int p = 0; p < P; ++p) {
         const int j0 = 16 * p;
+        // (a)
         if (w == p) chol_inv16(Ls + j0 * kLeafLd + j0, kLeafLd, Xd + p * 16 * kLeafLdd, &bad);
         __syncthreads();
-        const bool mine = w > p && w < P;
-        double *band = Ls + (16 * w) * kLeafLd;
-        if (mine) {  // L21 = A21 · X_ppᵀ for rows [16w, 16w + 16)
+        // (b)
+        const bool later = w > p && w < P;
+        if (later) {  // L21 = A21 · X_ppᵀ for rows [16w, 16w + 16), into shared memory and global memory
             double af[8], b0[4], b1[4], d0[4] = {0.0, 0.0, 0.0, 0.0}, d1[4] = {0.0, 0.0, 0.0, 0.0};
             const double *xp = Xd + p * 16 * kLeafLdd;
 #pragma unroll
@@ -331,56 +405,42 @@ __global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, 
             dmma16816(d1, af, b1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                double *row = band + (g + 8 * h) * kLeafLd + j0 + 2 * tq;
+                const int i = 16 * w + g + 8 * h, c = j0 + 2 * tq;
+                double *row = band + (g + 8 * h) * kLeafLd + c;
                 *reinterpret_cast<double2 *>(row) = make_double2(d0[2 * h], d0[2 * h + 1]);
                 *reinterpret_cast<double2 *>(row + 8) = make_double2(d1[2 * h], d1[2 * h + 1]);
+                if (i < nb) {
+                    double *dst = Ab + (int64_t)i * lda + c;
+                    if (c < nb) dst[0] = d0[2 * h];
+                    if (c + 1 < nb) dst[1] = d0[2 * h + 1];
+                    if (c + 8 < nb) dst[8] = d1[2 * h];
+                    if (c + 9 < nb) dst[9] = d1[2 * h + 1];
+                }
+            }
+            if (w == p + 1) {  // the next panel's diagonal block, from this warp's own rows: A_dd −= L21·L21ᵀ
+                __syncwarp();
+                leaf_trailing(band, Ls, j0, 2 * w, 2 * w + 1, g, tq);
+            }
+        } else if (w == p) {  // L_pp to global memory
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int r = (lane >> 4) + 2 * e, c = lane & 15, i = j0 + r;
+                if (i < nb && j0 + c < nb) Ab[(int64_t)i * lda + j0 + c] = Ls[i * kLeafLd + j0 + c];
             }
         }
         __syncthreads();
-        if (mine) {  // A22 −= L21 · L21ᵀ over this band's column tiles 2p + 2 .. 2w + 1
-            double af[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) af[e] = -band[(g + 8 * (e & 1)) * kLeafLd + j0 + tq + 4 * (e >> 1)];
-#pragma unroll
-            for (int ct = 2; ct < 16; ++ct) {  // unrolled so the independent tiles' MMAs overlap
-                if (ct < 2 * p + 2 || ct > 2 * w + 1) continue;  // warp-uniform
-                double bf[4], cf[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) bf[e] = Ls[(8 * ct + g) * kLeafLd + j0 + tq + 4 * e];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const double2 v = *reinterpret_cast<const double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq);
-                    cf[2 * h] = v.x;
-                    cf[2 * h + 1] = v.y;
-                }
-                dmma16816(cf, af, bf);
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    *reinterpret_cast<double2 *>(band + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq) =
-                        make_double2(cf[2 * h], cf[2 * h + 1]);
-            }
-        }
-    }
-    __syncthreads();
-    {
-        const int c = t & (NB - 1);
-        double *dst = A + (int64_t)k0 * lda + k0 + c;
-        if (c < nb) {
-#pragma unroll 8
-            for (int i = t >> 7; i < nb; i += kLeafThreads / NB) dst[(int64_t)i * lda] = Ls[i * kLeafLd + c];
-        }
-    }
-    // inverse: R[ct][e] = element (16w + g + 8(e >> 1), 8ct + 2tq + (e & 1)) of this warp's band, starting at I
-    double R[16][4];
-#pragma unroll
-    for (int ct = 0; ct < 16; ++ct)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) R[ct][e] = (16 * w + g + 8 * (e >> 1) == 8 * ct + 2 * tq + (e & 1)) ? 1.0 : 0.0;
-    for (int q = 0; q < P; ++q) {
-        if (w == q) {  // X[q] = X_qq · R[q]: only the column tiles ct < 2q + 2 are non-zero
+        // (c)
+        if (later && w > p + 1) {  // A22 −= L21 · L21ᵀ over this band's column tiles 2p + 2 .. 2w + 1
+            leaf_trailing(band, Ls, j0, 2 * p + 2, 2 * w + 1, g, tq);
+            if (p >= 1) leaf_inverse_update(R, band + 16 * (p - 1), Xp0 + ((p - 1) & 1) * 16 * kLeafLd, p - 1, g, tq);
+        } else if (w == p) {  // the last updates of R[p], then X[p] = X_pp · R[p]
+            if (p >= 2) leaf_inverse_update(R, band + 16 * (p - 2), Xp0 + (p & 1) * 16 * kLeafLd, p - 2, g, tq);
+            if (p >= 1) leaf_inverse_update(R, band + 16 * (p - 1), Xp0 + ((p - 1) & 1) * 16 * kLeafLd, p - 1, g, tq);
+            double *Xp = Xp0 + (p & 1) * 16 * kLeafLd;  // X[p − 2]'s buffer, read above by this warp only
+            __syncwarp();
 #pragma unroll
             for (int ct = 0; ct < 16; ++ct) {
-                if (ct >= 2 * q + 2) continue;
+                if (ct >= 2 * p + 2) continue;
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
                     *reinterpret_cast<double2 *>(Xp + (g + 8 * h) * kLeafLd + 8 * ct + 2 * tq) =
@@ -388,12 +448,12 @@ __global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, 
             }
             __syncwarp();
             double af[8];
-            const double *xq = Xd + q * 16 * kLeafLdd;
+            const double *xq = Xd + p * 16 * kLeafLdd;
 #pragma unroll
             for (int e = 0; e < 8; ++e) af[e] = xq[(g + 8 * (e & 1)) * kLeafLdd + tq + 4 * (e >> 1)];
 #pragma unroll
             for (int ct = 0; ct < 16; ++ct) {
-                if (ct >= 2 * q + 2) continue;
+                if (ct >= 2 * p + 2) continue;
                 double bf[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) bf[e] = Xp[(tq + 4 * e) * kLeafLd + 8 * ct + g];
@@ -406,10 +466,10 @@ __global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, 
             for (int ct = 0; ct < 16; ++ct) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int i = 16 * q + g + 8 * h, c = 8 * ct + 2 * tq;
-                    const double v0 = (ct < 2 * q + 2) ? R[ct][2 * h] : 0.0;
-                    const double v1 = (ct < 2 * q + 2) ? R[ct][2 * h + 1] : 0.0;
-                    if (ct < 2 * q + 2)
+                    const int i = j0 + g + 8 * h, c = 8 * ct + 2 * tq;
+                    const double v0 = (ct < 2 * p + 2) ? R[ct][2 * h] : 0.0;
+                    const double v1 = (ct < 2 * p + 2) ? R[ct][2 * h + 1] : 0.0;
+                    if (ct < 2 * p + 2)
                         *reinterpret_cast<double2 *>(Xp + (g + 8 * h) * kLeafLd + c) = make_double2(v0, v1);
                     if (i < nb) {
                         double *xr = X + (int64_t)(k0 + i) * ldx + k0;
@@ -419,23 +479,8 @@ __global__ void __launch_bounds__(kLeafThreads, 1) diag_block_kernel(double *A, 
                 }
             }
         }
-        __syncthreads();
-        if (w > q && w < P) {  // R[w] −= L[w][q] · X[q]
-            double af[8];
-            const double *band = Ls + (16 * w) * kLeafLd + 16 * q;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) af[e] = -band[(g + 8 * (e & 1)) * kLeafLd + tq + 4 * (e >> 1)];
-#pragma unroll
-            for (int ct = 0; ct < 16; ++ct) {
-                if (ct >= 2 * q + 2) continue;
-                double bf[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) bf[e] = Xp[(tq + 4 * e) * kLeafLd + 8 * ct + g];
-                dmma16816(R[ct], af, bf);
-            }
-        }
-        __syncthreads();
     }
+    __syncthreads();
     if (t == 0 && bad) atomicCAS(status, 0, LAMQ_ERR_NOT_PD);
 }
 
