@@ -18,6 +18,9 @@
 // and inverted by one CTA, the block held in registers (right-looking, one barrier per column).
 #include <algorithm>
 #include <climits>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #include "lamq_common.cuh"
@@ -633,56 +636,181 @@ int dgemm(cudaStream_t s, int transB, int M, int N, int K, double alpha, const d
     return launch_dgemm<TileS>(s, g);
 }
 
-// Recursive Cholesky with inverse of the block [o, o+m) of A (lower part read): L overwrites A's lower part, L⁻¹ goes
-// to X's lower part. [[A11, ·], [A21, A22]]: (L11, X11) = rec(A11); L21 = A21·X11ᵀ; A22 -= L21·L21ᵀ;
-// (L22, X22) = rec(A22); X21 = −X22·(L21·X11). W has room for (m/2 + NB) x m/2 doubles.
-int chol_inv_rec(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx, int o, int m, double *W, int *status) {
+// Recursive Cholesky with inverse of the block [o, o+m) of A (lower part read); L⁻¹ goes to X's lower part, and A
+// (scratch) keeps only the factor's diagonal blocks. [[A11, ·], [A21, A22]]: (L11, X11) = rec(A11); L21 = A21·X11ᵀ
+// (held in X21's place); A22 −= L21·L21ᵀ; (L22, X22) = rec(A22); X21 = −X22·(L21·X11).
+// The recursion's chain runs on a high-priority stream; T = L21·X11 depends only on L21 and X11, so it runs on a
+// low-priority stream of its depth while A22 is updated and factored (whose leaves and small products leave most SMs
+// idle), and is joined before X21. T of depth d goes to its own buffer W_d.
+constexpr int kAuxStreams = 8;
+constexpr int kMaxDepth = 32;
+
+struct FactorStreams {
+    cudaStream_t crit = nullptr;
+    cudaStream_t aux[kAuxStreams] = {};
+};
+
+// One set of internal streams per (device, caller stream): calls made on different streams keep running side by side.
+int factor_streams(cudaStream_t caller, FactorStreams **out) {
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, FactorStreams> cache;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error("factorization: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({dev, caller});
+    if (it == cache.end()) {
+        int least = 0, greatest = 0;
+        FactorStreams fs;
+        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&fs.crit, cudaStreamNonBlocking, greatest);
+        for (int d = 0; e == cudaSuccess && d < kAuxStreams; ++d)
+            e = cudaStreamCreateWithPriority(&fs.aux[d], cudaStreamNonBlocking, least);
+        if (e != cudaSuccess) {
+            set_error("factorization streams: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        it = cache.emplace(std::make_pair(dev, caller), fs).first;
+    }
+    *out = &it->second;
+    return LAMQ_OK;
+}
+
+struct FactorCtx {
+    FactorStreams *fs;
+    cudaEvent_t fork;
+    cudaEvent_t join[kMaxDepth];
+    double *W[kMaxDepth];  // T buffers per depth
+    int *status;
+};
+
+// The largest T (m2 x m1 doubles) at each depth of the recursion over m.
+void t_sizes(int m, int d, std::vector<size_t> &mx) {
+    if (m <= NB) return;
+    const int nblk = (m + NB - 1) / NB;
+    const int m1 = (nblk / 2) * NB, m2 = m - m1;
+    if ((int)mx.size() <= d) mx.resize(d + 1, 0);
+    mx[d] = std::max(mx[d], (size_t)m2 * m1);
+    t_sizes(m1, d + 1, mx);
+    t_sizes(m2, d + 1, mx);
+}
+
+size_t w_elems(int n) {
+    std::vector<size_t> mx;
+    t_sizes(n, 0, mx);
+    size_t total = 0;
+    for (size_t v : mx) total += (v + 31) / 32 * 32;  // 256-byte aligned buffers
+    return total;
+}
+
+int chol_inv_rec(FactorCtx &c, double *A, int64_t lda, double *X, int64_t ldx, int o, int m, int depth) {
+    cudaStream_t s = c.fs->crit;
     if (m <= NB) {
-        diag_block_kernel<<<1, kLeafThreads, kLeafSmem, s>>>(A, lda, o, m, X, ldx, status);
+        diag_block_kernel<<<1, kLeafThreads, kLeafSmem, s>>>(A, lda, o, m, X, ldx, c.status);
         LAMQ_CHECK_LAUNCH("diagonal block");
         return LAMQ_OK;
     }
+    if (depth >= kMaxDepth) {
+        set_error("factorization: recursion deeper than %d", kMaxDepth);
+        return LAMQ_ERR_INVALID;
+    }
     const int nblk = (m + NB - 1) / NB;
     const int m1 = (nblk / 2) * NB, m2 = m - m1;
-    int st = chol_inv_rec(s, A, lda, X, ldx, o, m1, W, status);
+    int st = chol_inv_rec(c, A, lda, X, ldx, o, m1, depth + 1);
     if (st) return st;
-    double *A21 = A + (int64_t)(o + m1) * lda + o;
+    const double *A21 = A + (int64_t)(o + m1) * lda + o;
     double *A22 = A + (int64_t)(o + m1) * lda + o + m1;
-    double *X11 = X + (int64_t)o * ldx + o;
+    const double *X11 = X + (int64_t)o * ldx + o;
     double *X21 = X + (int64_t)(o + m1) * ldx + o;
-    double *X22 = X + (int64_t)(o + m1) * ldx + o + m1;
-    // L21 = A21·X11ᵀ (X11 lower), staged in X21 then copied over A21
+    const double *X22 = X + (int64_t)(o + m1) * ldx + o + m1;
+    double *T = c.W[depth];
+    // L21 = A21·X11ᵀ (X11 lower), held in X21's place until X21 is formed
     st = dgemm(s, 1, m2, m1, m1, 1.0, A21, lda, X11, ldx, 0.0, X21, ldx, 0, 0, 1);
     if (st) return st;
-    copy_block_kernel<<<grid_for((int64_t)m2 * m1), 256, 0, s>>>(X21, ldx, A21, lda, m2, m1);
-    LAMQ_CHECK_LAUNCH("panel copy");
+    // T = L21·X11 beside the rest of this node
+    cudaStream_t aux = c.fs->aux[std::min(depth, kAuxStreams - 1)];
+    cudaError_t e = cudaEventRecord(c.fork, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(aux, c.fork, 0);
+    if (e != cudaSuccess) {
+        set_error("factorization fork: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    st = dgemm(aux, 0, m2, m1, m1, 1.0, X21, ldx, X11, ldx, 0.0, T, m1, 0, 0, 1);
+    if (st) return st;
+    e = cudaEventRecord(c.join[depth], aux);
+    if (e != cudaSuccess) {
+        set_error("factorization join: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
     // A22 -= L21·L21ᵀ (lower part)
-    st = dgemm(s, 1, m2, m2, m1, -1.0, A21, lda, A21, lda, 1.0, A22, lda, 1);
+    st = dgemm(s, 1, m2, m2, m1, -1.0, X21, ldx, X21, ldx, 1.0, A22, lda, 1);
     if (st) return st;
-    st = chol_inv_rec(s, A, lda, X, ldx, o + m1, m2, W, status);
+    st = chol_inv_rec(c, A, lda, X, ldx, o + m1, m2, depth + 1);
     if (st) return st;
-    // X21 = −X22·(L21·X11): X11 and X22 lower triangular
-    st = dgemm(s, 0, m2, m1, m1, 1.0, A21, lda, X11, ldx, 0.0, W, m1, 0, 0, 1);
-    if (st) return st;
-    return dgemm(s, 0, m2, m1, m2, -1.0, X22, ldx, W, m1, 0.0, X21, ldx, 0, 1, 0);
+    e = cudaStreamWaitEvent(s, c.join[depth], 0);
+    if (e != cudaSuccess) {
+        set_error("factorization join: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    // X21 = −X22·T: X22 lower triangular
+    return dgemm(s, 0, m2, m1, m2, -1.0, X22, ldx, T, m1, 0.0, X21, ldx, 0, 1, 0);
 }
 
-int chol_inv(cudaStream_t s, double *A, int64_t lda, double *X, int64_t ldx, int n, double *W, int *status) {
-    const cudaError_t e = smem_limit_once((const void *)diag_block_kernel, (int)kLeafSmem);
+// L⁻¹ of the n x n matrix in A (lower part read; A is scratch) into X's lower part (strict upper zeroed), on
+// `caller`'s stream order (internal streams joined before the return).
+int chol_inv(cudaStream_t caller, double *A, int64_t lda, double *X, int64_t ldx, int n, double *W, int *status) {
+    cudaError_t e = smem_limit_once((const void *)diag_block_kernel, (int)kLeafSmem);
     if (e != cudaSuccess) {
         set_error("cholesky leaf: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
     }
-    int st = chol_inv_rec(s, A, lda, X, ldx, 0, n, W, status);
+    FactorCtx c{};
+    int st = factor_streams(caller, &c.fs);
     if (st) return st;
-    zero_upper_kernel<<<grid_for((int64_t)n * n), 256, 0, s>>>(A, lda, n);
-    LAMQ_CHECK_LAUNCH("zero upper");
-    zero_upper_kernel<<<grid_for((int64_t)n * n), 256, 0, s>>>(X, ldx, n);
-    LAMQ_CHECK_LAUNCH("zero upper");
-    return LAMQ_OK;
+    c.status = status;
+    std::vector<size_t> mx;
+    t_sizes(n, 0, mx);
+    if (mx.size() > (size_t)kMaxDepth) {
+        set_error("factorization: n = %d is too large", n);
+        return LAMQ_ERR_INVALID;
+    }
+    for (size_t d = 0; d < mx.size(); ++d) {
+        c.W[d] = W;
+        W += (mx[d] + 31) / 32 * 32;
+    }
+    const int depths = (int)mx.size();
+    e = cudaEventCreateWithFlags(&c.fork, cudaEventDisableTiming);
+    for (int d = 0; e == cudaSuccess && d < depths; ++d) e = cudaEventCreateWithFlags(&c.join[d], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(c.fork, caller);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(c.fs->crit, c.fork, 0);
+    if (e != cudaSuccess) {
+        set_error("factorization: %s", cudaGetErrorString(e));
+        return LAMQ_ERR_CUDA;
+    }
+    st = chol_inv_rec(c, A, lda, X, ldx, 0, n, 0);
+    if (st == LAMQ_OK) {
+        zero_upper_kernel<<<grid_for((int64_t)n * n), 256, 0, c.fs->crit>>>(X, ldx, n);
+        cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) {
+            set_error("zero upper: %s", cudaGetErrorString(le));
+            st = LAMQ_ERR_CUDA;
+        }
+    }
+    // the caller's stream continues after the internal streams' work (also on an error, so nothing is left behind)
+    e = cudaEventRecord(c.fork, c.fs->crit);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(caller, c.fork, 0);
+    cudaEventDestroy(c.fork);
+    for (int d = 0; d < depths; ++d)
+        if (c.join[d]) cudaEventDestroy(c.join[d]);
+    if (st == LAMQ_OK && e != cudaSuccess) {
+        set_error("factorization: %s", cudaGetErrorString(e));
+        st = LAMQ_ERR_CUDA;
+    }
+    return st;
 }
-
-size_t w_elems(int n) { return (size_t)((n + 1) / 2 + NB) * (size_t)((n + 1) / 2 + NB); }
 
 }  // namespace
 
