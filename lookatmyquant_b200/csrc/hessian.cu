@@ -24,13 +24,12 @@
 // From d = 512 on, xtx_pair_kernel (below) computes 256 × 256 tiles on pairs of CTAs (cta_group::2 MMAs): half the
 // operand bytes per CTA per flop, a 6-stage ring.
 //
-// Flush order: a tile's chunks are added into the accumulator in chunk order, whichever CTAs computed them. Each
-// launch has one ticket per (tile, CTA of the pair) counting the drain threads that have added their part of a chunk;
-// a drain thread adds chunk c only once the ticket reaches 256·c (the units of a tile's chunks are issued in chunk
-// order, so the wait is on earlier units and ends), then counts itself. Every element's fp32 sum therefore runs in the same order on every
-// run: the statistics, and the layer built from them, are bit-reproducible for a given call sequence. Inside a full
-// window a tile's chunks fall to one CTA and the ticket is always ready; a wait longer than kGateTimeoutNs (CTAs not
-// co-resident) adds unordered rather than stall.
+// Fixed summation order: inside a full window CTA b computes the window's tile b over every chunk in turn, so each
+// element of that tile is added into the accumulator by one thread, chunk after chunk. The last, partial window has
+// fewer tiles than CTAs, so a tile's chunks run on several CTAs at once: there each unit stores its tile (times the
+// launch's scale) into a scratch slot of its own, and after the launch a reduction adds every element's slots into the
+// accumulator in chunk order. Every element's fp32 sum therefore runs in the same order on every run: the statistics,
+// and the layer built from them, are bit-reproducible for a given call sequence and GPU.
 //
 // Token weights: bf16 products are exact in fp32, but w·x is not a bf16 number. So the main pass runs with w = 1
 // (A = X, B = X: exact products), and the weighted tokens add Σ_t (w_t − 1)·x_t x_tᵀ in a second pass over only
@@ -71,8 +70,6 @@ constexpr size_t kSmemBytes = 1024 + STAGES * STAGE_BYTES + 256;
 // error) switches the gate off for the rest of the launch.
 constexpr unsigned long long kGateTimeoutNs = 20000000ull;
 constexpr int kGateSlots = 64;
-constexpr int kTicketSlots = 16;
-constexpr int kMaxTickets = 2 * 128 * 128;  // tickets of the largest ordered launch: d <= 32768 (128 x 128 pair tiles)
 
 struct GemmParams {
     float *acc;
@@ -91,7 +88,9 @@ struct GemmParams {
     int64_t units;
     int *status;
     unsigned int *gate;     // units whose loads have all been issued (the wave gate), zeroed before the launch
-    unsigned int *tickets;  // per tile and CTA of the pair: chunks added so far (zeroed), or null: unordered adds
+    float *scratch;         // the last window's units: slot (chunk, tile − last0, CTA of the pair), or null
+    int64_t last0;          // the first tile of the last window (tiles from here on go through the scratch)
+    int last_tiles;
 };
 
 struct Unit {
@@ -159,23 +158,26 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int *p) {
     return v;
 }
 
-// Before a unit's tile is added: wait until every drain thread has added the tile's earlier chunks (see "Flush order"
-// above; each drain thread waits for itself, so no barrier is shared with a thread that may have stopped on an error).
-__device__ __forceinline__ void flush_wait(const unsigned int *ticket, int chunk) {
-    if (ticket == nullptr || chunk == 0) return;
-    const unsigned int target = (unsigned int)chunk * (kEpiWarps * 32);
-    const unsigned long long t0 = globaltimer();
-    while (ld_acquire_u32(ticket) < target) {
-        if (globaltimer() - t0 > kGateTimeoutNs) break;  // not co-resident: add unordered rather than stall
-        __nanosleep(64);
-    }
-}
+constexpr int kSlotFloats = 128 * 256;  // one CTA's part of a unit's tile: 128 rows x 256 columns
 
-// After a drain thread's adds: they are performed before its count reaches the ticket.
-__device__ __forceinline__ void flush_done(unsigned int *ticket) {
-    if (ticket == nullptr) return;
-    __threadfence();
-    atomicAdd(ticket, 1u);
+// A drain thread's part of a unit's tile (row i_loc of the CTA's 128, columns c0.. c0 + 127 of its 256) into the
+// accumulator (atomic adds; one writer per element in a full window) or, in the last window, into the unit's scratch
+// slot (column-major within the slot, so a warp's stores are coalesced).
+__device__ __forceinline__ void flush_tile(const GemmParams &p, const Unit &U, int rank, int i_loc, int c0,
+                                           const float (&tile)[128], int i, int j0) {
+    if (p.scratch != nullptr && U.tile >= p.last0) {
+        float *slot = p.scratch +
+                      (((int64_t)U.chunk * p.last_tiles + (U.tile - p.last0)) * 2 + rank) * kSlotFloats;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) slot[(int64_t)(c0 + c) * 128 + i_loc] = tile[c] * p.scale;
+        return;
+    }
+    if (i >= p.d) return;
+#pragma unroll
+    for (int c = 0; c < 128; ++c) {
+        const int j = j0 + c;
+        if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
+    }
 }
 
 // 32 lanes x 32 bits, 32 consecutive columns: thread t of the warp gets lane (base lane + t).
@@ -360,17 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc ^= 1;
             }
             if (!ok) break;
-            unsigned int *ticket = p.tickets ? p.tickets + 2 * U.tile : nullptr;
-            flush_wait(ticket, U.chunk);
-            const int i = U.ti * BM + 32 * q + lane;
-            if (i < p.d) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int j = U.tj * BN + 128 * half + c;
-                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
-                }
-            }
-            flush_done(ticket);
+            flush_tile(p, U, 0, 32 * q + lane, 128 * half, tile, U.ti * BM + 32 * q + lane, U.tj * BN + 128 * half);
         }
     }
     tc_fence_before();
@@ -555,17 +547,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc ^= 1;
             }
             if (!ok) break;
-            unsigned int *ticket = p.tickets ? p.tickets + 2 * U.tile + rank : nullptr;
-            flush_wait(ticket, U.chunk);
-            const int i = U.ti * 256 + 128 * (int)rank + 32 * q + lane;
-            if (i < p.d) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int j = U.tj * BN + 128 * half + c;
-                    if (j < p.d) atomicAdd(p.acc + (int64_t)j * p.ldc + i, p.scale == 1.0f ? tile[c] : tile[c] * p.scale);
-                }
-            }
-            flush_done(ticket);
+            flush_tile(p, U, (int)rank, 32 * q + lane, 128 * half, tile, U.ti * 256 + 128 * (int)rank + 32 * q + lane,
+                       U.tj * BN + 128 * half);
         }
     }
     tc_fence_before();
@@ -620,6 +603,29 @@ __global__ void finalize_kernel(const float *__restrict__ accH, const float *__r
     }
 }
 
+// The last window's slots added into the accumulator in chunk order: thread e of the grid owns one element of one
+// CTA part of one last-window tile.
+__global__ void last_window_reduce_kernel(GemmParams p) {
+    const int64_t per_tile = 2 * (int64_t)kSlotFloats;
+    const int64_t n = (int64_t)p.last_tiles * per_tile;
+    const int64_t chunk_stride = n;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int tl = (int)(e / per_tile);
+        const int rank = (int)((e / kSlotFloats) & 1);
+        const int loc = (int)(e % kSlotFloats), col = loc >> 7, i_loc = loc & 127;
+        if (!p.pair && rank == 1) continue;
+        int ti, tj;
+        tile_at(p.last0 + tl, p, ti, tj);
+        const int i = p.pair ? ti * 256 + 128 * rank + i_loc : ti * BM + i_loc;
+        const int j = tj * BN + col;
+        if (i >= p.d || j >= p.d) continue;
+        float *dst = p.acc + (int64_t)j * p.ldc + i;
+        float v = *dst;
+        for (int c = 0; c < p.nchunk; ++c) v = __fadd_rn(v, p.scratch[(int64_t)c * chunk_stride + e]);
+        *dst = v;
+    }
+}
+
 // ---- host
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -662,45 +668,6 @@ int make_map(CUtensorMap *m, const void *base, int64_t tokens, int d, int64_t ld
 
 constexpr int kMaxDevices = 64;
 __device__ unsigned int g_gate[kGateSlots];  // one array per device (module globals are per device)
-__device__ unsigned int g_tickets[kTicketSlots][kMaxTickets];
-
-// The flush tickets of one launch on the current device (`n` of them, zeroed on the launch's stream), or null when
-// the launch has more tiles than a slot holds (its adds are then unordered). Slots go round robin like the gate's.
-int ticket_slot(cudaStream_t stream, int64_t n, unsigned int **out) {
-    static std::mutex mu;
-    static unsigned int *base[kMaxDevices] = {};
-    static unsigned int next[kMaxDevices] = {};
-    *out = nullptr;
-    if (n > kMaxTickets) return LAMQ_OK;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-        set_error("lamq_xtx_accumulate: no usable current device");
-        return LAMQ_ERR_CUDA;
-    }
-    unsigned int *slot;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (base[dev] == nullptr) {
-            void *sym = nullptr;
-            e = cudaGetSymbolAddress(&sym, g_tickets);
-            if (e != cudaSuccess || sym == nullptr) {
-                set_error("lamq_xtx_accumulate: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-                return LAMQ_ERR_CUDA;
-            }
-            base[dev] = reinterpret_cast<unsigned int *>(sym);
-        }
-        slot = base[dev] + (size_t)(next[dev]++ % kTicketSlots) * kMaxTickets;
-    }
-    e = cudaMemsetAsync(slot, 0, (size_t)n * sizeof(unsigned int), stream);
-    if (e != cudaSuccess) {
-        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
-        return LAMQ_ERR_CUDA;
-    }
-    *out = slot;
-    return LAMQ_OK;
-}
-
 // A wave-gate counter for one launch on the current device: slots are handed out round robin (launches in flight at
 // once take different slots) and zeroed on the launch's stream.
 int gate_counter(cudaStream_t stream, unsigned int **out) {
@@ -733,6 +700,40 @@ int gate_counter(cudaStream_t stream, unsigned int **out) {
         return LAMQ_ERR_CUDA;
     }
     *out = slot;
+    return LAMQ_OK;
+}
+
+// A stream-ordered memory pool of the library's own per device, keeping what it has grown to (the last-window scratch
+// of a launch is allocated and freed on the launch's stream; with the default pool's release threshold of zero every
+// launch would map its scratch anew).
+int scratch_pool(cudaMemPool_t *out) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("lamq_xtx_accumulate: no usable current device");
+        return LAMQ_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (pools[dev] == nullptr) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        e = cudaMemPoolCreate(&pool, &props);
+        if (e == cudaSuccess) {
+            uint64_t keep = UINT64_MAX;
+            e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        if (e != cudaSuccess) {
+            set_error("lamq_xtx_accumulate: scratch pool: %s", cudaGetErrorString(e));
+            return LAMQ_ERR_CUDA;
+        }
+        pools[dev] = pool;
+    }
+    *out = pools[dev];
     return LAMQ_OK;
 }
 
@@ -807,20 +808,35 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
     p.ntiles = tiles;
     st = gate_counter((cudaStream_t)stream, &p.gate);
     if (st != LAMQ_OK) return st;
-    // one chunk per tile needs no order
-    if (p.nchunk > 1) {
-        st = ticket_slot((cudaStream_t)stream, 2 * tiles, &p.tickets);
+    // the last window (tiles beyond the last full one) goes through scratch slots when its tiles have several chunks
+    const int grid_units = (int)std::min<int64_t>(p.units, p.pair ? num_sms() / 2 : num_sms());
+    p.last0 = tiles / grid_units * grid_units;
+    p.last_tiles = (int)(tiles - p.last0);
+    float *scratch = nullptr;
+    const size_t scratch_bytes = (size_t)p.nchunk * p.last_tiles * 2 * kSlotFloats * sizeof(float);
+    if (p.nchunk > 1 && p.last_tiles > 0) {
+        cudaMemPool_t pool = nullptr;
+        st = scratch_pool(&pool);
         if (st != LAMQ_OK) return st;
+        const cudaError_t ea =
+            cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scratch), scratch_bytes, pool, (cudaStream_t)stream);
+        if (ea != cudaSuccess) {
+            set_error("lamq_xtx_accumulate: %zu bytes of scratch: %s", scratch_bytes, cudaGetErrorString(ea));
+            return LAMQ_ERR_CUDA;
+        }
+        p.scratch = scratch;
     }
+    auto fail = [&](cudaError_t err) {
+        set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(err));
+        if (scratch != nullptr) cudaFreeAsync(scratch, (cudaStream_t)stream);
+        return LAMQ_ERR_CUDA;
+    };
     cudaError_t e;
     if (p.pair) {
         const int64_t clusters = std::min<int64_t>(p.units, num_sms() / 2);
         p.win = (int)clusters;
         e = cudaFuncSetAttribute(xtx_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes);
-        if (e != cudaSuccess) {
-            set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
-            return LAMQ_ERR_CUDA;
-        }
+        if (e != cudaSuccess) return fail(e);
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
         cfg.blockDim = dim3(kThreads, 1, 1);
@@ -834,22 +850,31 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, xtx_pair_kernel, ma, mb, p);
-        if (e != cudaSuccess) {
-            set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
-            return LAMQ_ERR_CUDA;
-        }
+        if (e != cudaSuccess) return fail(e);
         count_launch();
     } else {
         e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        if (e != cudaSuccess) return fail(e);
+        const int64_t grid = p.units < num_sms() ? p.units : num_sms();
+        p.win = (int)grid;
+        xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(e);
+        count_launch();
+    }
+    if (scratch != nullptr) {
+        const int64_t n = (int64_t)p.last_tiles * 2 * kSlotFloats;
+        const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+        last_window_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(e);
+        count_launch();
+        e = cudaFreeAsync(scratch, (cudaStream_t)stream);
         if (e != cudaSuccess) {
             set_error("lamq_xtx_accumulate: %s", cudaGetErrorString(e));
             return LAMQ_ERR_CUDA;
         }
-        const int64_t grid = p.units < num_sms() ? p.units : num_sms();
-        p.win = (int)grid;
-        xtx_kernel<<<(unsigned)grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(ma, mb, p);
     }
-    LAMQ_CHECK_LAUNCH("lamq_xtx_accumulate");
     return LAMQ_OK;
 }
 
