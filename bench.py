@@ -642,6 +642,9 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        # NCCL writes its debug lines (the version banner, when NCCL_DEBUG is set) to stdout by default: send them to
+        # stderr so that stdout carries the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     from lookatmyquant_b200 import _lib
