@@ -35,12 +35,13 @@ SMS = 148
 FP32_LANES = 128
 
 
-# DRAM bytes (read + write) of the statistics kernel per calibration token, summed over the 16 launches of one
-# config-3 layer (H and D of every stage, and of its weighted tokens): ncu dram__bytes_read.sum + dram__bytes_write.sum
-# of every xtx launch of `python -m lookatmyquant_b200.layer --tokens 65536` (31.40 GB / 65,536 tokens). The kernel's
-# traffic per token does not depend on the token count (each launch streams its tokens once through the same tile
-# order), so a launch at any token count moves this many bytes per token.
-XTX_DRAM_BYTES_PER_TOKEN = 479_169
+# DRAM bytes (read + write) of the statistics kernels per calibration token, summed over the 16 launches of one
+# config-3 layer (H and D of every stage, and of its weighted tokens) and the fixed-order reductions of their last
+# windows: ncu dram__bytes_read.sum + dram__bytes_write.sum of every xtx and last_window launch of
+# `python -m lookatmyquant_b200.layer --tokens 65536` (31.58 GB / 65,536 tokens). The kernel's traffic per token does
+# not depend on the token count (each launch streams its tokens once through the same tile order), so a launch at any
+# token count moves this many bytes per token.
+XTX_DRAM_BYTES_PER_TOKEN = 481_864
 XTX_LAUNCHES_PER_LAYER = 16
 
 

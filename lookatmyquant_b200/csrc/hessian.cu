@@ -603,25 +603,25 @@ __global__ void finalize_kernel(const float *__restrict__ accH, const float *__r
     }
 }
 
-// The last window's slots added into the accumulator in chunk order: thread e of the grid owns one element of one
-// CTA part of one last-window tile.
+// The last window's slots added into the accumulator in chunk order: block row y = one CTA part (tile, rank) of the
+// last window, its threads over the part's 128 x 256 elements.
 __global__ void last_window_reduce_kernel(GemmParams p) {
-    const int64_t per_tile = 2 * (int64_t)kSlotFloats;
-    const int64_t n = (int64_t)p.last_tiles * per_tile;
-    const int64_t chunk_stride = n;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-        const int tl = (int)(e / per_tile);
-        const int rank = (int)((e / kSlotFloats) & 1);
-        const int loc = (int)(e % kSlotFloats), col = loc >> 7, i_loc = loc & 127;
-        if (!p.pair && rank == 1) continue;
-        int ti, tj;
-        tile_at(p.last0 + tl, p, ti, tj);
+    const int part = blockIdx.y, tl = part >> 1, rank = part & 1;
+    if (!p.pair && rank == 1) return;
+    __shared__ int tij[2];
+    if (threadIdx.x == 0) tile_at(p.last0 + tl, p, tij[0], tij[1]);
+    __syncthreads();
+    const int ti = tij[0], tj = tij[1];
+    const int64_t chunk_stride = (int64_t)p.last_tiles * 2 * kSlotFloats;
+    const float *src = p.scratch + (int64_t)part * kSlotFloats;
+    for (int loc = blockIdx.x * blockDim.x + threadIdx.x; loc < kSlotFloats; loc += gridDim.x * blockDim.x) {
+        const int col = loc >> 7, i_loc = loc & 127;
         const int i = p.pair ? ti * 256 + 128 * rank + i_loc : ti * BM + i_loc;
         const int j = tj * BN + col;
         if (i >= p.d || j >= p.d) continue;
         float *dst = p.acc + (int64_t)j * p.ldc + i;
         float v = *dst;
-        for (int c = 0; c < p.nchunk; ++c) v = __fadd_rn(v, p.scratch[(int64_t)c * chunk_stride + e]);
+        for (int c = 0; c < p.nchunk; ++c) v = __fadd_rn(v, src[(int64_t)c * chunk_stride + loc]);
         *dst = v;
     }
 }
@@ -863,9 +863,7 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
         count_launch();
     }
     if (scratch != nullptr) {
-        const int64_t n = (int64_t)p.last_tiles * 2 * kSlotFloats;
-        const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
-        last_window_reduce_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(p);
+        last_window_reduce_kernel<<<dim3(kSlotFloats / 256 / 8, 2 * p.last_tiles), 256, 0, (cudaStream_t)stream>>>(p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail(e);
         count_launch();
