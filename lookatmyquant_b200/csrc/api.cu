@@ -36,6 +36,14 @@ cudaError_t smem_limit_once(const void *kernel, int bytes) {
     return e;
 }
 
+cudaError_t smem_limit_max_once(const void *kernel) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    return smem_limit_once(kernel, optin);
+}
+
 }  // namespace lamq
 
 extern "C" int lamq_abi_version(void) { return 4; }

@@ -835,7 +835,7 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
     if (p.pair) {
         const int64_t clusters = std::min<int64_t>(p.units, num_sms() / 2);
         p.win = (int)clusters;
-        e = cudaFuncSetAttribute(xtx_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes);
+        e = smem_limit_once((const void *)xtx_pair_kernel, (int)kPairSmemBytes);
         if (e != cudaSuccess) return fail(e);
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
@@ -853,7 +853,7 @@ extern "C" int lamq_xtx_accumulate_scaled(const uint16_t *A, int64_t lda, const 
         if (e != cudaSuccess) return fail(e);
         count_launch();
     } else {
-        e = cudaFuncSetAttribute(xtx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        e = smem_limit_once((const void *)xtx_kernel, (int)kSmemBytes);
         if (e != cudaSuccess) return fail(e);
         const int64_t grid = p.units < num_sms() ? p.units : num_sms();
         p.win = (int)grid;

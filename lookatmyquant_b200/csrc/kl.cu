@@ -497,8 +497,7 @@ int run_pass(int mode, const uint16_t *H, int64_t ldh, int64_t ntok, int d, cons
     // ranges past the last one hold no partials: mark them empty so the combine skips them
     cudaError_t e = cudaMemsetAsync(*pbv, 0, l.b, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(*ps, 0, l.s, s);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kl_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)kSmemBytes);
+    if (e == cudaSuccess) e = smem_limit_once((const void *)kl_head_kernel, (int)kSmemBytes);
     if (e != cudaSuccess) {
         set_error("lamq_kl_head: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;

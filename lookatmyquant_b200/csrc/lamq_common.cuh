@@ -13,6 +13,9 @@ void set_error(const char *fmt, ...);
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device (thread-safe; defined in api.cu).
 cudaError_t smem_limit_once(const void *kernel, int bytes);
+// The same, to the device's opt-in maximum: for kernels whose shared memory varies from call to call, so that a call
+// on one host thread never lowers the limit under another thread's launch.
+cudaError_t smem_limit_max_once(const void *kernel);
 
 // Counts one kernel launch of this library (lamq_kernel_launches()).
 void count_launch();

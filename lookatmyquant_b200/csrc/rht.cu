@@ -379,7 +379,7 @@ __global__ void transpose_kernel(const double *__restrict__ in, int64_t ldi, dou
 template <int NA, int NB>
 int launch_rht(const RhtParams &p, cudaStream_t stream) {
     const size_t smem = (size_t)p.a * p.b * sizeof(double);
-    cudaError_t e = cudaFuncSetAttribute(rht_rows_kernel<NA, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = smem_limit_max_once((const void *)rht_rows_kernel<NA, NB>);
     if (e != cudaSuccess) {
         set_error("lamq_rht_rows: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;

@@ -277,7 +277,7 @@ extern "C" int lamq_ldlq_rowtrellis(double *T, int64_t ldT, int64_t rows, int n,
     SweepParams p{T, ldT, n, rowlist, nrows, counters, row_bits, k_all, U, ldU, dead, S, tables,
                   width, look, lazy, ts, Z, rstate, 0, 0, 0, states, settled};
     const size_t smem = (size_t)kPairs * ts * sizeof(double) + 16 + kUnionBytes;
-    cudaError_t e = cudaFuncSetAttribute(sweep_run_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = smem_limit_max_once((const void *)sweep_run_kernel);
     if (e != cudaSuccess) {
         set_error("lamq_ldlq_rowtrellis: %s", cudaGetErrorString(e));
         return LAMQ_ERR_CUDA;
