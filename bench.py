@@ -196,7 +196,7 @@ class Config3:
         from lookatmyquant_b200.layer import build_stage, build_stages_sharded, stacked_tables
         tables = stacked_tables(12, 256, self.device)
         out = {}
-        if self.world >= 4:  # every stage's statistics first, the stages' factorizations on separate rank pairs
+        if self.world >= 2:  # every stage's statistics first, the stages' factorizations on rank pairs, beside the sweeps
             stats = []
             for s in self.stages:
                 x, xr = self.acts[s.name]
@@ -263,8 +263,8 @@ class Config3:
                 "trellis": "L=12 reference e-means tables (4096 states) for every width",
                 "qep_alpha": 0.5, "width": 16, "look": 8, "lazy": 128,
                 "parallelism": f"tokens x{self.world} (H/D all-reduce), rows x{self.world}, " +
-                               ("each stage's two factorizations on ranks 0/1, broadcast" if self.world < 4 else
-                                "the stages' factorizations on separate rank pairs, broadcast"),
+                               ("each stage's two factorizations on ranks 0/1, broadcast" if self.world < 2 else
+                                "the stages' factorizations on rank pairs beside the other stages' sweeps, broadcast"),
                 "l2": "inputs (60 GB of activations) far larger than L2"}
 
     def roofline(self, pk):

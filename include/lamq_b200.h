@@ -153,7 +153,10 @@ int lamq_ldlq_coltrellis(double *T, int64_t ldT, int64_t rows, int n, const doub
  * Tensor-core contraction over tokens: acc[j][i] += Σ_t A[t][i]·B[t][j] (bf16 in, fp32 accumulate) for i, j < d.
  * A, B: tokens x d bf16 (raw 16-bit words), row-major with leading dimensions lda, ldb (multiples of 8, 16-byte
  * aligned). acc: d x d fp32 (ldacc), accumulated into (zero it before the first call). The sum is accumulated on chip
- * over chunks of `chunk_tokens` tokens (a multiple of 64) and each chunk's partial is added into acc.
+ * over chunks of `chunk_tokens` tokens (a multiple of 64) and each chunk's partial is added into acc, in chunk order
+ * for every element: the result is bit-reproducible for a given call sequence. Where a tile's chunks run on several
+ * CTAs at once (the last wave of tiles), their partials go through scratch taken stream-ordered from a memory pool the
+ * library keeps per device (at most chunks x 74 tiles x 256 KiB) and are added after the launch.
  * symmetric != 0 (A and B the same tokens, C symmetric): only the blocks of rows j >= columns i are computed; read
  * the result through lamq_hessian_finalize. status: a device int, 0 on entry; a bounded device wait that gives up
  * sets it to LAMQ_ERR_TIMEOUT (then the result is invalid). H = XᵀX is A = B = X; the QEP moment D = X_refᵀX is A = X,

@@ -38,10 +38,12 @@ cudaError_t smem_limit_once(const void *kernel, int bytes) {
 
 cudaError_t smem_limit_max_once(const void *kernel) {
     int dev = 0, optin = 0;
+    cudaFuncAttributes fa{};
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return e;
-    return smem_limit_once(kernel, optin);
+    return smem_limit_once(kernel, optin - (int)fa.sharedSizeBytes);  // dynamic + static <= the opt-in maximum
 }
 
 }  // namespace lamq

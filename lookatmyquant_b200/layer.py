@@ -57,6 +57,7 @@ def row_plan(rows: int, seed: int, group: int = 64, widths=(1, 2, 3, 4), probs=(
 
 
 _SIDE = {}
+_FACTOR = {}
 
 
 def _side_stream(dev) -> torch.cuda.Stream:
@@ -184,25 +185,46 @@ def build_stage_from_statistics(spec: StageSpec, weights: dict, st: Statistics, 
     return res
 
 
+def _factor_stream(dev) -> torch.cuda.Stream:
+    if dev not in _FACTOR:
+        _FACTOR[dev] = torch.cuda.Stream(device=dev)
+    return _FACTOR[dev]
+
+
 def build_stages_sharded(stages, weights: dict, stats: list, bits: dict, layer: int = 0, group=None,
                          dequantize: bool = True, tables=None, n_tok_total: int | None = None) -> dict:
-    """All stages of a layer over a group of 4 or more ranks, from their accumulated statistics: every stage's H and D
+    """All stages of a layer over a group of 2 or more ranks, from their accumulated statistics: every stage's H and D
     reduced first, then every stage's two factorizations queued at once on the rank pairs `factor_owners` assigns
-    (with 8 ranks each stage has its own pair), then stage by stage the factors are broadcast and each rank maps and
-    sweeps its rows. The factorizations of different stages overlap instead of adding up; the results equal
-    build_stage's. Returns {stage: StageResult} (this rank's rows)."""
+    (with 8 ranks each stage has its own pair) on a factorization stream, then stage by stage — the smallest first —
+    the factors are broadcast as soon as that stage's are done and each rank maps and sweeps its rows. The
+    factorizations of different stages overlap one another, and a rank that owns the large stage's factorization
+    sweeps the smaller stages' rows while it runs; the results equal build_stage's. Returns {stage: StageResult}
+    (this rank's rows)."""
     world, rank = group.size(), group.rank()
     HD = [_reduce_finalize(st, group, n_tok_total) for st in stats]
     owners = factor_owners([s.d for s in stages], world)
     dev = HD[0][0].device
     rots = [Rotation(s.d, _in_seed(s, layer), dev) for s in stages]
-    bufs = [_own_factors(rots[i], HD[i][0], rank, *owners[i]) for i in range(len(stages))]
+    order = sorted(range(len(stages)), key=lambda i: (stages[i].d, i))  # the same on every rank
+    main, fs = torch.cuda.current_stream(dev), _factor_stream(dev)
+    fs.wait_stream(main)
+    bufs, done = [None] * len(stages), [None] * len(stages)
+    with torch.cuda.stream(fs):
+        for i in order:
+            bufs[i] = _own_factors(rots[i], HD[i][0], rank, *owners[i])
+            done[i] = torch.cuda.Event()
+            done[i].record(fs)
+    for b in bufs:
+        for t in b:
+            t.record_stream(main)
     out = {}
-    for i, s in enumerate(stages):
+    for i in order:
+        s = stages[i]
+        main.wait_event(done[i])
         factors = _share_factors(rots[i], HD[i][0], bufs[i], *owners[i], group)
         out[s.name] = build_stage_from_statistics(s, weights, None, bits, layer, group, dequantize, tables,
-                                                  n_tok_total, HD=HD[i], factors=factors)
-    return out
+                                                  n_tok_total, HD=HD[i], factors=factors, rot=rots[i])
+    return {s.name: out[s.name] for s in stages}
 
 
 def _own_factors(rot, H, rank: int, env_rank: int, qep_rank: int):

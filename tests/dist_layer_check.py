@@ -1,6 +1,6 @@
 """Worker of test_gpu_multi.py, launched by torch.distributed.run with one process per GPU: a small two-stage layer
-built with its tokens and rows sharded over the ranks (H and D all-reduced; a stage's two factorizations on two ranks
-and broadcast — with 4 or more ranks, each stage on its own rank pair after every stage's statistics), every rank's
+built with its tokens and rows sharded over the ranks (H and D all-reduced after every stage's statistics, the stages'
+factorizations on rank pairs — each stage on its own pair with 4 or more ranks — and broadcast), every rank's
 states gathered to rank 0 and compared with the same layer built on one GPU."""
 
 import datetime
@@ -28,7 +28,7 @@ def main():
     lo, hi = token_shard(tokens, rank, world)
     stages, weights, acts, w, bits = config3(tokens, device=dev, lo=lo, hi=hi, stages=spec)
     group = torch.distributed.group.WORLD
-    if world >= 4:  # every stage's statistics first, the stages' factorizations on separate rank pairs
+    if world >= 2:  # every stage's statistics first, the stages' factorizations on rank pairs
         from lookatmyquant_b200.hessian import Statistics
         from lookatmyquant_b200.layer import build_stages_sharded
         stats = []
