@@ -643,9 +643,11 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        # NCCL writes its debug lines (the version banner, when NCCL_DEBUG is set) to stdout by default: send them to
-        # stderr so that stdout carries the one JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        # NCCL prints its version banner (when NCCL_DEBUG is set) to file descriptor 1: point that descriptor at
+        # stderr and keep Python's stdout on the original one, so stdout carries only the JSON line
+        sys.stdout.flush()
+        sys.stdout = os.fdopen(os.dup(1), "w", buffering=1)
+        os.dup2(2, 1)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     from lookatmyquant_b200 import _lib
