@@ -205,7 +205,7 @@ def gather_records(res: dict, group, order: list) -> dict:
 
 
 def run(layers=range(2), options=("tr2", "tr3", "tr4"), n_layers: int = 32, windows: int = 8, T: int = 2048,
-        calib: int = 16, chunk: int = 4, kl_batch: int = 2, seed: int = 0, device="cuda", log=print,
+        calib: int = 16, chunk: int = 4, kl_batch: int = 8, seed: int = 0, device="cuda", log=print,
         rank: int = 0, world: int = 1, group=None, dense_piece: bool = False) -> dict:
     """The measure sweep over the linear pieces of `layers`: returns the records and the timing. With world > 1 this
     rank probes only its share of the pieces (assign_pieces) on its own model replica, and with a process group the
