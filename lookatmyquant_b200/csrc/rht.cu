@@ -8,6 +8,9 @@
 //
 // One CTA transforms one row in shared memory, in place: phase 1 (one warp per row p of V) forms Z = V·Beᵀ, phase 2
 // (one warp per column q) forms Y = Ae·Z; each lane keeps the sign bits of the factor rows it produces in registers.
+// A factor that is a natural-order Sylvester matrix (found on the device from its sign bits: every A here, and B when
+// n is a power of four) is applied by fast Walsh–Hadamard butterflies instead, log2(order) additions per element
+// (64 → 6 at n = 9728; 128 → 7 at 2560; both factors at 4096).
 // Fewer than kSplitRows rows (a decode step's few input vectors) are spread over many CTAs instead (the split form).
 // The general form computed is y = scale · post ⊙ ((Ae ⊗ Be)·(pre ⊙ v)), so R (Ae = A, Be = B, pre = s) and Rᵀ
 // (Ae = Aᵀ, Be = Bᵀ, post = s) are both one pass.
@@ -67,19 +70,67 @@ __device__ __forceinline__ void signed_sums(const double *__restrict__ src, int 
     }
 }
 
+// Whether a factor's sign bits are the natural-order Sylvester matrix H[i][j] = (-1)^popcount(i & j) of a power-of-
+// two order (every A of codes.hadamard_factors, and B when n is a power of four): checked by the whole CTA.
+__device__ __forceinline__ bool sylvester_factor(const uint32_t *__restrict__ bits, int order, int words) {
+    bool ok = (order & (order - 1)) == 0;
+    for (int e = threadIdx.x; ok && e < order * words; e += blockDim.x) {
+        const int r = e / words, w = e - r * words;
+        uint32_t want = 0u;
+        for (int k = 0; k < 32 && 32 * w + k < order; ++k) want |= (uint32_t)(__popc(r & (32 * w + k)) & 1) << k;
+        ok = bits[e] == want;
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
+// x ← H·x for a Sylvester H of order `order` (a power of two), x spread over the warp as x[c] = element lane + 32c:
+// the fast Walsh–Hadamard butterflies, log2(order) additions per element instead of `order` signed ones.
+template <int NC>
+__device__ __forceinline__ void fwht_warp(double (&x)[NC], int order, int lane) {
+    for (int h = 1; h < order && h < 32; h <<= 1) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const double v = __shfl_xor_sync(0xffffffffu, x[c], h);
+            x[c] = (lane & h) ? __dsub_rn(v, x[c]) : __dadd_rn(x[c], v);
+        }
+    }
+#pragma unroll
+    for (int hc = 1; hc < NC; hc <<= 1) {
+        if (32 * hc >= order) break;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            if (c & hc) continue;
+            const double u = x[c], v = x[c + hc];
+            x[c] = __dadd_rn(u, v);
+            x[c + hc] = __dsub_rn(u, v);
+        }
+    }
+}
+
 // NA = ceil(a/32), NB = ceil(b/32): output chunks per lane (and sign words per factor row) of the two phases.
 template <int NA, int NB>
 __global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
     extern __shared__ __align__(16) double sv[];
     const int n = p.a * p.b;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = kRhtThreads / 32;
+    const bool fast_a = sylvester_factor(p.abits, p.a, p.wa), fast_b = sylvester_factor(p.bbits, p.b, p.wb);
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const double *src = p.in + row * p.ldi;
 #pragma unroll 8
         for (int e = threadIdx.x; e < n; e += kRhtThreads) sv[e] = p.pre ? src[e] * p.pre[e] : src[e];
         __syncthreads();
         // phase 1: Z[pr][q] = Σ_q' Be[q][q'] · V[pr][q'], a warp per row pr of V, lanes over q
-        {
+        if (fast_b) {
+            for (int pr = warp; pr < p.a; pr += nwarps) {
+                double x[NB];
+#pragma unroll
+                for (int c = 0; c < NB; ++c) x[c] = (lane + 32 * c < p.b) ? sv[pr * p.b + lane + 32 * c] : 0.0;
+                fwht_warp<NB>(x, p.b, lane);
+#pragma unroll
+                for (int c = 0; c < NB; ++c)
+                    if (lane + 32 * c < p.b) sv[pr * p.b + lane + 32 * c] = x[c];
+            }
+        } else {
             uint32_t bits[NB][8];
 #pragma unroll
             for (int c = 0; c < NB; ++c) {
@@ -103,7 +154,17 @@ __global__ void __launch_bounds__(kRhtThreads) rht_rows_kernel(RhtParams p) {
         }
         __syncthreads();
         // phase 2: Y[pr][q] = Σ_p' Ae[pr][p'] · Z[p'][q], a warp per column q, lanes over pr
-        {
+        if (fast_a) {
+            for (int q = warp; q < p.b; q += nwarps) {
+                double x[NA];
+#pragma unroll
+                for (int c = 0; c < NA; ++c) x[c] = (lane + 32 * c < p.a) ? sv[(lane + 32 * c) * p.b + q] : 0.0;
+                fwht_warp<NA>(x, p.a, lane);
+#pragma unroll
+                for (int c = 0; c < NA; ++c)
+                    if (lane + 32 * c < p.a) sv[(lane + 32 * c) * p.b + q] = x[c];
+            }
+        } else {
             uint32_t bits[NA][8];
 #pragma unroll
             for (int c = 0; c < NA; ++c) {
@@ -156,7 +217,19 @@ __global__ void __launch_bounds__(kSplitWarps * 32) rht_split_rows_kernel(RhtPar
     const double *src = p.in + row * p.ldi + off;
     for (int e = threadIdx.x; e < nr * p.b; e += blockDim.x) sz[e] = p.pre ? src[e] * p.pre[off + e] : src[e];
     __syncthreads();
+    const bool fast = sylvester_factor(p.bbits, p.b, p.wb);  // the whole CTA, before any warp leaves
     if (warp >= nr) return;
+    double *dst = p.out + row * p.ldo + off + (int64_t)warp * p.b;
+    if (fast) {  // the same butterflies as rht_rows_kernel, so the two forms stay equal
+        double x[NB];
+#pragma unroll
+        for (int c = 0; c < NB; ++c) x[c] = (lane + 32 * c < p.b) ? sz[warp * p.b + lane + 32 * c] : 0.0;
+        fwht_warp<NB>(x, p.b, lane);
+#pragma unroll
+        for (int c = 0; c < NB; ++c)
+            if (lane + 32 * c < p.b) dst[lane + 32 * c] = x[c];
+        return;
+    }
     uint32_t bits[NB][8];
 #pragma unroll
     for (int c = 0; c < NB; ++c) {
@@ -168,7 +241,6 @@ __global__ void __launch_bounds__(kSplitWarps * 32) rht_split_rows_kernel(RhtPar
 #pragma unroll
     for (int c = 0; c < NB; ++c) acc[c] = 0.0;
     signed_sums<NB>(sz + warp * p.b, 1, p.b, bits, acc);
-    double *dst = p.out + row * p.ldo + off + (int64_t)warp * p.b;
 #pragma unroll
     for (int c = 0; c < NB; ++c) {
         const int q = lane + 32 * c;
@@ -191,7 +263,25 @@ __global__ void __launch_bounds__(kSplitWarps * 32) rht_split_cols_kernel(RhtPar
         sz[w * ld + pr] = Z[(int64_t)pr * p.b + q0 + w];
     }
     __syncthreads();
+    const bool fast = sylvester_factor(p.abits, p.a, p.wa);  // the whole CTA, before any warp leaves
     if (warp >= nq) return;
+    const int q = q0 + warp;
+    if (fast) {  // the same butterflies as rht_rows_kernel, so the two forms stay equal
+        double x[NA];
+#pragma unroll
+        for (int c = 0; c < NA; ++c) x[c] = (lane + 32 * c < p.a) ? sz[warp * ld + lane + 32 * c] : 0.0;
+        fwht_warp<NA>(x, p.a, lane);
+#pragma unroll
+        for (int c = 0; c < NA; ++c) {
+            const int pr = lane + 32 * c;
+            if (pr < p.a) {
+                const int64_t e = (int64_t)pr * p.b + q;
+                const double y = x[c] * p.scale;
+                Z[e] = p.post ? y * p.post[e] : y;
+            }
+        }
+        return;
+    }
     uint32_t bits[NA][8];
 #pragma unroll
     for (int c = 0; c < NA; ++c) {
@@ -203,7 +293,6 @@ __global__ void __launch_bounds__(kSplitWarps * 32) rht_split_cols_kernel(RhtPar
 #pragma unroll
     for (int c = 0; c < NA; ++c) acc[c] = 0.0;
     signed_sums<NA>(sz + warp * ld, 1, p.a, bits, acc);
-    const int q = q0 + warp;
 #pragma unroll
     for (int c = 0; c < NA; ++c) {
         const int pr = lane + 32 * c;

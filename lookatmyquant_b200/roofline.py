@@ -11,6 +11,7 @@ DGEMM reaches 35.8). Inputs are seeded synthetic data with the configurations' s
 from __future__ import annotations
 
 import argparse
+import math
 import json
 import statistics
 from pathlib import Path
@@ -180,20 +181,28 @@ def run(device="cuda", log=print, only=None) -> list:
         del A, B
 
     if want("a3"):  # the randomized Hadamard transform of a stage's targets (9728 x 2560) and of H (9728²)
+        def adds_per_row(n_):
+            """Additions per row: a Sylvester factor (a power-of-two order, applied by butterflies) costs log2 of its
+            order per element, a Paley one its order (dense signed sums)."""
+            A, B = codes.hadamard_factors(n_)
+            na, nb = int(A.shape[0]), int(B.shape[0])
+            sylvester = lambda m: m & (m - 1) == 0 and m > 1
+            ca = math.log2(na) if sylvester(na) else na
+            cb = math.log2(nb) if sylvester(nb) and torch.equal(B, codes._sylvester(int(math.log2(nb)))) else nb
+            return na, nb, float(na * nb) * (ca + cb)
         for n_, rows_ in ((2560, 9728), (9728, 2560)):
             rot = Rotation(n_, 301, dev)
             X = 0.02 * torch.randn(rows_, n_, dtype=torch.float64, device=dev, generator=g)
             ms = timer(lambda: rot.rows(X))
-            na, nb = (int(f.shape[0]) for f in codes.hadamard_factors(n_))
-            adds = float(rows_) * na * nb * (na + nb)  # A·V and V·Bᵀ with ±1 factors: one add per product
-            add(_record("a3", "rht_rows_kernel (A·V·Bᵀ with ±1 Kronecker factors, fp64)",
-                        f"{rows_} x {n_} ({na} x {nb})", ms, adds, "T fp64 add/s", FP64_ADD_T,
+            na, nb, per_row = adds_per_row(n_)
+            add(_record("a3", "rht_rows_kernel (A·V·Bᵀ: butterflies for the Sylvester factor, signed sums for Paley)",
+                        f"{rows_} x {n_} ({na} x {nb})", ms, rows_ * per_row, "T fp64 add/s", FP64_ADD_T,
                         f"{16.0 * X.numel() / (ms * 1e-3) / 1e9:.0f} GB/s of HBM", "fp64 pipe"))
             del X
         rot9 = Rotation(n, 301, dev)
         ms = timer(lambda: rot9.conj(H))
-        na, nb = (int(f.shape[0]) for f in codes.hadamard_factors(n))
-        add(_record("a3", "rht_rows_kernel x2 + transpose (R·H·Rᵀ)", f"{n}²", ms, 2.0 * n * na * nb * (na + nb),
+        na, nb, per_row = adds_per_row(n)
+        add(_record("a3", "rht_rows_kernel x2 + transpose (R·H·Rᵀ)", f"{n}²", ms, 2.0 * n * per_row,
                     "T fp64 add/s", FP64_ADD_T, "two row passes", "fp64 pipe"))
 
     if want("a6"):  # the fused row-trellis sweep (4096 x 2560 at k = 2, and the down_proj shape)
