@@ -216,3 +216,41 @@ def test_synthetic_codebooks_match_reference(golden):
     for bits in (1, 2, 3, 4):
         L, v = synthetic_codebook(bits)
         assert L == bits + 4 and torch.equal(v, torch.as_tensor(g[f"codebook_{bits}"]))
+
+
+@pytest.mark.parametrize("n", [2560, 4096, 9728, 960, 1536])
+def test_hadamard_factor_a_is_the_sylvester_pattern_the_device_checks(n):
+    """Every A of hadamard_factors (and B when it is a power-of-two Sylvester matrix) has exactly the sign bits the
+    rotation kernel's device check accepts for its butterfly path: bit k of word w of row r set iff
+    popcount(r & (32w + k)) is odd."""
+    from lookatmyquant_b200.codes import hadamard_factors
+    from lookatmyquant_b200.rotation import _sign_bits
+    A, B = hadamard_factors(n)
+
+    def pattern(order):
+        words = (order + 31) // 32
+        out = np.zeros((order, words), dtype=np.uint32)
+        for r in range(order):
+            for c in range(order):
+                if bin(r & c).count("1") & 1:
+                    out[r, c // 32] |= np.uint32(1) << np.uint32(c % 32)
+        return out
+
+    a = A.shape[0]
+    assert a & (a - 1) == 0
+    assert np.array_equal(_sign_bits(A).numpy().view(np.uint32), pattern(a))
+    b = B.shape[0]
+    if b & (b - 1) == 0 and b > 2:
+        assert np.array_equal(_sign_bits(B).numpy().view(np.uint32), pattern(b))
+
+
+def test_host_build_takes_the_stage_with_the_least_work_last():
+    """build_layer_from_host copies and builds the stages in order of the work after their statistics (the largest
+    factorization and sweep first), the same order on every rank."""
+    from lookatmyquant_b200.layer import qwen3_4b_stages, tail_order
+    stages = qwen3_4b_stages()
+    one = [s.name for s in tail_order(stages, 1)]
+    assert one[0] == "down_in" and one[-1] == "o_in"
+    assert [s.name for s in tail_order(list(reversed(stages)), 1)] == one
+    eight = [s.name for s in tail_order(stages, 8)]
+    assert eight[0] == "down_in" and set(eight) == set(one)
