@@ -1,4 +1,4 @@
-// Dense fp64 linear algebra on the fp64 tensor cores (mma.sync m8n8k4 f64): the GEMM, blocked Cholesky and
+// Dense fp64 linear algebra on the fp64 tensor cores (mma.sync m16n8k16 f64): the GEMM, blocked Cholesky and
 // triangular inverse behind the environment factor U and the QEP target.
 //
 // Reference: opgraph/frame.py:515-522 (`Environment`: dead inputs, damping, U = chol(cholesky_inverse(chol(H)))ᵀ)
@@ -14,8 +14,9 @@
 // SMs — K in steps of 16 through a 4-stage cp.async ring (rows padded so fragment loads are bank-conflict free); a
 // triangular operand clips each tile's K range.
 // Cholesky and inverse together, recursively: (L11, X11) = rec(A11), L21 = A21·X11ᵀ, A22 −= L21·L21ᵀ,
-// (L22, X22) = rec(A22), X21 = −X22·(L21·X11) — 0.58n³ multiply-adds in large GEMMs; 128 x 128 leaves are factored
-// and inverted by one CTA, the block held in registers (right-looking, one barrier per column).
+// (L22, X22) = rec(A22), X21 = −X22·(L21·X11) — most of the 2n³/3 multiply-adds in large GEMMs, T = L21·X11 on a
+// low-priority stream beside the A22 recursion; 128 x 128 leaves are factored and inverted by one CTA in shared
+// memory, 16-column panels on fp64 MMAs (diag_block_kernel).
 #include <algorithm>
 #include <climits>
 #include <map>
@@ -75,12 +76,6 @@ __device__ __forceinline__ void dmma16816(double (&c)[4], const double (&a)[8], 
         : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
         : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]), "d"(b[0]), "d"(b[1]),
           "d"(b[2]), "d"(b[3]));
-}
-
-__device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b) {
-    asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
-                 : "+d"(c0), "+d"(c1)
-                 : "d"(a), "d"(b));
 }
 
 __device__ __forceinline__ void cp8(double *dst, const double *src, bool ok) {
@@ -651,9 +646,14 @@ struct FactorStreams {
 };
 
 // One set of internal streams per (device, caller stream): calls made on different streams keep running side by side.
+// At most kMaxStreamSets sets per device are created; callers beyond them share the existing sets in turn (still
+// correct — every call forks from its caller's stream and joins back — only no longer side by side).
+constexpr int kMaxStreamSets = 8;
+
 int factor_streams(cudaStream_t caller, FactorStreams **out) {
     static std::mutex mu;
-    static std::map<std::pair<int, cudaStream_t>, FactorStreams> cache;
+    static std::map<std::pair<int, cudaStream_t>, FactorStreams *> assigned;
+    static std::map<int, std::vector<FactorStreams *>> sets;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -661,21 +661,29 @@ int factor_streams(cudaStream_t caller, FactorStreams **out) {
         return LAMQ_ERR_CUDA;
     }
     std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find({dev, caller});
-    if (it == cache.end()) {
-        int least = 0, greatest = 0;
-        FactorStreams fs;
-        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
-        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&fs.crit, cudaStreamNonBlocking, greatest);
-        for (int d = 0; e == cudaSuccess && d < kAuxStreams; ++d)
-            e = cudaStreamCreateWithPriority(&fs.aux[d], cudaStreamNonBlocking, least);
-        if (e != cudaSuccess) {
-            set_error("factorization streams: %s", cudaGetErrorString(e));
-            return LAMQ_ERR_CUDA;
+    auto it = assigned.find({dev, caller});
+    if (it == assigned.end()) {
+        std::vector<FactorStreams *> &mine = sets[dev];
+        FactorStreams *fs = nullptr;
+        if ((int)mine.size() < kMaxStreamSets) {
+            int least = 0, greatest = 0;
+            FactorStreams made;
+            e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+            if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&made.crit, cudaStreamNonBlocking, greatest);
+            for (int d = 0; e == cudaSuccess && d < kAuxStreams; ++d)
+                e = cudaStreamCreateWithPriority(&made.aux[d], cudaStreamNonBlocking, least);
+            if (e != cudaSuccess) {
+                set_error("factorization streams: %s", cudaGetErrorString(e));
+                return LAMQ_ERR_CUDA;
+            }
+            fs = new FactorStreams(made);  // kept for the life of the process, like the streams themselves
+            mine.push_back(fs);
+        } else {
+            fs = mine[assigned.size() % mine.size()];
         }
-        it = cache.emplace(std::make_pair(dev, caller), fs).first;
+        it = assigned.emplace(std::make_pair(dev, caller), fs).first;
     }
-    *out = &it->second;
+    *out = it->second;
     return LAMQ_OK;
 }
 
